@@ -1,0 +1,476 @@
+"""Packed-SDM decode benchmark (BASELINE metric: decode tokens/s at batch 64 per GPU).
+
+Workload (configuration 3, the synthetic random-route serving screen): 7
+independent SDM pools (layers), N=256 slots, D=128, H=1, top-16 reads / top-4
+writes, uniform seeded routes, batch 64 requests per GPU, prefix 2,048 tokens
+(sparse prefill handoff), then decode with a four-step growth quantum
+(``max(16, 64*4*4) = 1,024`` rows).  One *step* = one decode token for every
+request through all 7 pools = one fused ``cow_decode_step`` launch.
+
+Reported numbers (one JSON line from rank 0):
+
+* ``value``: device throughput, inputs resident in HBM.  Each timed step is a
+  CUDA graph of the one fused launch; L2 is flushed (a 256 MiB write) before
+  every timed step and the step is timed alone with CUDA events on the
+  launching stream, so the pool state starts cold in HBM.
+* ``e2e``: the same metric through the public Python API with host buffers:
+  every step copies its routes from pinned host memory, runs
+  ``packed_sdm_cow_step_layers`` (with the per-step capacity proof) and reads
+  the readouts back to the host.
+* ``roofline``: algorithmic bytes per launch / mean launch time vs the
+  measured HBM copy bandwidth.
+* ``dense_control``: the dense-table control kernel timed the same way, and
+  the packed path's latency overhead against it.
+* ``cpu_baseline``: the CPU restatement of the reference's deterministic
+  path, timed on a bounded sample on this host.
+
+Multi-GPU: one process per GPU (torchrun); each rank owns its own 64
+requests (weak scaling, no collective on the data path); time is the max over
+ranks.  ``--impl reference`` times the reference's CPU algorithm instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "packed-SDM decode tokens/s at batch 64, 1/2/4/8 B200; % of HBM roofline"
+LAYERS, SLOTS, WIDTH, HEADS, READS, WRITES = 7, 256, 128, 1, 16, 4
+BATCH, PREFIX, QUANTUM_STEPS = 64, 2048, 4
+L2_FLUSH_BYTES = 256 << 20
+
+
+def algorithmic_bytes(banks: int, first_touches: int, *, idx_bytes=8, val_bytes=4, act_bytes=4) -> int:
+    """Per-launch algorithmic bytes of the fused step (all pools).
+
+    Per (bank, layer, token): D*s_v*(2W+R) row traffic + D*(s_in+s_out)
+    value/readout + (W+R)*(s_idx + 4 + s_w) routes/map/weights + 3*s_g + 8
+    gates and template; plus 8 bytes per first touch (stack read + map store).
+    """
+    per = (WIDTH * val_bytes * (2 * WRITES + READS) + WIDTH * 2 * act_bytes
+           + (WRITES + READS) * (idx_bytes + 4 + act_bytes) + 3 * act_bytes + 8)
+    return banks * per + 8 * first_touches
+
+
+def dense_algorithmic_bytes(banks: int) -> int:
+    per = (WIDTH * 4 * (2 * WRITES + READS) + WIDTH * 2 * 4 + (WRITES + READS) * (8 + 4) + 3 * 4)
+    return banks * per
+
+
+# --------------------------------------------------------------------------
+# synthetic inputs
+# --------------------------------------------------------------------------
+
+
+def uniform_routes(gen: torch.Generator, shape, k: int, device) -> torch.Tensor:
+    keys = torch.rand(*shape, SLOTS, generator=gen, device=device)
+    return keys.argsort(dim=-1)[..., :k].contiguous()
+
+
+def step_inputs(gen, banks, steps, device):
+    """Decode inputs for ``steps`` tokens and all layers: dict of [S, L, banks, ...]."""
+    shape = (steps, LAYERS, banks)
+    return dict(
+        write_indices=uniform_routes(gen, shape, WRITES, device),
+        write_weights=torch.softmax(torch.randn(*shape, WRITES, generator=gen, device=device), -1),
+        values=torch.randn(*shape, WIDTH, generator=gen, device=device),
+        input_gate=torch.rand(*shape, generator=gen, device=device),
+        forget_log_gate=-torch.rand(*shape, generator=gen, device=device),
+        read_indices=uniform_routes(gen, shape, READS, device),
+        read_weights=torch.softmax(torch.randn(*shape, READS, generator=gen, device=device), -1),
+    )
+
+
+def prefill_pools(gen, banks, device):
+    from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState
+
+    q = max(16, banks * WRITES * QUANTUM_STEPS)
+    states = []
+    for _ in range(LAYERS):
+        m0 = 0.02 * torch.randn(HEADS, SLOTS, WIDTH, generator=gen, device=device)
+        shape = (banks, PREFIX)
+        st, _ = PackedSDMCopyOnWriteState.from_prefix_routes(
+            m0,
+            uniform_routes(gen, shape, WRITES, device),
+            torch.softmax(torch.randn(*shape, WRITES, generator=gen, device=device), -1),
+            torch.randn(*shape, WIDTH, generator=gen, device=device),
+            torch.rand(*shape, generator=gen, device=device),
+            -torch.rand(*shape, generator=gen, device=device),
+            uniform_routes(gen, shape, READS, device),
+            torch.softmax(torch.randn(*shape, READS, generator=gen, device=device), -1),
+            template_indices=torch.zeros(banks, dtype=torch.int64, device=device),
+            growth_quantum_rows=q,
+        )
+        states.append(st)
+    return states
+
+
+# --------------------------------------------------------------------------
+# clocks
+# --------------------------------------------------------------------------
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+
+
+def _c_step(inputs, s, l, outputs):
+    from copy_on_write_sdm_b200 import _lib
+
+    def p(name):
+        return inputs[name][s, l].data_ptr()
+
+    return _lib.CowStep(p("write_indices"), p("write_weights"), p("values"), p("input_gate"),
+                        p("input_gate"), p("forget_log_gate"), p("read_indices"), p("read_weights"),
+                        outputs[l].data_ptr(), None)
+
+
+def run_gpu(args, rank, world, device):
+    from copy_on_write_sdm_b200 import _lib, allocator, packed_sdm_cow_step_layers, dense_sdm_sparse_step_layers
+
+    lib = _lib.load()
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    banks = BATCH * HEADS
+    K, Wm = args.steps, args.warmup
+    t_setup = time.time()
+    states = prefill_pools(gen, banks, device)
+    inputs = step_inputs(gen, banks, K + Wm, device)
+    torch.cuda.synchronize(device)
+    setup_s = time.time() - t_setup
+
+    # Warm-up steps through the public API (capacity proof + growth as in serving).
+    for s in range(Wm):
+        for st in states:
+            st.prepare_step_capacity(banks * WRITES)
+        packed_sdm_cow_step_layers(states, [{k: v[s, l] for k, v in inputs.items()} for l in range(LAYERS)])
+    # Prove capacity for every timed step up front (pessimistic: W first touches per bank-step).
+    for st in states:
+        st.prepare_step_capacity(banks * WRITES * K)
+    free_before = sum(int(st.free_count) for st in states)
+    for st in states:
+        st.validate_invariants()
+
+    outputs = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
+    scratch = allocator.decode_scratch(device, banks * LAYERS, LAYERS)
+    pools = (_lib.CowPool * LAYERS)(*[st._pool() for st in states])
+    stream = torch.cuda.Stream(device)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in range(Wm, Wm + K):
+            steps = (_lib.CowStep * LAYERS)(*[_c_step(inputs, s, l, outputs) for l in range(LAYERS)])
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                _lib.check(lib.cow_decode_step(pools, steps, LAYERS, WRITES, READS, _lib.I64, _lib.F32,
+                                               scratch.data_ptr(), scratch.numel(), stream.cuda_stream),
+                           "cow_decode_step")
+            graphs.append(g)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    with ClockSampler(device.index) as clocks:
+        barrier()
+        torch.cuda.synchronize(device)
+        with torch.cuda.stream(stream):
+            for s in range(K):
+                flush.fill_(float(s))
+                ev[s][0].record(stream)
+                graphs[s].replay()
+                ev[s][1].record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+    free_after = sum(int(st.free_count) for st in states)
+    first_touches = free_before - free_after
+    for st in states:
+        st.validate_invariants()
+
+    # Warm-L2 trace: the same K steps replayed back to back (state L2-resident).
+    warm = None
+    if rank == 0:
+        # replaying re-applies the same routes on the evolved state; allocation
+        # cannot grow (every slot of every bank is already private)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            flush.fill_(0.0)
+            e0.record(stream)
+            for g in graphs:
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(device)
+        warm = e0.elapsed_time(e1)
+
+    # Dense-table control, same routes, same timing discipline.
+    dense_ms = None
+    if rank == 0:
+        mems = [st.materialize_dense() for st in states]
+        dptrs = (ctypes.c_void_p * LAYERS)(*[m.data_ptr() for m in mems])
+        dbanks = (ctypes.c_int64 * LAYERS)(*([banks] * LAYERS))
+        dgraphs = []
+        with torch.cuda.stream(stream):
+            for s in range(Wm, Wm + K):
+                steps = (_lib.CowStep * LAYERS)(*[_c_step(inputs, s, l, outputs) for l in range(LAYERS)])
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    _lib.check(lib.cow_dense_step(dptrs, dbanks, steps, LAYERS, SLOTS, WIDTH, _lib.F32, WRITES,
+                                                  READS, _lib.I64, _lib.F32, stream.cuda_stream), "cow_dense_step")
+                dgraphs.append(g)
+        dev_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        with torch.cuda.stream(stream):
+            for s in range(K):
+                flush.fill_(float(s))
+                dev_ev[s][0].record(stream)
+                dgraphs[s].replay()
+                dev_ev[s][1].record(stream)
+        torch.cuda.synchronize(device)
+        dense_ms = sum(a.elapsed_time(b) for a, b in dev_ev)
+        del mems, dgraphs
+
+    # End to end through the public API with host buffers.
+    host = {k: v[Wm:Wm + K].cpu().pin_memory() for k, v in inputs.items()}
+    dev_in = {k: torch.empty_like(v[0]) for k, v in inputs.items()}
+    host_out = torch.empty(LAYERS, banks, WIDTH, pin_memory=True)
+    dev_out = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
+    h2d = sum(v[0].numel() * v.element_size() for v in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for s in range(K):
+            for k in dev_in:
+                dev_in[k].copy_(host[k][s], non_blocking=True)
+            for st in states:
+                st.prepare_step_capacity(banks * WRITES)
+            packed_sdm_cow_step_layers(states, [{k: v[l] for k, v in dev_in.items()} for l in range(LAYERS)],
+                                       outputs=dev_out)
+            for l in range(LAYERS):
+                host_out[l].copy_(dev_out[l], non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    state_bytes = {}
+    for st in states:
+        for k, v in st.storage_bytes().items():
+            state_bytes[k] = state_bytes.get(k, 0) + v
+    used = [st.used_bytes() for st in states]
+    return dict(total_ms=total_ms, step_ms=step_ms, e2e_ms=e2e_ms, warm_ms=warm, dense_ms=dense_ms,
+                first_touches=first_touches, h2d=h2d, d2h=d2h, clocks=clocks.summary(), setup_s=setup_s,
+                state_bytes=state_bytes, live_value_bytes=sum(u["live_value_bytes"] for u in used),
+                allocated_rows=sum(u["allocated_rows"] for u in used),
+                capacity_rows=sum(st.capacity_rows for st in states))
+
+
+# --------------------------------------------------------------------------
+# CPU arms (the reference's algorithm, restated in oracle/)
+# --------------------------------------------------------------------------
+
+
+def cpu_decode_rate(seconds: float, threads: int, *, warmup: int = 0, steps: int | None = None) -> dict:
+    """Tokens/s of the oracle's packed decode step on this host (bounded sample).
+
+    The sample starts from a post-prefix pool (every slot private, as uniform
+    2,048-token prefixes leave it), 7 layers x 64 requests, and runs decode
+    steps -- ``steps`` of them after ``warmup``, or as many as fit in
+    ``seconds`` -- with the layers spread over ``threads`` host threads.
+    """
+    from oracle import cow_oracle as O
+
+    rng = np.random.default_rng(7)
+    banks = BATCH * HEADS
+    pools = []
+    for _ in range(LAYERS):
+        m0 = (0.02 * rng.standard_normal((HEADS, SLOTS, WIDTH))).astype(np.float32)
+        dense = rng.standard_normal((banks, SLOTS, WIDTH)).astype(np.float32)
+        pools.append(O.from_dense_overlay(m0, dense, np.ones((banks, SLOTS), bool),
+                                          template_indices=np.zeros(banks, np.int64),
+                                          capacity_rows=banks * SLOTS))
+    batches = [[O.synthetic_step_inputs(rng, banks, SLOTS, WIDTH, WRITES, READS) for _ in range(LAYERS)]
+               for _ in range(8)]
+    done = 0
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        def one(i):
+            list(ex.map(lambda lx: O.packed_step(lx[0], **lx[1]), zip(pools, batches[i % len(batches)])))
+
+        for i in range(warmup):
+            one(i)
+        t0 = time.perf_counter()
+        while (steps is not None and done < steps) or (steps is None and time.perf_counter() - t0 < seconds):
+            one(done)
+            done += 1
+        dt = time.perf_counter() - t0
+    return {"value": BATCH * done / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{done} decode steps x {LAYERS} layers x {banks} banks (N={SLOTS}, D={WIDTH}, "
+                      f"top-{READS}/top-{WRITES}) from a post-prefix pool, {dt:.2f} s, numpy oracle"}
+
+
+def config_block(world: int) -> dict:
+    return {"workload": "config 3 synthetic random-route serving screen: 7 independent SDM pools, N=256, D=128, "
+                        "H=1, top-16 read/top-4 write, uniform seeded routes, prefix 2048 (sparse prefill), "
+                        "growth quantum 4 steps",
+            "batch_per_gpu": BATCH, "global_batch": BATCH * world, "prefix": PREFIX,
+            "layers": LAYERS, "slots": SLOTS, "width": WIDTH, "heads": HEADS, "reads": READS, "writes": WRITES,
+            "growth_quantum_rows": max(16, BATCH * HEADS * WRITES * QUANTUM_STEPS),
+            "parallelism": f"requests sharded, {BATCH} per GPU x {world} GPU(s), no collective",
+            "l2": "flushed (256 MiB write) before every timed step; each step timed alone"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        threads = min(LAYERS, os.cpu_count() or 1)
+        cpu = cpu_decode_rate(0.0, threads, warmup=args.warmup, steps=args.steps)
+        v = cpu["value"]
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * BATCH / v,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config_block(args.gpus), "cpu_baseline": cpu,
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    if world > 1:
+        torch.distributed.init_process_group("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    res = run_gpu(args, rank, world, device)
+
+    total_ms, e2e_ms = res["total_ms"], res["e2e_ms"]
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return 0
+
+    K = args.steps
+    tokens = BATCH * world * K
+    value = tokens / (total_ms / 1e3)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(peaks_path):
+        peak, peak_src = json.load(open(peaks_path))["hbm_gbs"], "measured"
+    else:
+        peak, peak_src = 6650.0, "fallback"
+    per_launch = algorithmic_bytes(BATCH * HEADS * LAYERS, res["first_touches"] // max(K, 1))
+    mean_launch_s = (res["total_ms"] / K) / 1e3
+    achieved = per_launch / mean_launch_s / 1e9
+    dense_bytes = dense_algorithmic_bytes(BATCH * HEADS * LAYERS)
+    cpu = cpu_decode_rate(args.cpu_seconds, min(LAYERS, os.cpu_count() or 1))
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": per_launch, "mean_launch_us": mean_launch_s * 1e6,
+                     "kernel": "cow_decode_kernel<f32,1,8>"},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
+                "d2h_bytes_per_step": res["d2h"], "path": "packed_sdm_cow_step_layers, pinned host buffers"},
+        "gpu_launches": K,
+        "clocks": res["clocks"],
+        "cpu_baseline": cpu,
+        "dense_control": None if res["dense_ms"] is None else {
+            "value": BATCH * K / (res["dense_ms"] / 1e3), "unit": "tokens/s",
+            "ms_per_step": res["dense_ms"] / K,
+            "packed_latency_overhead_pct": 100.0 * (res["total_ms"] / res["dense_ms"] - 1.0),
+            "achieved_gbs": dense_bytes / (res["dense_ms"] / K / 1e3) / 1e9},
+        "warm_l2_trace": None if res["warm_ms"] is None else {
+            "value": BATCH * K / (res["warm_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": res["warm_ms"] / K,
+            "note": "same K graph steps back to back, pool state L2-resident"},
+        "retained_state": {"allocated_rows": res["allocated_rows"], "capacity_rows": res["capacity_rows"],
+                           "live_value_bytes": res["live_value_bytes"], **res["state_bytes"]},
+        "first_touches_in_timed_steps": res["first_touches"],
+        "setup_s": res["setup_s"],
+    }
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

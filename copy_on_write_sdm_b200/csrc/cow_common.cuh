@@ -1,0 +1,387 @@
+// cow_common.cuh -- shared device helpers of the packed copy-on-write SDM kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cow_sdm.h"
+
+#define COW_ABI_VERSION 1
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kBanksPerCta = 4;  // warps per decode CTA
+constexpr int kSpinLimit = 1 << 21;
+
+// --------------------------------------------------------------------------
+// element access
+// --------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 f4_axpy(float a, float4 x, float4 y) {
+  return make_float4(fmaf(a, x.x, y.x), fmaf(a, x.y, y.y), fmaf(a, x.z, y.z), fmaf(a, x.w, y.w));
+}
+__device__ __forceinline__ float4 f4_scale(float a, float4 x) {
+  return make_float4(a * x.x, a * x.y, a * x.z, a * x.w);
+}
+
+template <int DT>
+struct Elem;
+
+template <>
+struct Elem<COW_F32> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t e) {
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + e);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t e, float4 v) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + e) = v;
+  }
+  static __device__ __forceinline__ float4 round4(float4 v) { return v; }
+  static __device__ __forceinline__ float ld1(const void* p, int64_t i) {
+    return static_cast<const float*>(p)[i];
+  }
+};
+
+template <>
+struct Elem<COW_BF16> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t e) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + e);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t e, float4 v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<unsigned*>(&a);
+    u.y = *reinterpret_cast<unsigned*>(&b);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + e) = u;
+  }
+  static __device__ __forceinline__ float r1(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  static __device__ __forceinline__ float4 round4(float4 v) {
+    return make_float4(r1(v.x), r1(v.y), r1(v.z), r1(v.w));
+  }
+  static __device__ __forceinline__ float ld1(const void* p, int64_t i) {
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  }
+};
+
+template <>
+struct Elem<COW_F16> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t e) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p) + e);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t e, float4 v) {
+    __half2 a = __floats2half2_rn(v.x, v.y);
+    __half2 b = __floats2half2_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<unsigned*>(&a);
+    u.y = *reinterpret_cast<unsigned*>(&b);
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p) + e) = u;
+  }
+  static __device__ __forceinline__ float r1(float x) { return __half2float(__float2half_rn(x)); }
+  static __device__ __forceinline__ float4 round4(float4 v) {
+    return make_float4(r1(v.x), r1(v.y), r1(v.z), r1(v.w));
+  }
+  static __device__ __forceinline__ float ld1(const void* p, int64_t i) {
+    return __half2float(static_cast<const __half*>(p)[i]);
+  }
+};
+
+// Activation tensors (weights, values, gates, readouts) carry a runtime dtype:
+// the branch is warp-uniform and off the row-traffic critical path.
+__device__ __forceinline__ float ld1_rt(const void* p, int64_t i, int dt) {
+  if (dt == COW_F32) return Elem<COW_F32>::ld1(p, i);
+  if (dt == COW_BF16) return Elem<COW_BF16>::ld1(p, i);
+  return Elem<COW_F16>::ld1(p, i);
+}
+__device__ __forceinline__ float4 ld4_rt(const void* p, int64_t e, int dt) {
+  if (dt == COW_F32) return Elem<COW_F32>::ld4(p, e);
+  if (dt == COW_BF16) return Elem<COW_BF16>::ld4(p, e);
+  return Elem<COW_F16>::ld4(p, e);
+}
+__device__ __forceinline__ void st4_rt(void* p, int64_t e, float4 v, int dt) {
+  if (dt == COW_F32) Elem<COW_F32>::st4(p, e, v);
+  else if (dt == COW_BF16) Elem<COW_BF16>::st4(p, e, v);
+  else Elem<COW_F16>::st4(p, e, v);
+}
+__device__ __forceinline__ int64_t ld_index(const void* p, int64_t i, int idx64) {
+  return idx64 ? static_cast<const long long*>(p)[i] : static_cast<const int*>(p)[i];
+}
+__device__ __forceinline__ float4 ld4_m0(const float* m0, int64_t e) {
+  return __ldg(reinterpret_cast<const float4*>(m0 + e));
+}
+
+// --------------------------------------------------------------------------
+// per-warp route metadata (shared memory, broadcast reads)
+// --------------------------------------------------------------------------
+
+struct WarpMeta {
+  int widx[COW_MAX_WRITES];
+  int wphys[COW_MAX_WRITES];  // map entry before the step (-1 = shared M0)
+  float ww[COW_MAX_WRITES];
+  int ridx[COW_MAX_READS];
+  int rsrc[COW_MAX_READS];  // >= 0 slab row, -1 M0 row, <= -2 forwarded write slot -(w+2)
+  float rw[COW_MAX_READS];
+  float fwt[COW_MAX_WRITES];  // summed read weight of reads that hit write slot w this step
+};
+
+struct DecodeLayer {
+  const float* m0;
+  const int64_t* templates;
+  void* slab;
+  int32_t* map;
+  const int32_t* free_rows;
+  int32_t* free_count;
+  int32_t* status;
+  cow_step step;
+  int64_t banks, slots, capacity, template_count;
+  int32_t tile_begin, tiles;
+};
+
+struct DecodeLaunch {
+  DecodeLayer layer[COW_MAX_LAYERS];
+  uint32_t* header;    // [ticket, done, epoch, pad]
+  uint64_t* flags;     // one per tile (global ticket)
+  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, _pad;
+};
+
+constexpr uint32_t kFlagAggregate = 1u;
+constexpr uint32_t kFlagInclusive = 2u;
+
+__device__ __forceinline__ uint64_t pack_flag(uint32_t epoch, uint32_t st, uint32_t v) {
+  return (static_cast<uint64_t>(epoch) << 32) | (static_cast<uint64_t>(st) << 30) | (v & 0x3fffffffu);
+}
+
+__device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t* p) {
+  return *reinterpret_cast<const volatile uint64_t*>(p);
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Load the W write routes and R read routes of one bank into the warp's
+// metadata.  Returns a warp-uniform "bad" flag (an index out of range or a
+// repeated write address); `first_mask` has bit w set for first touches.
+//
+// `row` indexes the [rows, W] / [rows, R] route tensors; `map_row` selects the
+// bank's map row (they differ in the prefill, whose routes are [banks*T, ...]).
+template <bool kDense>
+__device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, const int32_t* map,
+                                            int64_t row, int64_t map_row, int64_t N, int W, int R,
+                                            int idx64, int adt, int lane, unsigned& first_mask,
+                                            int& error_bits) {
+  bool bad = false;
+  int wi = 0, wp = -1;
+  float wwv = 0.f;
+  if (lane < W) {
+    const int64_t raw = ld_index(st.write_indices, row * W + lane, idx64);
+    const bool ok = raw >= 0 && raw < N;
+    wi = ok ? static_cast<int>(raw) : 0;
+    if (!kDense) wp = map[map_row * N + wi];
+    wwv = ld1_rt(st.write_weights, row * W + lane, adt);
+    bad = !ok;
+  }
+  // Out-of-range lanes get a unique sentinel so they never count as repeats.
+  const bool valid_w = lane < W && !bad;
+  const unsigned same = __match_any_sync(kFull, valid_w ? wi : -1 - lane);
+  const bool dup = valid_w && __popc(same) > 1;
+  first_mask = __ballot_sync(kFull, lane < W && wp < 0 && !kDense);
+  sm.widx[lane] = wi;
+  sm.wphys[lane] = wp;
+  sm.ww[lane] = wwv;
+  __syncwarp();
+  for (int r = lane; r < R; r += 32) {
+    const int64_t raw = ld_index(st.read_indices, row * R + r, idx64);
+    const bool ok = raw >= 0 && raw < N;
+    const int ri = ok ? static_cast<int>(raw) : 0;
+    const int p = kDense ? -1 : map[map_row * N + ri];
+    int fw = -1;
+    for (int w = 0; w < W; ++w) fw = (sm.widx[w] == ri) ? w : fw;
+    sm.ridx[r] = ri;
+    sm.rsrc[r] = fw >= 0 ? -(fw + 2) : (p >= 0 ? p : -1);
+    sm.rw[r] = ld1_rt(st.read_weights, row * R + r, adt);
+    bad |= !ok;
+  }
+  __syncwarp();
+  // Reads of a slot written this step see the updated row (read-after-write,
+  // allocator.py:1503-1517); its value is still in registers, so those reads
+  // are folded into one weight per write slot instead of reloading the row.
+  if (lane < W) {
+    float f = 0.f;
+    for (int r = 0; r < R; ++r) f += (sm.rsrc[r] == -(lane + 2)) ? sm.rw[r] : 0.f;
+    sm.fwt[lane] = f;
+  }
+  const bool any_dup = __any_sync(kFull, dup);
+  const bool any_oob = __any_sync(kFull, bad);
+  error_bits = (any_dup ? COW_ST_DUPLICATE_WRITE : 0) | (any_oob ? COW_ST_INDEX_RANGE : 0);
+  __syncwarp();
+  return any_dup || any_oob;
+}
+
+// Gated-delta update of the W write rows (allocator.py:1489-1501): the rows
+// arrive in `upd` (already loaded), leave as the updated values rounded to
+// the slab dtype.
+template <int SDT, int CH, int WMAX>
+__device__ __forceinline__ void gated_delta(float4 (&upd)[WMAX][CH], const WarpMeta& sm, int W,
+                                            float alpha, float in_g, float er_g,
+                                            const float4 (&val)[CH], int lane, int D) {
+  float4 ret[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) ret[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int w = 0; w < WMAX; ++w) {
+    if (w < W) {
+      const float wt = sm.ww[w];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        upd[w][c] = f4_scale(alpha, upd[w][c]);
+        ret[c] = f4_axpy(wt, upd[w][c], ret[c]);
+      }
+    }
+  }
+  float4 delta[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    delta[c] = make_float4(in_g * val[c].x - er_g * ret[c].x, in_g * val[c].y - er_g * ret[c].y,
+                           in_g * val[c].z - er_g * ret[c].z, in_g * val[c].w - er_g * ret[c].w);
+  }
+#pragma unroll
+  for (int w = 0; w < WMAX; ++w) {
+    if (w < W) {
+      const float wt = sm.ww[w];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) upd[w][c] = Elem<SDT>::round4(f4_axpy(wt, delta[c], upd[w][c]));
+    }
+  }
+  (void)lane;
+  (void)D;
+}
+
+// Weighted sparse read after the write (allocator.py:1507-1517).  Rows of
+// slots written this step come from registers; the rest from the slab
+// (private) or M0 (shared).  Loads are issued in groups for memory-level
+// parallelism.
+template <int SDT, int CH, int WMAX>
+__device__ __forceinline__ void sparse_read(float4 (&acc)[CH], const float4 (&upd)[WMAX][CH],
+                                            const WarpMeta& sm, int W, int R, const void* rows,
+                                            int64_t row_base, const float* m0, int64_t m0_base,
+                                            int lane, int D) {
+  constexpr int G = CH >= 4 ? 2 : (CH == 2 ? 4 : 8);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r0 = 0; r0 < R; r0 += G) {
+    float4 v[G][CH];
+    float wt[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int r = r0 + j;
+      const int src = r < R ? sm.rsrc[r] : -2;
+      wt[j] = src >= -1 ? sm.rw[r] : 0.f;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int col = (c * 32 + lane) * 4;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col < D) {
+          if (src >= 0) x = Elem<SDT>::ld4(rows, (row_base + src) * D + col);
+          else if (src == -1) x = ld4_m0(m0, (m0_base + sm.ridx[r]) * D + col);
+        }
+        v[j][c] = x;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c) acc[c] = f4_axpy(wt[j], v[j][c], acc[c]);
+    }
+  }
+#pragma unroll
+  for (int w = 0; w < WMAX; ++w) {
+    if (w < W) {
+      const float f = sm.fwt[w];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) acc[c] = f4_axpy(f, upd[w][c], acc[c]);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// host helpers
+// --------------------------------------------------------------------------
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+// Last CUDA error seen by an entry point on this host thread (cow_last_error).
+namespace cowrt {
+extern thread_local int last_cuda_error;
+}  // namespace cowrt
+
+namespace {
+
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return COW_OK;
+  cowrt::last_cuda_error = static_cast<int>(e);
+  return COW_ERR_CUDA;
+}
+
+inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return static_cast<int>(b);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool valid_dtype(int dt) { return dt == COW_F32 || dt == COW_BF16 || dt == COW_F16; }
+inline int elem_size(int dt) { return dt == COW_F32 ? 4 : 2; }
+inline bool row_aligned(const void* p, int dt) {
+  // 4-element row vectors need 16-byte (f32) or 8-byte (16-bit) alignment.
+  return (reinterpret_cast<uintptr_t>(p) & static_cast<uintptr_t>(4 * elem_size(dt) - 1)) == 0;
+}
+
+inline int width_chunks(int64_t width) {
+  if (width <= 128) return 1;
+  if (width <= 256) return 2;
+  return 4;
+}
+
+inline bool check_step_shape(int64_t width, int writes, int reads) {
+  return width > 0 && width % 4 == 0 && width <= COW_MAX_WIDTH && writes >= 1 && writes <= COW_MAX_WRITES &&
+         reads >= 1 && reads <= COW_MAX_READS;
+}
+
+inline bool check_step_ptrs(const cow_step& s, int adt) {
+  return s.write_indices && s.write_weights && s.values && s.input_gate && s.erase_gate && s.forget_log_gate &&
+         s.read_indices && s.read_weights && s.output && row_aligned(s.values, adt) && row_aligned(s.output, adt);
+}
+
+#define COW_SELECT_KERNEL(KERNEL, SDT, CH, WMAX_SMALL, FN)                 \
+  do {                                                                      \
+    if (SDT == COW_F32) {                                                   \
+      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_F32, 1, 8> : KERNEL<COW_F32, 1, 32>;   \
+      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_F32, 2, 8> : KERNEL<COW_F32, 2, 32>; \
+      else FN = WMAX_SMALL ? KERNEL<COW_F32, 4, 8> : KERNEL<COW_F32, 4, 32>;           \
+    } else if (SDT == COW_BF16) {                                           \
+      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_BF16, 1, 8> : KERNEL<COW_BF16, 1, 32>; \
+      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_BF16, 2, 8> : KERNEL<COW_BF16, 2, 32>; \
+      else FN = WMAX_SMALL ? KERNEL<COW_BF16, 4, 8> : KERNEL<COW_BF16, 4, 32>;         \
+    } else {                                                                \
+      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_F16, 1, 8> : KERNEL<COW_F16, 1, 32>;   \
+      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_F16, 2, 8> : KERNEL<COW_F16, 2, 32>; \
+      else FN = WMAX_SMALL ? KERNEL<COW_F16, 4, 8> : KERNEL<COW_F16, 4, 32>;           \
+    }                                                                       \
+  } while (0)
+
+}  // namespace

@@ -1,0 +1,133 @@
+// cow_dense.cu -- dense-table control kernel (the latency reference).
+
+#include "cow_common.cuh"
+
+namespace {
+
+// --------------------------------------------------------------------------
+// dense-table control
+// --------------------------------------------------------------------------
+
+struct DenseLayer {
+  void* memory;
+  cow_step step;
+  int64_t banks, bank_begin;
+};
+struct DenseLaunch {
+  DenseLayer layer[COW_MAX_LAYERS];
+  int64_t slots, total_banks;
+  int32_t layers, width, writes, reads, idx64, act_dt;
+};
+
+template <int SDT, int CH, int WMAX>
+__global__ void __launch_bounds__(kBanksPerCta * 32)
+    cow_dense_kernel(const __grid_constant__ DenseLaunch P) {
+  __shared__ WarpMeta s_meta[kBanksPerCta];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * kBanksPerCta + warp;
+  if (g >= P.total_banks) return;
+  int l = 0;
+  while (l + 1 < P.layers && g >= P.layer[l].bank_begin + P.layer[l].banks) ++l;
+  const DenseLayer& L = P.layer[l];
+  const int64_t bank = g - L.bank_begin;
+  const int D = P.width, W = P.writes, R = P.reads;
+  const int64_t N = P.slots;
+  WarpMeta& sm = s_meta[warp];
+  unsigned first_mask;
+  int route_bits;
+  const bool bad = load_routes<true>(sm, L.step, nullptr, bank, bank, N, W, R, P.idx64, P.act_dt,
+                                     lane, first_mask, route_bits);
+  float4 acc[CH];
+  if (!bad) {
+    const float alpha = expf(ld1_rt(L.step.forget_log_gate, bank, P.act_dt));
+    const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
+    const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+    float4 upd[WMAX][CH];
+    const int64_t base = bank * N;
+#pragma unroll
+    for (int w = 0; w < WMAX; ++w) {
+      if (w < W) {
+        const int slot = sm.widx[w];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int col = (c * 32 + lane) * 4;
+          upd[w][c] = col < D ? Elem<SDT>::ld4(L.memory, (base + slot) * D + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+    float4 val[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
+#pragma unroll
+    for (int w = 0; w < WMAX; ++w) {
+      if (w < W) {
+        const int slot = sm.widx[w];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int col = (c * 32 + lane) * 4;
+          if (col < D) Elem<SDT>::st4(L.memory, (base + slot) * D + col, upd[w][c]);
+        }
+      }
+    }
+    // In the dense table every read slot is "private": rsrc = slot.
+    for (int r = lane; r < R; r += 32) {
+      if (sm.rsrc[r] == -1) sm.rsrc[r] = sm.ridx[r];
+    }
+    __syncwarp();
+    sparse_read<SDT, CH, WMAX>(acc, upd, sm, W, R, L.memory, base, nullptr, 0, lane, D);
+  } else {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], P.act_dt);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int cow_dense_step(void* const* memories, const int64_t* banks, const cow_step* steps, int32_t layers, int64_t slots,
+                   int64_t width, int32_t mem_dtype, int32_t writes, int32_t reads, int32_t index_dtype,
+                   int32_t act_dtype, void* stream) {
+  if (!memories || !banks || !steps || layers < 1 || layers > COW_MAX_LAYERS || slots < 1) return COW_ERR_INVALID;
+  if (!valid_dtype(act_dtype) || !valid_dtype(mem_dtype) || (index_dtype != COW_I32 && index_dtype != COW_I64))
+    return COW_ERR_INVALID;
+  if (!check_step_shape(width, writes, reads)) return COW_ERR_UNSUPPORTED;
+  DenseLaunch P{};
+  int64_t total = 0;
+  for (int l = 0; l < layers; ++l) {
+    if (!memories[l] || banks[l] < 0 || !row_aligned(memories[l], mem_dtype) || !check_step_ptrs(steps[l], act_dtype))
+      return COW_ERR_INVALID;
+    P.layer[l].memory = memories[l];
+    P.layer[l].step = steps[l];
+    P.layer[l].banks = banks[l];
+    P.layer[l].bank_begin = total;
+    total += banks[l];
+  }
+  if (total == 0) return COW_OK;
+  P.slots = slots;
+  P.total_banks = total;
+  P.layers = layers;
+  P.width = static_cast<int32_t>(width);
+  P.writes = writes;
+  P.reads = reads;
+  P.idx64 = index_dtype == COW_I64;
+  P.act_dt = act_dtype;
+  void (*fn)(DenseLaunch) = nullptr;
+  const int ch = width_chunks(width);
+  COW_SELECT_KERNEL(cow_dense_kernel, mem_dtype, ch, writes <= 8, fn);
+  const int64_t blocks = (total + kBanksPerCta - 1) / kBanksPerCta;
+  fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+/*
+ * cow_sdm.h -- C ABI of the B200 (sm_100a) packed copy-on-write SDM library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, cast to cudaStream_t inside), allocates nothing and
+ * returns an int status (COW_OK on success).  Device-side failures that can
+ * only be detected while a kernel runs (slab exhaustion, bad route indices,
+ * duplicate writes, a bounded wait that gave up) are OR-ed into the state's
+ * 32-bit device status word (COW_ST_* bits); the host reads it at its next
+ * synchronisation point.  Nothing traps or asserts on the device.
+ *
+ * Storage conventions are those of the reference's PackedSDMCopyOnWriteState
+ * (copy_on_write_sdm/allocator.py:477-505):
+ *   m0         [templates, slots, width]  shared initial memory (float32 here)
+ *   templates  [banks] int64              template of each bank (bank = request*H + head)
+ *   slab       [capacity, width]          pooled private rows (f32 / bf16 / f16)
+ *   map        [banks, slots] int32       logical -> physical row, -1 = shared M0
+ *   free_rows  [capacity] int32           free stack, top at free_rows[free_count-1]
+ *   free_count int32 (device scalar)
+ *   status     int32 (device scalar)      the reference's overflow_flag, widened to bits
+ */
+#ifndef COW_SDM_H
+#define COW_SDM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---------------------------------------------------- */
+#define COW_OK 0
+#define COW_ERR_INVALID 1      /* bad argument (null pointer, size, alignment) */
+#define COW_ERR_UNSUPPORTED 2  /* shape outside the compiled kernels (see each entry) */
+#define COW_ERR_CUDA 3         /* a CUDA runtime call or launch failed */
+#define COW_ERR_DEVICE 4       /* a *_checked call found status bits set */
+
+/* ---- element / index type codes -------------------------------------- */
+#define COW_F32 0
+#define COW_BF16 1
+#define COW_F16 2
+#define COW_I32 0
+#define COW_I64 1
+
+/* ---- device status bits ---------------------------------------------- */
+#define COW_ST_SLAB_EXHAUSTED 0x1     /* a first touch found the free stack empty */
+#define COW_ST_INDEX_RANGE 0x2        /* a route index lies outside [0, slots) */
+#define COW_ST_DUPLICATE_WRITE 0x4    /* one step wrote one logical slot twice */
+#define COW_ST_WAIT_TIMEOUT 0x8       /* a bounded inter-CTA wait gave up */
+#define COW_ST_TEMPLATE_RANGE 0x10    /* a template index lies outside m0 */
+#define COW_ST_BAD_BANK_LIST 0x20     /* released/retained bank index invalid or duplicated */
+#define COW_ST_DISCARD_LIVE 0x40      /* retain_banks would drop a bank that still owns rows */
+#define COW_ST_MULTI_OWNER 0x100      /* validate: a physical row has several owners */
+#define COW_ST_FREE_DUPLICATE 0x200   /* validate: free stack holds a row twice */
+#define COW_ST_NOT_COVERED 0x400      /* validate: a row is neither live nor free */
+#define COW_ST_ROW_RANGE 0x800        /* validate: a map / stack entry lies outside capacity */
+
+#define COW_MAX_LAYERS 8
+#define COW_MAX_WRITES 32
+#define COW_MAX_READS 256
+#define COW_MAX_WIDTH 512
+
+/* One packed pool: the reference's PackedSDMCopyOnWriteState fields. */
+typedef struct cow_pool {
+  const float* m0;
+  const int64_t* templates;
+  void* slab;
+  int32_t* map;
+  int32_t* free_rows;
+  int32_t* free_count;
+  int32_t* status;
+  int64_t banks, slots, width, capacity, template_count;
+  int32_t slab_dtype; /* COW_F32 / COW_BF16 / COW_F16 */
+  int32_t _pad;
+} cow_pool;
+
+/* One decode step's routes for one pool (the arguments of
+ * packed_sdm_cow_step, allocator.py:1382-1396).  Index tensors are [banks,W] /
+ * [banks,R] in index_dtype; weights, values, gates and output share act_dtype.
+ * erase_gate may equal input_gate (the reference's default, allocator.py:1439).
+ * first_touch (optional, may be NULL) receives uint8 [banks,W]. */
+typedef struct cow_step {
+  const void* write_indices;
+  const void* write_weights;
+  const void* values;
+  const void* input_gate;
+  const void* erase_gate;
+  const void* forget_log_gate;
+  const void* read_indices;
+  const void* read_weights;
+  void* output;
+  uint8_t* first_touch;
+} cow_step;
+
+/* Library / ABI version and the bytes of decode scan scratch a launch of
+ * `layers` pools with `total_banks` banks needs (zero-filled before first use,
+ * reused across launches on one stream; calls that overlap on the GPU must
+ * use distinct scratch). */
+int cow_abi_version(void);
+/* Text of the last CUDA error an entry point of this thread returned
+ * COW_ERR_CUDA for ("no error" if none). */
+const char* cow_last_error(void);
+int64_t cow_decode_scratch_bytes(int64_t total_banks, int32_t layers);
+
+/* Fused packed decode step over `layers` independent pools in ONE launch.
+ * Replaces packed_sdm_cow_step's Triton path (allocator.py:1179-1262, kernel
+ * allocator.py:74-229) and its torch path (allocator.py:1467-1526), with the
+ * torch path's deterministic pop order: pop free_rows[old_free-1-rank], rank
+ * = prefix count of first touches over the flattened [banks,W] order.
+ * Limits: width % 4 == 0, width <= 512, W <= 32, R <= 256, layers <= 8; all
+ * pools share width, W, R, slab dtype, act dtype and index dtype. */
+int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers,
+                    int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
+                    void* scan_scratch, int64_t scratch_bytes, void* stream);
+
+/* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
+ * allocator.py:368-460): the same math on dense [banks,slots,width] tables.
+ * memories[l] has dtype mem_dtype; same limits as cow_decode_step. */
+int cow_dense_step(void* const* memories, const int64_t* banks, const cow_step* steps,
+                   int32_t layers, int64_t slots, int64_t width, int32_t mem_dtype,
+                   int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
+                   void* stream);
+
+/* Fill a fresh pool: map = -1, free_rows = arange(capacity), free_count =
+ * capacity, status = 0 (PackedSDMCopyOnWriteState.allocate, allocator.py:507-586). */
+int cow_init_pool(const cow_pool* pool, void* stream);
+
+/* Prefix-count helpers shared by the lifecycle operations.  `flags_scratch`
+ * is int32 [cow_scan_blocks(n) + 8].  Phase 1 counts (and, for release /
+ * append, updates free_count on the device); the total lands in
+ * flags_scratch[0] so the host can size new buffers before phase 2. */
+int64_t cow_scan_blocks(int64_t n);
+
+/* Prefill handoff, sparse form.  Marks the union of hard-written addresses
+ * of a [banks,T,W] route list (the active mask of inference.py:334-347):
+ * map[bank, slot] = 0 for every written slot.  `map` must hold -1 elsewhere
+ * (the caller fills it).  Out-of-range indices set COW_ST_INDEX_RANGE. */
+int cow_prefill_mark(const void* write_indices, int32_t index_dtype, int64_t banks, int64_t time,
+                     int32_t writes, int64_t slots, int32_t* map, int32_t* status, void* stream);
+
+/* map[i] = active[i] ? 0 : -1 for a uint8/bool [banks,slots] mask. */
+int cow_mask_to_map(const uint8_t* active, int64_t n, int32_t* map, void* stream);
+
+/* nonzero()-order layout, phase 1: count the entries of `map` that are >= 0.
+ * The total lands in flags_scratch[0] (device int32), which the host reads
+ * to size the slab before phase 2. */
+int cow_pack_count(const int32_t* map, int64_t n, int32_t* flags_scratch, void* stream);
+/* from_dense_overlay layout (allocator.py:589-690), phase 2: map[i] = rank in
+ * nonzero() order (or -1), src_index[rank] = i, free_rows[:cap-A] = arange(A,
+ * cap), free_count = cap - A, status = 0.  Rows are copied by cow_copy_rows. */
+int cow_pack_apply(int32_t* map, int64_t n, int32_t* src_index, const cow_pool* pool,
+                   int32_t* flags_scratch, void* stream);
+
+/* Copy rows into a slab.  mode 0: dst[dst_rows ? dst_rows[k] : k] =
+ * src[src_rows ? src_rows[k] : k]; mode 1: src_rows[k] is a flat (bank*slots+slot)
+ * index and the row comes from m0[templates[bank], slot] (first-touch copy). */
+int cow_copy_rows(void* dst, int32_t dst_dtype, const int32_t* dst_rows, const void* src,
+                  int32_t src_dtype, const int32_t* src_rows, int64_t count, int64_t width,
+                  int32_t mode, const float* m0, const int64_t* templates, int64_t slots,
+                  void* stream);
+
+/* Sparse prefix recurrence on a packed pool whose touched rows are already
+ * materialised from m0: one warp per bank walks the T tokens, applying the
+ * gated-delta write (sdm.py:474-529 restricted to written rows) and the
+ * read-after-write readout.  Inputs [banks,T,...]; readings [banks,T,width]. */
+int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t time,
+                           int32_t writes, int32_t reads, int32_t index_dtype,
+                           int32_t act_dtype, void* stream);
+
+/* grow_capacity (allocator.py:692-744): copy rows [0,old_cap) into the new
+ * slab, the old free stack below arange(old_cap,new_cap) in the new stack,
+ * free_count += new_cap-old_cap, status = 0. */
+int cow_grow(const void* old_slab, const int32_t* old_free_rows, int64_t old_capacity,
+             void* new_slab, int32_t* new_free_rows, int64_t new_capacity, int64_t width,
+             int32_t slab_dtype, int32_t* free_count, int32_t* status, void* stream);
+
+/* release (allocator.py:1019-1068): push every live row of the selected banks
+ * at old_free + rank over the flattened [S,slots] order given; clear their map
+ * rows.  `released` receives the count (device int32).  `bank_mask` is int32
+ * [banks] scratch used to reject out-of-range or repeated bank indices
+ * (COW_ST_BAD_BANK_LIST in the pool status; nothing is released then). */
+int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count,
+                int32_t* bank_mask, int32_t* flags_scratch, int32_t* released, void* stream);
+
+/* trim_capacity (allocator.py:776-840), phase 2 after cow_pack_count on the
+ * pool's map: new_map = rank in nonzero() order, rows gathered into
+ * new_slab[0..A), new_free_rows[:new_cap-A] = arange(A,new_cap). */
+int cow_repack(const cow_pool* pool, int32_t* new_map, void* new_slab, int32_t* new_free_rows,
+               int64_t new_capacity, int32_t* src_rows, int32_t* flags_scratch, void* stream);
+
+/* append_banks_from (allocator.py:842-915), after cow_pack_count on other's
+ * map: pop A rows from the top of dst's stack in other's nonzero() order, copy
+ * the rows, write the admitted map rows into admitted_map [other.banks,slots]
+ * and decrement dst's free_count. */
+int cow_append(const cow_pool* dst, const cow_pool* other, int32_t* admitted_map,
+               int32_t* src_rows, int32_t* dst_rows, int32_t* flags_scratch, void* stream);
+
+/* retain_banks (allocator.py:917-943): new_map[s] = map[idx[s]], new_templates[s]
+ * = templates[idx[s]]; sets COW_ST_BAD_BANK_LIST / COW_ST_DISCARD_LIVE in
+ * `status` (a scratch status word, not the pool's) instead of raising.
+ * `selected` is int32 [banks] scratch. */
+int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count,
+               int32_t* new_map, int64_t* new_templates, int32_t* selected, int32_t* status,
+               void* stream);
+
+/* validate_invariants (allocator.py:1070-1096) on the device: `counts` is
+ * int32 [capacity] scratch; result bits are OR-ed into `status`. */
+int cow_validate(const cow_pool* pool, int32_t* counts, int32_t* status, void* stream);
+
+/* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
+int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COW_SDM_H */
