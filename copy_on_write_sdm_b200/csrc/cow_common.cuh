@@ -15,6 +15,7 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kBanksPerCta = 4;  // warps per decode CTA
 constexpr int kSpinLimit = 1 << 21;
+constexpr int kScanHeaderBytes = 8 * COW_MAX_LAYERS;  // per pool: ticket, epoch
 
 // --------------------------------------------------------------------------
 // element access
@@ -147,9 +148,9 @@ struct DecodeLayer {
 
 struct DecodeLaunch {
   DecodeLayer layer[COW_MAX_LAYERS];
-  uint32_t* header;    // [ticket, done, epoch, pad]
-  uint64_t* flags;     // one per tile (global ticket)
-  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, _pad;
+  uint32_t* header;    // per pool: [ticket, epoch]
+  uint64_t* flags;     // one per tile, pool-major
+  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles;
 };
 
 constexpr uint32_t kFlagAggregate = 1u;
@@ -175,51 +176,72 @@ __device__ __forceinline__ int warp_sum(int v) {
 //
 // `row` indexes the [rows, W] / [rows, R] route tensors; `map_row` selects the
 // bank's map row (they differ in the prefill, whose routes are [banks*T, ...]).
-template <bool kDense>
+// Every index and weight is loaded in one round, every map entry in a second:
+// two dependent memory round trips in all.  Lane l holds write slot l and read
+// slots l, l+32, ... (R <= 32*RC).
+template <bool kDense, int RC>
 __device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, const int32_t* map,
                                             int64_t row, int64_t map_row, int64_t N, int W, int R,
                                             int idx64, int adt, int lane, unsigned& first_mask,
                                             int& error_bits) {
-  bool bad = false;
-  int wi = 0, wp = -1;
+  int64_t wraw = 0;
   float wwv = 0.f;
   if (lane < W) {
-    const int64_t raw = ld_index(st.write_indices, row * W + lane, idx64);
-    const bool ok = raw >= 0 && raw < N;
-    wi = ok ? static_cast<int>(raw) : 0;
-    if (!kDense) wp = map[map_row * N + wi];
+    wraw = ld_index(st.write_indices, row * W + lane, idx64);
     wwv = ld1_rt(st.write_weights, row * W + lane, adt);
-    bad = !ok;
+  }
+  int64_t rraw[RC];
+  float rwv[RC];
+#pragma unroll
+  for (int c = 0; c < RC; ++c) {
+    const int r = c * 32 + lane;
+    rraw[c] = 0;
+    rwv[c] = 0.f;
+    if (r < R) {
+      rraw[c] = ld_index(st.read_indices, row * R + r, idx64);
+      rwv[c] = ld1_rt(st.read_weights, row * R + r, adt);
+    }
+  }
+  const bool wok = lane < W && wraw >= 0 && wraw < N;
+  bool bad = lane < W && !wok;
+  const int wi = wok ? static_cast<int>(wraw) : 0;
+  int wp = -1;
+  if (!kDense && lane < W) wp = map[map_row * N + wi];
+  int ri[RC], rp[RC];
+#pragma unroll
+  for (int c = 0; c < RC; ++c) {
+    const int r = c * 32 + lane;
+    const bool ok = rraw[c] >= 0 && rraw[c] < N;
+    ri[c] = ok ? static_cast<int>(rraw[c]) : 0;
+    rp[c] = -1;
+    if (r < R) {
+      bad |= !ok;
+      if (!kDense) rp[c] = map[map_row * N + ri[c]];
+    }
   }
   // Out-of-range lanes get a unique sentinel so they never count as repeats.
-  const bool valid_w = lane < W && !bad;
-  const unsigned same = __match_any_sync(kFull, valid_w ? wi : -1 - lane);
-  const bool dup = valid_w && __popc(same) > 1;
+  const unsigned same = __match_any_sync(kFull, wok ? wi : -1 - lane);
+  const bool dup = wok && __popc(same) > 1;
   first_mask = __ballot_sync(kFull, lane < W && wp < 0 && !kDense);
-  sm.widx[lane] = wi;
+  sm.widx[lane] = lane < W ? wi : -1;
   sm.wphys[lane] = wp;
   sm.ww[lane] = wwv;
-  __syncwarp();
-  for (int r = lane; r < R; r += 32) {
-    const int64_t raw = ld_index(st.read_indices, row * R + r, idx64);
-    const bool ok = raw >= 0 && raw < N;
-    const int ri = ok ? static_cast<int>(raw) : 0;
-    const int p = kDense ? -1 : map[map_row * N + ri];
-    int fw = -1;
-    for (int w = 0; w < W; ++w) fw = (sm.widx[w] == ri) ? w : fw;
-    sm.ridx[r] = ri;
-    sm.rsrc[r] = fw >= 0 ? -(fw + 2) : (p >= 0 ? p : -1);
-    sm.rw[r] = ld1_rt(st.read_weights, row * R + r, adt);
-    bad |= !ok;
-  }
+  sm.fwt[lane] = 0.f;
   __syncwarp();
   // Reads of a slot written this step see the updated row (read-after-write,
   // allocator.py:1503-1517); its value is still in registers, so those reads
-  // are folded into one weight per write slot instead of reloading the row.
-  if (lane < W) {
-    float f = 0.f;
-    for (int r = 0; r < R; ++r) f += (sm.rsrc[r] == -(lane + 2)) ? sm.rw[r] : 0.f;
-    sm.fwt[lane] = f;
+  // are folded into one weight per write slot (fwt) instead of reloading it.
+#pragma unroll
+  for (int c = 0; c < RC; ++c) {
+    const int r = c * 32 + lane;
+    if (r < R) {
+      int fw = -1;
+      for (int w = 0; w < W; ++w) fw = (sm.widx[w] == ri[c]) ? w : fw;
+      sm.ridx[r] = ri[c];
+      sm.rsrc[r] = fw >= 0 ? -(fw + 2) : (rp[c] >= 0 ? rp[c] : -1);
+      sm.rw[r] = rwv[c];
+      if (fw >= 0) atomicAdd(&sm.fwt[fw], rwv[c]);
+    }
   }
   const bool any_dup = __any_sync(kFull, dup);
   const bool any_oob = __any_sync(kFull, bad);
@@ -267,43 +289,66 @@ __device__ __forceinline__ void gated_delta(float4 (&upd)[WMAX][CH], const WarpM
   (void)D;
 }
 
-// Weighted sparse read after the write (allocator.py:1507-1517).  Rows of
-// slots written this step come from registers; the rest from the slab
-// (private) or M0 (shared).  Loads are issued in groups for memory-level
-// parallelism.
-template <int SDT, int CH, int WMAX>
-__device__ __forceinline__ void sparse_read(float4 (&acc)[CH], const float4 (&upd)[WMAX][CH],
-                                            const WarpMeta& sm, int W, int R, const void* rows,
-                                            int64_t row_base, const float* m0, int64_t m0_base,
-                                            int lane, int D) {
-  constexpr int G = CH >= 4 ? 2 : (CH == 2 ? 4 : 8);
+// Weighted sparse read after the write (allocator.py:1507-1517), in pieces so
+// the first group of read rows can be requested together with the write rows.
+// Rows of slots written this step come from registers (add_forwarded); the
+// rest from the slab / dense table (src >= 0) or M0 (src == -1).
+template <int CH>
+struct ReadGroup {
+  static constexpr int G = CH >= 4 ? 4 : 16 / CH;
+};
+
+template <int SDT, int CH>
+__device__ __forceinline__ void load_read_group(float4 (&v)[ReadGroup<CH>::G][CH], float (&wt)[ReadGroup<CH>::G],
+                                                const WarpMeta& sm, int r0, int R, const void* rows,
+                                                int64_t row_base, const float* m0, int64_t m0_base, int lane,
+                                                int D) {
+  constexpr int G = ReadGroup<CH>::G;
 #pragma unroll
-  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int r0 = 0; r0 < R; r0 += G) {
-    float4 v[G][CH];
-    float wt[G];
+  for (int j = 0; j < G; ++j) {
+    const int r = r0 + j;
+    const int src = r < R ? sm.rsrc[r] : -2;
+    wt[j] = src >= -1 ? sm.rw[r] : 0.f;
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int r = r0 + j;
-      const int src = r < R ? sm.rsrc[r] : -2;
-      wt[j] = src >= -1 ? sm.rw[r] : 0.f;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int col = (c * 32 + lane) * 4;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (col < D) {
-          if (src >= 0) x = Elem<SDT>::ld4(rows, (row_base + src) * D + col);
-          else if (src == -1) x = ld4_m0(m0, (m0_base + sm.ridx[r]) * D + col);
-        }
-        v[j][c] = x;
+    for (int c = 0; c < CH; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col < D) {
+        if (src >= 0) x = Elem<SDT>::ld4(rows, (row_base + src) * D + col);
+        else if (src == -1) x = ld4_m0(m0, (m0_base + sm.ridx[r]) * D + col);
       }
-    }
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-#pragma unroll
-      for (int c = 0; c < CH; ++c) acc[c] = f4_axpy(wt[j], v[j][c], acc[c]);
+      v[j][c] = x;
     }
   }
+}
+
+template <int CH>
+__device__ __forceinline__ void accumulate_group(float4 (&acc)[CH], const float4 (&v)[ReadGroup<CH>::G][CH],
+                                                 const float (&wt)[ReadGroup<CH>::G]) {
+#pragma unroll
+  for (int j = 0; j < ReadGroup<CH>::G; ++j) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) acc[c] = f4_axpy(wt[j], v[j][c], acc[c]);
+  }
+}
+
+// Groups after the first: load and accumulate in turn.
+template <int SDT, int CH>
+__device__ __forceinline__ void read_remaining(float4 (&acc)[CH], const WarpMeta& sm, int R, const void* rows,
+                                               int64_t row_base, const float* m0, int64_t m0_base, int lane,
+                                               int D) {
+  constexpr int G = ReadGroup<CH>::G;
+  for (int r0 = G; r0 < R; r0 += G) {
+    float4 v[G][CH];
+    float wt[G];
+    load_read_group<SDT, CH>(v, wt, sm, r0, R, rows, row_base, m0, m0_base, lane, D);
+    accumulate_group<CH>(acc, v, wt);
+  }
+}
+
+template <int CH, int WMAX>
+__device__ __forceinline__ void add_forwarded(float4 (&acc)[CH], const float4 (&upd)[WMAX][CH], const WarpMeta& sm,
+                                              int W) {
 #pragma unroll
   for (int w = 0; w < WMAX; ++w) {
     if (w < W) {
@@ -367,21 +412,23 @@ inline bool check_step_ptrs(const cow_step& s, int adt) {
          s.read_indices && s.read_weights && s.output && row_aligned(s.values, adt) && row_aligned(s.output, adt);
 }
 
-#define COW_SELECT_KERNEL(KERNEL, SDT, CH, WMAX_SMALL, FN)                 \
-  do {                                                                      \
-    if (SDT == COW_F32) {                                                   \
-      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_F32, 1, 8> : KERNEL<COW_F32, 1, 32>;   \
-      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_F32, 2, 8> : KERNEL<COW_F32, 2, 32>; \
-      else FN = WMAX_SMALL ? KERNEL<COW_F32, 4, 8> : KERNEL<COW_F32, 4, 32>;           \
-    } else if (SDT == COW_BF16) {                                           \
-      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_BF16, 1, 8> : KERNEL<COW_BF16, 1, 32>; \
-      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_BF16, 2, 8> : KERNEL<COW_BF16, 2, 32>; \
-      else FN = WMAX_SMALL ? KERNEL<COW_BF16, 4, 8> : KERNEL<COW_BF16, 4, 32>;         \
-    } else {                                                                \
-      if (CH == 1) FN = WMAX_SMALL ? KERNEL<COW_F16, 1, 8> : KERNEL<COW_F16, 1, 32>;   \
-      else if (CH == 2) FN = WMAX_SMALL ? KERNEL<COW_F16, 2, 8> : KERNEL<COW_F16, 2, 32>; \
-      else FN = WMAX_SMALL ? KERNEL<COW_F16, 4, 8> : KERNEL<COW_F16, 4, 32>;           \
-    }                                                                       \
+// Kernel variants: slab dtype x row chunks (width <= 128/256/512) x route
+// capacity ("small": W <= 8 and R <= 32; otherwise W <= 32 and R <= 256).
+#define COW_VARIANT(KERNEL, SDT_, CH_, SMALL) (SMALL ? KERNEL<SDT_, CH_, 8, 1> : KERNEL<SDT_, CH_, 32, 8>)
+#define COW_SELECT_KERNEL(KERNEL, SDT, CH, SMALL, FN)                                          \
+  do {                                                                                          \
+    if (SDT == COW_F32) {                                                                       \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F32, 1, SMALL)                                     \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F32, 2, SMALL) : COW_VARIANT(KERNEL, COW_F32, 4, SMALL)); \
+    } else if (SDT == COW_BF16) {                                                               \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_BF16, 1, SMALL)                                    \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_BF16, 2, SMALL) : COW_VARIANT(KERNEL, COW_BF16, 4, SMALL)); \
+    } else {                                                                                    \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F16, 1, SMALL)                                     \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F16, 2, SMALL) : COW_VARIANT(KERNEL, COW_F16, 4, SMALL)); \
+    }                                                                                           \
   } while (0)
+
+inline bool small_routes(int writes, int reads) { return writes <= 8 && reads <= 32; }
 
 }  // namespace

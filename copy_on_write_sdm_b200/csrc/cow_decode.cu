@@ -25,70 +25,83 @@ namespace {
 // fused packed decode step
 // --------------------------------------------------------------------------
 
-template <int SDT, int CH, int WMAX>
+template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_decode_kernel(const __grid_constant__ DecodeLaunch P) {
   __shared__ WarpMeta s_meta[kBanksPerCta];
-  __shared__ int s_cnt[kBanksPerCta];
-  __shared__ uint32_t s_ticket, s_epoch;
-  __shared__ int s_layer, s_old_free, s_tile_excl;
+  __shared__ int s_tile;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int D = P.width, W = P.writes, R = P.reads;
 
-  if (threadIdx.x == 0) {
-    const uint32_t t = atomicAdd(&P.header[0], 1u);
-    int l = 0;
-    while (l + 1 < P.layers && static_cast<int>(t) >= P.layer[l].tile_begin + P.layer[l].tiles) ++l;
-    s_ticket = t;
-    s_layer = l;
-    s_epoch = *reinterpret_cast<volatile uint32_t*>(&P.header[2]);
-    s_old_free = *reinterpret_cast<volatile int32_t*>(P.layer[l].free_count);
+  // Pool of this block: contiguous block ranges, pool-major.
+  int l = 0;
+  while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l].tile_begin + P.layer[l].tiles) ++l;
+  const DecodeLayer& L = P.layer[l];
+  uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
+  int tile;
+  if (P.dynamic_tiles) {
+    // More blocks than can be resident at once: a ticket orders the tiles by
+    // start time, so a warp only ever waits on warps that are running.
+    if (threadIdx.x == 0) s_tile = static_cast<int>(atomicAdd(&hdr[0], 1u));
+    __syncthreads();
+    tile = s_tile;
+  } else {
+    tile = static_cast<int>(blockIdx.x) - L.tile_begin;
   }
-  __syncthreads();
-  const DecodeLayer& L = P.layer[s_layer];
-  const int tile = static_cast<int>(s_ticket) - L.tile_begin;
+  // One warp = one bank = one scan element; nothing below synchronises the block.
   const int64_t bank = static_cast<int64_t>(tile) * kBanksPerCta + warp;
-  const bool live = bank < L.banks;
+  if (bank >= L.banks) return;
   const int64_t N = L.slots;
   WarpMeta& sm = s_meta[warp];
+  uint64_t* const flags = P.flags + static_cast<int64_t>(L.tile_begin) * kBanksPerCta;
 
-  unsigned first_mask = 0;
-  bool bad = false;
-  int route_bits = 0;
-  int64_t tmpl = 0;
-  if (live) {
-    const bool bad_route = load_routes<false>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64,
-                                              P.act_dt, lane, first_mask, route_bits);
-    tmpl = L.templates[bank];
-    const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
-    bad = bad_route || bad_tmpl;
-    if (bad && lane == 0) {
-      atomicOr(L.status, route_bits | (bad_tmpl ? COW_ST_TEMPLATE_RANGE : 0));
-    }
-    if (bad) first_mask = 0;
+  // Round 1: everything that does not depend on the routes.  The epoch and
+  // the free count are read before this warp publishes anything; the pool's
+  // last bank rewrites them only after every bank has published, so all
+  // banks see the launch's starting values.
+  uint32_t epoch = 0;
+  int old_free = 0;
+  if (lane == 0) {
+    epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
+    old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
   }
-  if (lane == 0) s_cnt[warp] = __popc(first_mask);
-  __syncthreads();
-
-  // Publish this tile's first-touch aggregate as early as possible.
-  int tile_agg = 0;
+  const int64_t tmpl = L.templates[bank];
+  const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
+  const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
+  const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  float4 val[CH];
 #pragma unroll
-  for (int w = 0; w < kBanksPerCta; ++w) tile_agg += s_cnt[w];
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t st = tile == 0 ? kFlagInclusive : kFlagAggregate;
-    *reinterpret_cast<volatile uint64_t*>(&P.flags[s_ticket]) =
-        pack_flag(s_epoch, st, static_cast<uint32_t>(tile_agg));
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  unsigned first_mask = 0;
+  int route_bits = 0;
+  const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
+                                                first_mask, route_bits);
+  const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
+  const bool bad = bad_route || bad_tmpl;
+  if (bad) {
+    if (lane == 0) atomicOr(L.status, route_bits | (bad_tmpl ? COW_ST_TEMPLATE_RANGE : 0));
+    first_mask = 0;
+  }
+  epoch = __shfl_sync(kFull, epoch, 0);
+  old_free = __shfl_sync(kFull, old_free, 0);
+  const int count = __popc(first_mask);
+  if (lane == 0) {
+    *reinterpret_cast<volatile uint64_t*>(flags + bank) =
+        pack_flag(epoch, bank == 0 ? kFlagInclusive : kFlagAggregate, static_cast<uint32_t>(count));
   }
 
-  // Row traffic and arithmetic: independent of where first touches land.
+  // Row traffic and arithmetic; only the placement of first touches waits
+  // for the scan.  Write rows and the first read group are requested together.
   float4 upd[WMAX][CH];
-  if (live && !bad) {
-    const float alpha = expf(ld1_rt(L.step.forget_log_gate, bank, P.act_dt));
-    const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
-    const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  float4 acc[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (!bad) {
     const int64_t m0_base = tmpl * N;
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -107,13 +120,10 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 val[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
+    float4 v0[ReadGroup<CH>::G][CH];
+    float wt0[ReadGroup<CH>::G];
+    load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
+    gated_delta<SDT, CH, WMAX>(upd, sm, W, expf(fl), in_g, er_g, val, lane, D);
     // Rows that already had a private copy are written back in place now.
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -128,89 +138,82 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 acc[CH];
-    sparse_read<SDT, CH, WMAX>(acc, upd, sm, W, R, L.slab, 0, L.m0, m0_base, lane, D);
+    accumulate_group<CH>(acc, v0, wt0);
+    read_remaining<SDT, CH>(acc, sm, R, L.slab, 0, L.m0, m0_base, lane, D);
+    add_forwarded<CH, WMAX>(acc, upd, sm, W);
+  }
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], P.act_dt);
-    }
-  } else if (live) {
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) st4_rt(L.step.output, bank * D + col, make_float4(0.f, 0.f, 0.f, 0.f), P.act_dt);
-    }
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], P.act_dt);
   }
 
-  // Decoupled look-back over the preceding tiles of this pool (warp 0).
-  if (warp == 0) {
-    int excl = 0;
-    if (tile > 0) {
-      int64_t pred = static_cast<int64_t>(s_ticket) - 1;
-      const int64_t first_ticket = L.tile_begin;
-      bool timed_out = false;
-      while (true) {
-        const int64_t idx = pred - lane;
-        uint32_t st = kFlagInclusive, v = 0;
-        if (idx >= first_ticket) {
-          int spins = 0;
-          while (true) {
-            const uint64_t f = ld_volatile_u64(&P.flags[idx]);
-            st = (static_cast<uint32_t>(f >> 32) == s_epoch) ? static_cast<uint32_t>((f >> 30) & 3u) : 0u;
-            v = static_cast<uint32_t>(f & 0x3fffffffu);
-            if (st != 0u) break;
-            if (++spins > kSpinLimit) {
-              timed_out = true;
-              st = kFlagInclusive;
-              v = 0;
-              break;
-            }
-            __nanosleep(spins < 64 ? 32 : 256);
+  // Decoupled look-back over the preceding banks of this pool, 32 at a time.
+  // It always runs, so inclusive prefixes keep successors' look-backs short.
+  int excl = 0;
+  if (bank > 0) {
+    int64_t pred = bank - 1;
+    bool timed_out = false;
+    while (true) {
+      const int64_t idx = pred - lane;
+      uint32_t st = kFlagInclusive, v = 0;
+      if (idx >= 0) {
+        int spins = 0;
+        while (true) {
+          const uint64_t f = ld_volatile_u64(flags + idx);
+          st = (static_cast<uint32_t>(f >> 32) == epoch) ? static_cast<uint32_t>((f >> 30) & 3u) : 0u;
+          v = static_cast<uint32_t>(f & 0x3fffffffu);
+          if (st != 0u) break;
+          if (++spins > kSpinLimit) {
+            timed_out = true;
+            st = kFlagInclusive;
+            v = 0;
+            break;
           }
+          __nanosleep(spins < 64 ? 20 : 200);
         }
-        __threadfence();
-        const unsigned incl = __ballot_sync(kFull, st == kFlagInclusive);
-        const int stop = incl ? __ffs(incl) - 1 : 31;
-        excl += warp_sum(lane <= stop ? static_cast<int>(v) : 0);
-        if (incl) break;
-        pred -= 32;
       }
-      if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+      const unsigned incl = __ballot_sync(kFull, st == kFlagInclusive);
+      const int stop = incl ? __ffs(incl) - 1 : 31;
+      excl += warp_sum(lane <= stop ? static_cast<int>(v) : 0);
+      if (incl) break;
+      pred -= 32;
     }
-    if (lane == 0) {
-      s_tile_excl = excl;
-      const int inclusive = excl + tile_agg;
-      if (tile > 0) {
-        __threadfence();
-        *reinterpret_cast<volatile uint64_t*>(&P.flags[s_ticket]) =
-            pack_flag(s_epoch, kFlagInclusive, static_cast<uint32_t>(inclusive));
-      }
-      if (tile == L.tiles - 1) {
-        const int remaining = s_old_free - inclusive;
+    if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+  }
+  if (lane == 0) {
+    const int inclusive = excl + count;
+    if (bank > 0) {
+      *reinterpret_cast<volatile uint64_t*>(flags + bank) =
+          pack_flag(epoch, kFlagInclusive, static_cast<uint32_t>(inclusive));
+    }
+    if (bank == L.banks - 1) {
+      // Every bank of this pool has published, hence has read the starting
+      // epoch and free count: close the launch for this pool.
+      if (inclusive > 0) {
+        const int remaining = old_free - inclusive;
         *L.free_count = remaining > 0 ? remaining : 0;
       }
+      if (P.dynamic_tiles) hdr[0] = 0u;
+      *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
     }
   }
-  __syncthreads();
 
   // Place the first touches: pop free_rows[old_free - 1 - rank].
-  if (live && !bad) {
-    int bank_excl = 0;
-    for (int w = 0; w < warp; ++w) bank_excl += s_cnt[w];
-    int newp = -1;
-    const bool first = lane < W && ((first_mask >> lane) & 1u);
-    if (first) {
-      const int rank = s_tile_excl + bank_excl + __popc(first_mask & ((1u << lane) - 1u));
-      const int pos = s_old_free - 1 - rank;
-      if (pos >= 0) {
-        newp = L.free_rows[pos];
-        L.map[bank * N + sm.widx[lane]] = newp;
-      } else {
-        atomicOr(L.status, COW_ST_SLAB_EXHAUSTED);
-      }
+  int newp = -1;
+  const bool first = lane < W && ((first_mask >> lane) & 1u);
+  if (first) {
+    const int rank = excl + __popc(first_mask & ((1u << lane) - 1u));
+    const int pos = old_free - 1 - rank;
+    if (pos >= 0) {
+      newp = L.free_rows[pos];
+      L.map[bank * N + sm.widx[lane]] = newp;
+    } else {
+      atomicOr(L.status, COW_ST_SLAB_EXHAUSTED);
     }
-    if (L.step.first_touch != nullptr && lane < W) L.step.first_touch[bank * W + lane] = (first && newp >= 0) ? 1 : 0;
+  }
+  if (L.step.first_touch != nullptr && lane < W) L.step.first_touch[bank * W + lane] = (first && newp >= 0) ? 1 : 0;
+  if (first_mask != 0u) {
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W && ((first_mask >> w) & 1u)) {
@@ -224,20 +227,6 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-  } else if (live && L.step.first_touch != nullptr && lane < W) {
-    L.step.first_touch[bank * W + lane] = 0;
-  }
-
-  // Recycle the scan header once every tile of this launch is finished.
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t d = atomicAdd(&P.header[1], 1u);
-    if (d == static_cast<uint32_t>(P.total_tiles) - 1u) {
-      P.header[0] = 0u;
-      P.header[1] = 0u;
-      __threadfence();
-      P.header[2] = s_epoch + 1u;
-    }
   }
 }
 
@@ -246,6 +235,36 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 namespace cowrt {
 thread_local int last_cuda_error = 0;
 }  // namespace cowrt
+
+namespace {
+
+// Blocks of `fn` that fit on the current device at once (cached per device
+// and kernel).  A launch within this bound runs its tiles in block order;
+// beyond it the kernel orders tiles by a ticket instead.
+int resident_blocks(const void* fn, int threads) {
+  struct Entry {
+    int device;
+    const void* fn;
+    int blocks;
+  };
+  static Entry cache[64];
+  static int used = 0;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 0;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].device == device && cache[i].fn == fn) return cache[i].blocks;
+  int sms = 0, per_sm = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int blocks = sms * per_sm;
+  if (used < 64) cache[used++] = Entry{device, fn, blocks};
+  return blocks;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -256,8 +275,9 @@ const char* cow_last_error(void) {
 }
 
 int64_t cow_decode_scratch_bytes(int64_t total_banks, int32_t layers) {
+  // one 8-byte scan flag per bank slot (pools padded to whole 4-bank tiles)
   const int64_t tiles = (total_banks + kBanksPerCta - 1) / kBanksPerCta + (layers > 0 ? layers : 1);
-  return 16 + 8 * tiles;
+  return kScanHeaderBytes + 8 * kBanksPerCta * tiles;
 }
 
 int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
@@ -297,9 +317,9 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     tiles += L.tiles;
   }
   if (tiles == 0) return COW_OK;
-  if (scratch_bytes < 16 + 8 * static_cast<int64_t>(tiles)) return COW_ERR_INVALID;
+  if (scratch_bytes < kScanHeaderBytes + 8 * kBanksPerCta * static_cast<int64_t>(tiles)) return COW_ERR_INVALID;
   P.header = static_cast<uint32_t*>(scan_scratch);
-  P.flags = reinterpret_cast<uint64_t*>(static_cast<char*>(scan_scratch) + 16);
+  P.flags = reinterpret_cast<uint64_t*>(static_cast<char*>(scan_scratch) + kScanHeaderBytes);
   P.layers = layers;
   P.width = static_cast<int32_t>(width);
   P.writes = writes;
@@ -309,7 +329,8 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   P.total_tiles = tiles;
   void (*fn)(DecodeLaunch) = nullptr;
   const int ch = width_chunks(width);
-  COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, writes <= 8, fn);
+  COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, small_routes(writes, reads), fn);
+  P.dynamic_tiles = tiles > resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32) ? 1 : 0;
   fn<<<tiles, kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();
 }

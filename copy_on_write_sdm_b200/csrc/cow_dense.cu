@@ -19,7 +19,7 @@ struct DenseLaunch {
   int32_t layers, width, writes, reads, idx64, act_dt;
 };
 
-template <int SDT, int CH, int WMAX>
+template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_dense_kernel(const __grid_constant__ DenseLaunch P) {
   __shared__ WarpMeta s_meta[kBanksPerCta];
@@ -34,15 +34,29 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const int D = P.width, W = P.writes, R = P.reads;
   const int64_t N = P.slots;
   WarpMeta& sm = s_meta[warp];
+  const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
+  const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
+  const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  float4 val[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   unsigned first_mask;
   int route_bits;
-  const bool bad = load_routes<true>(sm, L.step, nullptr, bank, bank, N, W, R, P.idx64, P.act_dt,
-                                     lane, first_mask, route_bits);
+  const bool bad = load_routes<true, RC>(sm, L.step, nullptr, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
+                                         first_mask, route_bits);
   float4 acc[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (!bad) {
-    const float alpha = expf(ld1_rt(L.step.forget_log_gate, bank, P.act_dt));
-    const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
-    const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+    // In the dense table every slot is its own row: rsrc = slot.
+    for (int r = lane; r < R; r += 32) {
+      if (sm.rsrc[r] == -1) sm.rsrc[r] = sm.ridx[r];
+    }
+    __syncwarp();
+    const float alpha = expf(fl);
     float4 upd[WMAX][CH];
     const int64_t base = bank * N;
 #pragma unroll
@@ -56,12 +70,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 val[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    float4 v0[ReadGroup<CH>::G][CH];
+    float wt0[ReadGroup<CH>::G];
+    load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.memory, base, nullptr, 0, lane, D);
     gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -74,15 +85,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    // In the dense table every read slot is "private": rsrc = slot.
-    for (int r = lane; r < R; r += 32) {
-      if (sm.rsrc[r] == -1) sm.rsrc[r] = sm.ridx[r];
-    }
-    __syncwarp();
-    sparse_read<SDT, CH, WMAX>(acc, upd, sm, W, R, L.memory, base, nullptr, 0, lane, D);
-  } else {
-#pragma unroll
-    for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    accumulate_group<CH>(acc, v0, wt0);
+    read_remaining<SDT, CH>(acc, sm, R, L.memory, base, nullptr, 0, lane, D);
+    add_forwarded<CH, WMAX>(acc, upd, sm, W);
   }
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
@@ -124,7 +129,7 @@ int cow_dense_step(void* const* memories, const int64_t* banks, const cow_step* 
   P.act_dt = act_dtype;
   void (*fn)(DenseLaunch) = nullptr;
   const int ch = width_chunks(width);
-  COW_SELECT_KERNEL(cow_dense_kernel, mem_dtype, ch, writes <= 8, fn);
+  COW_SELECT_KERNEL(cow_dense_kernel, mem_dtype, ch, small_routes(writes, reads), fn);
   const int64_t blocks = (total + kBanksPerCta - 1) / kBanksPerCta;
   fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();

@@ -19,7 +19,7 @@ struct PrefillLaunch {
   int32_t width, writes, reads, idx64, act_dt, _pad;
 };
 
-template <int SDT, int CH, int WMAX>
+template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_prefill_kernel(const __grid_constant__ PrefillLaunch P) {
   __shared__ WarpMeta s_meta[kBanksPerCta];
@@ -36,23 +36,32 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     return;
   }
   const int64_t m0_base = tmpl * N;
+  const cow_step& st = P.step;
   for (int64_t t = 0; t < T; ++t) {
-    // Token t of bank b is stored at row b*T + t of every [banks,T,...] input.
-    const cow_step& st = P.step;
+    // Token t of bank b is row b*T + t of every [banks,T,...] input.  The map
+    // is fixed during the walk (all written slots were placed beforehand), so
+    // only the row contents carry the token-to-token dependence.
     const int64_t row = bank * T + t;
+    const float fl = ld1_rt(st.forget_log_gate, row, P.act_dt);
+    const float in_g = ld1_rt(st.input_gate, row, P.act_dt);
+    const float er_g = ld1_rt(st.erase_gate, row, P.act_dt);
+    float4 val[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      val[c] = col < D ? ld4_rt(st.values, row * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     unsigned first_mask;
     int route_bits;
-    const bool bad = load_routes<false>(sm, st, P.map, row, bank, N, W, R, P.idx64, P.act_dt, lane,
-                                        first_mask, route_bits);
-    // Every written slot was materialised before the walk, so an unmapped
-    // write slot means the mark pass and the routes disagree.
+    const bool bad = load_routes<false, RC>(sm, st, P.map, row, bank, N, W, R, P.idx64, P.act_dt, lane,
+                                            first_mask, route_bits);
+    // Every written slot was placed before the walk, so an unmapped write
+    // slot means the mark pass and the routes disagree.
     if (bad || first_mask != 0u) {
       if (lane == 0) atomicOr(P.status, route_bits ? route_bits : COW_ST_INDEX_RANGE);
       return;
     }
-    const float alpha = expf(ld1_rt(st.forget_log_gate, row, P.act_dt));
-    const float in_g = ld1_rt(st.input_gate, row, P.act_dt);
-    const float er_g = ld1_rt(st.erase_gate, row, P.act_dt);
+    const float alpha = expf(fl);
     float4 upd[WMAX][CH];
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -66,12 +75,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 val[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      val[c] = col < D ? ld4_rt(st.values, row * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    float4 v0[ReadGroup<CH>::G][CH];
+    float wt0[ReadGroup<CH>::G];
+    load_read_group<SDT, CH>(v0, wt0, sm, 0, R, P.slab, 0, P.m0, m0_base, lane, D);
     gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -85,7 +91,11 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       }
     }
     float4 acc[CH];
-    sparse_read<SDT, CH, WMAX>(acc, upd, sm, W, R, P.slab, 0, P.m0, m0_base, lane, D);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    accumulate_group<CH>(acc, v0, wt0);
+    read_remaining<SDT, CH>(acc, sm, R, P.slab, 0, P.m0, m0_base, lane, D);
+    add_forwarded<CH, WMAX>(acc, upd, sm, W);
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int col = (c * 32 + lane) * 4;
@@ -125,7 +135,7 @@ int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t
   P.act_dt = act_dtype;
   void (*fn)(PrefillLaunch) = nullptr;
   const int ch = width_chunks(pool->width);
-  COW_SELECT_KERNEL(cow_prefill_kernel, pool->slab_dtype, ch, writes <= 8, fn);
+  COW_SELECT_KERNEL(cow_prefill_kernel, pool->slab_dtype, ch, small_routes(writes, reads), fn);
   const int64_t blocks = (pool->banks + kBanksPerCta - 1) / kBanksPerCta;
   fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();

@@ -1,0 +1,203 @@
+"""SDM controller (PyTorch) feeding the packed copy-on-write kernels.
+
+The controller is the caller of the hot path, not the hot path: layer norm,
+product-key top-k routing, value / gate projections before the step, readings
+norm + output gate + projection after it (reference ``copy_on_write_sdm/sdm.py:
+96-159, 998-1262``; decode split at ``inference.py:459-535``).  Parameter names
+and shapes equal the reference's ``SparseDeltaMemory`` so its checkpoints load
+unchanged (``load_state_dict``).
+
+The dense training recurrence (and its backward) is not part of this package:
+the eval ``forward`` runs the exact recurrence through the sparse prefill
+kernel on a throw-away pool, so it never materialises ``[B,T,N,D]`` states.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .allocator import PackedSDMCopyOnWriteState
+
+
+def product_key_routes(projected: torch.Tensor, *, slots: int, selected: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Product-key address selection (reference sdm.py:96-159).
+
+    ``projected [..., 2*sqrt(N)]`` holds two codebook score vectors.  Each
+    codebook keeps its best ``min(k, sqrt(N))`` entries, the Cartesian sums of
+    the two shortlists are ranked, the best ``k`` pairs give addresses
+    ``first * sqrt(N) + second``, addresses are sorted ascending and the
+    matching pair scores are softmax-normalised.  Returns ``(weights, indices)``.
+    """
+
+    if projected.ndim != 3:
+        raise ValueError("product-key projection must be [B,T,2*sqrt(N)]")
+    root = math.isqrt(slots)
+    if root * root != slots or projected.shape[-1] != 2 * root:
+        raise ValueError("slot count and product-key projection do not match")
+    if not 1 <= selected <= slots:
+        raise ValueError("selected product keys must be between one and slots")
+    short = min(selected, root)
+    a_score, a_idx = torch.topk(projected[..., :root], k=short, dim=-1)
+    b_score, b_idx = torch.topk(projected[..., root:], k=short, dim=-1)
+    # pair (i, j) -> flat position i * short + j, score a_i + b_j
+    pair_score = (a_score[..., :, None] + b_score[..., None, :]).flatten(-2)
+    pair_addr = (a_idx[..., :, None] * root + b_idx[..., None, :]).flatten(-2)
+    best_score, best_pos = torch.topk(pair_score, k=min(selected, pair_score.shape[-1]), dim=-1)
+    addr = pair_addr.gather(-1, best_pos)
+    addr, order = addr.sort(dim=-1)
+    return torch.softmax(best_score.gather(-1, order), dim=-1), addr
+
+
+@dataclass(frozen=True)
+class SDMStepInputs:
+    """Controller outputs for ``T`` positions, laid out per bank (``b*H + h``)."""
+
+    normalized: torch.Tensor  # [B, T, width]
+    write_indices: torch.Tensor  # [B*H, T, W]
+    write_weights: torch.Tensor
+    values: torch.Tensor  # [B*H, T, head_width]
+    input_gate: torch.Tensor  # [B*H, T]
+    forget_log_gate: torch.Tensor
+    read_indices: torch.Tensor  # [B*H, T, R]
+    read_weights: torch.Tensor
+
+
+class SparseDeltaMemory(nn.Module):
+    """One physical SDM layer's controller (reference sdm.py:998-1262 parameter layout)."""
+
+    def __init__(self, width: int, *, slots: int, reads: int, writes: int, memory_heads: int = 1,
+                 norm_eps: float = 1e-6) -> None:
+        super().__init__()
+        if width <= 0 or slots <= 0 or memory_heads <= 0:
+            raise ValueError("width, slots, and memory_heads must be positive")
+        if width % memory_heads:
+            raise ValueError("width must be divisible by memory_heads")
+        root = math.isqrt(slots)
+        if root * root != slots:
+            raise ValueError("faithful SDM slots must be a perfect square")
+        if not 1 <= reads <= slots or not 1 <= writes <= slots:
+            raise ValueError("read and write counts must lie within the table")
+        self.width, self.slots, self.total_slots = width, slots, slots
+        self.reads, self.writes, self.memory_heads = reads, writes, memory_heads
+        self.head_width = width // memory_heads
+        self.key_width_per_head = 2 * root
+        self.key_width = memory_heads * self.key_width_per_head
+        self.input_norm = nn.LayerNorm(width)
+        self.read_projection = nn.Linear(width, self.key_width)
+        self.write_projection = nn.Linear(width, self.key_width)
+        self.value_projection = nn.Linear(width, width)
+        self.forget_projection = nn.Linear(width, memory_heads)
+        self.input_projection = nn.Linear(width, memory_heads)
+        self.A_log = nn.Parameter(torch.empty(memory_heads))
+        self.dt_bias = nn.Parameter(torch.empty(memory_heads))
+        self.output_gate = nn.Linear(width, width)
+        self.output_projection = nn.Linear(width, width)
+        self.initial_memory = nn.Parameter(torch.empty(memory_heads, slots, self.head_width))
+        self.readings_norm = nn.LayerNorm(self.head_width, eps=norm_eps)
+        self.reset_parameters()
+
+    def _projections(self):
+        return (self.read_projection, self.write_projection, self.value_projection, self.forget_projection,
+                self.input_projection, self.output_gate, self.output_projection)
+
+    def _init_gates(self) -> None:
+        # A = U(0,16) clamped at 1e-4, stored as log; dt = exp(U(log 1e-3, log 1e-1)),
+        # stored through the inverse softplus (Mamba-style initialisation).
+        with torch.no_grad():
+            self.A_log.copy_(torch.empty_like(self.A_log).uniform_(0.0, 16.0).clamp_(min=1e-4).log())
+            dt = torch.empty_like(self.dt_bias).uniform_(math.log(1e-3), math.log(1e-1)).exp()
+            self.dt_bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+
+    def reset_parameters(self) -> None:
+        std = self.width ** -0.5
+        for proj in self._projections():
+            nn.init.trunc_normal_(proj.weight, mean=0.0, std=std, a=-3 * std, b=3 * std)
+            nn.init.zeros_(proj.bias)
+        self.input_norm.reset_parameters()
+        self.readings_norm.reset_parameters()
+        self._init_gates()
+        nn.init.trunc_normal_(self.initial_memory, mean=0.0, std=std, a=-3 * std, b=3 * std)
+
+    def reset_role_keyed(self, seed: int) -> None:
+        """Seeded initialisation, one stream per parameter role (random-init serving runs)."""
+        gen_state = torch.random.get_rng_state()
+        try:
+            std = self.width ** -0.5
+            self.input_norm.reset_parameters()
+            self.readings_norm.reset_parameters()
+            for offset, proj in enumerate(self._projections(), start=1):
+                torch.manual_seed(seed + offset)
+                nn.init.trunc_normal_(proj.weight, mean=0.0, std=std, a=-3 * std, b=3 * std)
+                nn.init.zeros_(proj.bias)
+            torch.manual_seed(seed + 8)
+            self._init_gates()
+            torch.manual_seed(seed + 10)
+            nn.init.trunc_normal_(self.initial_memory, mean=0.0, std=std, a=-3 * std, b=3 * std)
+        finally:
+            torch.random.set_rng_state(gen_state)
+
+    # ---------------- controller ----------------
+
+    def _per_bank(self, x: torch.Tensor, batch: int, time: int) -> torch.Tensor:
+        """[B, T, H*k] -> [B*H, T, k] (bank = b*H + h)."""
+        return x.reshape(batch, time, self.memory_heads, -1).permute(0, 2, 1, 3).reshape(
+            batch * self.memory_heads, time, -1)
+
+    def controller(self, tokens: torch.Tensor) -> SDMStepInputs:
+        """Position-parallel routes, values and gates (reference inference.py:459-519, sdm.py:1149-1184)."""
+        if tokens.ndim != 3 or tokens.shape[-1] != self.width:
+            raise ValueError(f"SDM tokens must be [B,T,{self.width}]")
+        batch, time, _ = tokens.shape
+        normalized = self.input_norm(tokens)
+        read_w, read_i = product_key_routes(self._per_bank(self.read_projection(normalized), batch, time).reshape(
+            batch * self.memory_heads, time, -1), slots=self.slots, selected=self.reads)
+        write_w, write_i = product_key_routes(self._per_bank(self.write_projection(normalized), batch, time),
+                                              slots=self.slots, selected=self.writes)
+        values = self._per_bank(self.value_projection(normalized), batch, time)
+        forget = -torch.exp(self.A_log) * F.softplus(self.forget_projection(normalized) + self.dt_bias)
+        gate_in = torch.sigmoid(self.input_projection(normalized))
+        return SDMStepInputs(
+            normalized=normalized,
+            write_indices=write_i, write_weights=write_w, values=values.contiguous(),
+            input_gate=gate_in.permute(0, 2, 1).reshape(batch * self.memory_heads, time),
+            forget_log_gate=forget.permute(0, 2, 1).reshape(batch * self.memory_heads, time),
+            read_indices=read_i, read_weights=read_w,
+        )
+
+    def finish(self, normalized: torch.Tensor, readings: torch.Tensor) -> torch.Tensor:
+        """Readings norm, channel gate and output projection (reference inference.py:522-535)."""
+        batch, time, _ = normalized.shape
+        r = self.readings_norm(readings).reshape(batch, self.memory_heads, time, self.head_width)
+        r = r.permute(0, 2, 1, 3).reshape(batch, time, self.width)
+        return self.output_projection(torch.sigmoid(self.output_gate(normalized)) * r)
+
+    def template_indices(self, batch: int, device) -> torch.Tensor:
+        return torch.arange(self.memory_heads, device=device, dtype=torch.int64).repeat(batch)
+
+    def prefill(self, tokens: torch.Tensor, *, capacity_rows: int | None = None,
+                maximum_future_allocations: int | None = None, growth_quantum_rows: int = 0,
+                state_dtype: torch.dtype = torch.float32) -> tuple[torch.Tensor, PackedSDMCopyOnWriteState]:
+        """Exact prefix pass + packed handoff through the sparse prefill kernel."""
+        step = self.controller(tokens)
+        batch = tokens.shape[0]
+        state, readings = PackedSDMCopyOnWriteState.from_prefix_routes(
+            self.initial_memory,
+            step.write_indices, step.write_weights, step.values, step.input_gate, step.forget_log_gate,
+            step.read_indices, step.read_weights,
+            template_indices=self.template_indices(batch, tokens.device),
+            capacity_rows=capacity_rows, state_dtype=state_dtype,
+            maximum_future_allocations=maximum_future_allocations,
+            growth_quantum_rows=growth_quantum_rows,
+        )
+        return self.finish(step.normalized, readings), state
+
+    @torch.no_grad()
+    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Eval-only exact forward (no gradients: training stays on the reference)."""
+        out, _ = self.prefill(tokens, growth_quantum_rows=max(16, tokens.shape[0] * self.memory_heads))
+        return out

@@ -232,6 +232,61 @@ def prefill_handoff(name, *, seed=3):
     _save(name, out, seed)
 
 
+def model_lifecycle(name, *, seed=0):
+    """Whole reference model: prefill handoff, decode, release/compact, admit, trim."""
+    from copy_on_write_sdm.model import LanguageModel
+
+    torch.manual_seed(seed)
+    model = LanguageModel(vocab_size=97, maximum_sequence_length=40, layout="BABB", width=32, heads=2,
+                          slots=16, reads=4, writes=2, memory_heads=2, activation_dtype=torch.float32)
+    model.initialize_role_keyed(seed)
+    model.eval()
+    g = torch.Generator().manual_seed(seed + 1)
+    out = {f"param_{k}": _np(v) for k, v in model.state_dict().items()}
+    prefix = torch.randint(97, (3, 10), generator=g)
+    out["prefix"] = _np(prefix)
+    with torch.no_grad():
+        logits, state = model.prefill(prefix, capacity=24, sdm_growth_quantum_rows=8)
+        out["prefill_logits"] = _np(logits)
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"prefill_l{i}_", st, out)
+        steps = torch.randint(97, (6, 3, 1), generator=g)
+        out["decode_ids"] = _np(steps)
+        for t in range(6):
+            out[f"decode{t}_logits"] = _np(model.decode(steps[t], state))
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"decoded_l{i}_", st, out)
+        out["released_rows"] = np.int64(state.release_and_compact([1]))
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"compact_l{i}_", st, out)
+        cohort = torch.randint(97, (2, 4), generator=g)
+        out["cohort"] = _np(cohort)
+        out["admit_logits"] = _np(model.admit(cohort, state))
+        # The reference allocates its K/V caches with torch.empty.  After this
+        # admission the per-request-position decode attends over slots that
+        # no token wrote (masked with -inf), and NaN bit patterns there turn
+        # whole rows into NaN.  Zero the never-written slots so the recorded
+        # trajectory is the well-defined one.
+        for cache in (*state.dense_keys, *state.dense_values):
+            for b, pos in enumerate(state.current_positions().tolist()):
+                cache[b, :, pos:].zero_()
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"admit_l{i}_", st, out)
+        out["admit_positions"] = _np(state.current_positions())
+        steps2 = torch.randint(97, (3, 4, 1), generator=g)
+        out["decode2_ids"] = _np(steps2)
+        for t in range(3):
+            out[f"decode2_{t}_logits"] = _np(model.decode(steps2[t], state))
+        out["trimmed_rows"] = np.int64(state.trim_sdm_pools(headroom_rows=4))
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"trim_l{i}_", st, out)
+        sb = state.storage_bytes()
+        out["storage_keys"] = np.array(sorted(sb))
+        out["storage_vals"] = np.array([sb[k] for k in sorted(sb)], dtype=np.int64)
+        out["final_positions"] = _np(state.current_positions())
+    _save(name, out, seed)
+
+
 def main() -> None:
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     # Configuration 1: H=1, N=256, D=128, top-16/top-4, seed 0, B=1, prefix 16 + 32 decode.
@@ -245,6 +300,7 @@ def main() -> None:
                  steps=12, capacity=64 * 64, heads=4)
     lifecycle_trace("lifecycle")
     prefill_handoff("prefill_handoff")
+    model_lifecycle("model_lifecycle")
 
 
 if __name__ == "__main__":

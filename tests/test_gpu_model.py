@@ -1,0 +1,109 @@
+"""Whole-model serving lifecycle on the GPU against the reference's own run.
+
+The golden trace holds a reference ``LanguageModel`` checkpoint and its
+outputs for: prefill handoff, 6 decode steps, release + compaction, admission
+of a cohort at a different position (per-request positions), 3 more decode
+steps and a pool trim.  This package's model loads the same checkpoint and
+must reproduce the allocator state bit for bit and the logits within 1e-4.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return torch.device("cuda:0")
+
+
+def check_pools(state, g, prefix):
+    for i, st in enumerate(state.sdm_states):
+        p = f"{prefix}_l{i}_"
+        np.testing.assert_array_equal(st.logical_to_physical.cpu().numpy(), g[p + "map"], err_msg=p)
+        fc = int(st.free_count)
+        assert fc == int(g[p + "free_count"]), p
+        np.testing.assert_array_equal(st.free_rows[:fc].cpu().numpy(), g[p + "free_stack"], err_msg=p)
+        assert st.capacity_rows == int(g[p + "capacity"]), p
+        mp = st.logical_to_physical.cpu().numpy()
+        b, s = np.nonzero(mp >= 0)
+        np.testing.assert_allclose(st.values.cpu().numpy()[mp[b, s]], g[p + "live_rows"], atol=1e-5, rtol=1e-5,
+                                   err_msg=p)
+        counters = [st.growth_events, st.growth_rows_added, st.growth_rows_copied,
+                    st.proven_maximum_additional_allocations, int(st.capacity_is_proven)]
+        np.testing.assert_array_equal(counters, g[p + "counters"], err_msg=p)
+        st.validate_invariants()
+
+
+def test_model_lifecycle_matches_reference(dev):
+    from copy_on_write_sdm_b200.model import LanguageModel
+
+    g = dict(np.load(os.path.join(GOLDEN, "model_lifecycle.npz")))
+    model = LanguageModel(vocab_size=97, maximum_sequence_length=40, layout="BABB", width=32, heads=2,
+                          slots=16, reads=4, writes=2, memory_heads=2, activation_dtype=torch.float32)
+    params = {k[len("param_"):]: torch.from_numpy(v) for k, v in g.items() if k.startswith("param_")}
+    model.load_state_dict(params, strict=True)
+    model = model.to(dev).eval()
+
+    def close(got, key):
+        # The reference allocates its K/V caches with torch.empty; after an
+        # admission at a different position its masked decode can pick up
+        # NaN bit patterns from unwritten slots (only some rows, depending on
+        # memory contents).  Rows where the reference is finite must match;
+        # ours must be finite everywhere.
+        got = got.float().cpu().numpy()
+        want = g[key]
+        finite = np.isfinite(want).all(axis=-1)
+        assert np.isfinite(got).all(), key
+        np.testing.assert_allclose(got[finite], want[finite], atol=LOGIT_TOL, rtol=LOGIT_TOL, err_msg=key)
+
+    logits, state = model.prefill(torch.from_numpy(g["prefix"]).to(dev), capacity=24, sdm_growth_quantum_rows=8)
+    close(logits, "prefill_logits")
+    check_pools(state, g, "prefill")
+    for t in range(6):
+        close(model.decode(torch.from_numpy(g["decode_ids"][t]).to(dev), state), f"decode{t}_logits")
+    check_pools(state, g, "decoded")
+    assert state.release_and_compact([1]) == int(g["released_rows"])
+    check_pools(state, g, "compact")
+    close(model.admit(torch.from_numpy(g["cohort"]).to(dev), state), "admit_logits")
+    check_pools(state, g, "admit")
+    np.testing.assert_array_equal(state.current_positions().cpu().numpy(), g["admit_positions"])
+    for t in range(3):
+        close(model.decode(torch.from_numpy(g["decode2_ids"][t]).to(dev), state), f"decode2_{t}_logits")
+    assert state.trim_sdm_pools(headroom_rows=4) == int(g["trimmed_rows"])
+    check_pools(state, g, "trim")
+    sb = state.storage_bytes()
+    assert sorted(sb) == list(g["storage_keys"])
+    np.testing.assert_array_equal([sb[k] for k in g["storage_keys"]], g["storage_vals"])
+    np.testing.assert_array_equal(state.current_positions().cpu().numpy(), g["final_positions"])
+
+
+def test_eval_forward_matches_prefill_logits(dev):
+    from copy_on_write_sdm_b200.model import LanguageModel
+
+    torch.manual_seed(0)
+    model = LanguageModel(vocab_size=50, maximum_sequence_length=32, layout="BAB", width=64, heads=4, slots=64,
+                          reads=8, writes=4, memory_heads=2, activation_dtype=torch.float32)
+    model.initialize_role_keyed(0)
+    model = model.to(dev).eval()
+    ids = torch.randint(50, (4, 20), device=dev)
+    full = model(ids)
+    logits, _ = model.prefill(ids, capacity=32, sdm_growth_quantum_rows=64)
+    torch.testing.assert_close(full, logits, atol=1e-5, rtol=1e-5)
+    # decode continues exactly where a longer prefill would be
+    logits_a, state = model.prefill(ids[:, :12], capacity=32, sdm_growth_quantum_rows=64)
+    outs = [model.decode(ids[:, t:t + 1], state) for t in range(12, 20)]
+    torch.testing.assert_close(torch.cat(outs, dim=1), full[:, 12:], atol=2e-5, rtol=2e-5)
