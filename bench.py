@@ -433,11 +433,10 @@ def main() -> int:
     torch.backends.cuda.matmul.allow_tf32 = False
     res = run_gpu(args, rank, world, device)
 
-    total_ms, e2e_ms = res["total_ms"], res["e2e_ms"]
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_ms], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms, e2e_ms = float(t[0]), float(t[1])
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    # Job time = the slowest rank (each rank owns its own 64 requests).
+    total_ms, e2e_ms = reduce_over_ranks([res["total_ms"], res["e2e_ms"]], op="max", device=device)
     if rank != 0:
         torch.distributed.destroy_process_group()
         return 0
