@@ -18,7 +18,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcowsdm.so")
 
 # return codes / dtype codes / status bits (mirrors include/cow_sdm.h)
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_SCRATCH_LIMIT = 0, 1, 2, 3, 4, 5
+NOALLOC_SCRATCH_BYTES = 1 << 20
 F32, BF16, F16 = 0, 1, 2
 I32, I64 = 0, 1
 ST_SLAB_EXHAUSTED = 0x1
@@ -79,6 +80,8 @@ _SIGNATURES = {
     "cow_decode_scratch_bytes": (c_int64, [c_int64, c_int32]),
     "cow_decode_step": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                   c_int32, c_int32, P, c_int64, P]),
+    "cow_decode_step_noalloc": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
+                                          c_int32, c_int32, P]),
     "cow_dense_step": (c_int32, [POINTER(c_void_p), POINTER(c_int64), POINTER(CowStep), c_int32,
                                  c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, P]),
     "cow_init_pool": (c_int32, [POINTER(CowPool), P]),
@@ -131,6 +134,9 @@ def check(rc: int, what: str) -> None:
     if rc in (ERR_INVALID, ERR_UNSUPPORTED):
         kind = "invalid argument" if rc == ERR_INVALID else "unsupported shape"
         raise ValueError(f"{what}: {kind} (libcowsdm code {rc})")
+    if rc == ERR_SCRATCH_LIMIT:
+        raise ValueError(f"{what}: more banks than the fixed no-alloc scratch holds "
+                         f"({NOALLOC_SCRATCH_BYTES} bytes); use the scratch-taking entry point")
     if rc == ERR_CUDA:
         msg = load().cow_last_error().decode()
         raise RuntimeError(f"{what}: CUDA error: {msg}")

@@ -17,6 +17,8 @@
 // COW_ST_WAIT_TIMEOUT instead of hanging.
 
 
+#include <mutex>
+
 #include "cow_common.cuh"
 
 namespace {
@@ -236,6 +238,45 @@ namespace cowrt {
 thread_local int last_cuda_error = 0;
 }  // namespace cowrt
 
+// Look-back scratch of cow_decode_step_noalloc.  Static device memory starts
+// zeroed when the module loads (ticket 0, epoch 0, every flag "not
+// published"), and each launch leaves it ready for the next one.  In host
+// code the name is only a stand-in: the device address comes from
+// cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[COW_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, resolved once
+// per device.
+int noalloc_scratch(void** out) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) {
+    cowrt::last_cuda_error = static_cast<int>(e);
+    return COW_ERR_CUDA;
+  }
+  if (device < 0 || device >= kMaxDevices) return COW_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return COW_OK;
+}
+
+}  // namespace
+
 namespace {
 
 // Blocks of `fn` that fit on the current device at once (cached per device
@@ -333,6 +374,22 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   P.dynamic_tiles = tiles > resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32) ? 1 : 0;
   fn<<<tiles, kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();
+}
+
+int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
+                            int32_t reads, int32_t index_dtype, int32_t act_dtype, void* stream) {
+  if (!pools || !steps || layers < 1 || layers > COW_MAX_LAYERS) return COW_ERR_INVALID;
+  int64_t total_banks = 0;
+  for (int l = 0; l < layers; ++l) {
+    if (pools[l].banks < 0) return COW_ERR_INVALID;
+    total_banks += pools[l].banks;
+  }
+  if (cow_decode_scratch_bytes(total_banks, layers) > COW_NOALLOC_SCRATCH_BYTES) return COW_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != COW_OK) return rc;
+  return cow_decode_step(pools, steps, layers, writes, reads, index_dtype, act_dtype, scratch,
+                         COW_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 }  // extern "C"

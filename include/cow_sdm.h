@@ -113,6 +113,31 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
                     int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
                     void* scan_scratch, int64_t scratch_bytes, void* stream);
 
+/* No counterpart in the reference.  cow_decode_step for callers that cannot
+ * allocate device memory when they call in: a host binding this C ABI from
+ * another language or runtime (cgo, JNI, a C++ server) that does not own the
+ * allocator managing the GPU's memory -- a cudaMalloc behind that allocator's
+ * back would escape its accounting and can synchronise the device -- or a
+ * serving loop that must not allocate while it decodes.  Same arguments and
+ * results as cow_decode_step, minus the scratch: the look-back flags live in a
+ * fixed COW_NOALLOC_SCRATCH_BYTES (1 MiB) array compiled into the library,
+ * which every GPU that loads the library holds until the process exits.
+ * - Limit: cow_decode_scratch_bytes(total banks, layers) must not exceed
+ *   COW_NOALLOC_SCRATCH_BYTES (about 131,000 banks per call); larger calls
+ *   return COW_ERR_SCRATCH_LIMIT and launch nothing.
+ * - The first call on a device resolves the array's address for that device
+ *   (cudaGetSymbolAddress, with the caller's current device); make that first
+ *   call before any stream capture.  `stream` must belong to the current device.
+ * - Every call on a device shares the one array and keeps what the last call
+ *   left there; the kernel returns it to a ready state at the end of each
+ *   launch.  Calls that overlap on the GPU (e.g. on two streams) race on it.
+ * Calls no cudaMalloc, cudaFree or other allocating routine. */
+#define COW_ERR_SCRATCH_LIMIT 5
+#define COW_NOALLOC_SCRATCH_BYTES (1 << 20)
+int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers,
+                            int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
+                            void* stream);
+
 /* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
  * allocator.py:368-460): the same math on dense [banks,slots,width] tables.
  * memories[l] has dtype mem_dtype; same limits as cow_decode_step. */
