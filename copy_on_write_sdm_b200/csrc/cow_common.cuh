@@ -15,6 +15,7 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kBanksPerCta = 4;  // warps per decode CTA
 constexpr int kSpinLimit = 1 << 21;
+constexpr int kLookbackPerLane = 4;  // scan flags each lane reads per look-back probe
 constexpr int kScanHeaderBytes = 8 * COW_MAX_LAYERS;  // per pool: ticket, epoch
 
 // --------------------------------------------------------------------------
@@ -119,6 +120,16 @@ __device__ __forceinline__ float4 ld4_m0(const float* m0, int64_t e) {
   return __ldg(reinterpret_cast<const float4*>(m0 + e));
 }
 
+// 16-byte global -> shared copies that bypass L1 and need no registers.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Largest logical table whose map row a decode warp may stage in shared memory.
+constexpr int kStageSlots = 1024;
+
 // --------------------------------------------------------------------------
 // per-warp route metadata (shared memory, broadcast reads)
 // --------------------------------------------------------------------------
@@ -142,15 +153,16 @@ struct DecodeLayer {
   int32_t* free_count;
   int32_t* status;
   cow_step step;
-  int64_t banks, slots, capacity, template_count;
+  int64_t banks, slots, capacity, template_count, group_begin;
   int32_t tile_begin, tiles;
 };
 
 struct DecodeLaunch {
   DecodeLayer layer[COW_MAX_LAYERS];
   uint32_t* header;    // per pool: [ticket, epoch]
-  uint64_t* flags;     // one per tile, pool-major
-  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles;
+  uint64_t* flags;        // one per bank slot, pool-major (tile_begin * 4 + bank)
+  uint64_t* group_flags;  // one per group of kScanGroup banks, pool-major (group_begin + group)
+  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, _pad;
 };
 
 constexpr uint32_t kFlagAggregate = 1u;
@@ -170,6 +182,72 @@ __device__ __forceinline__ int warp_sum(int v) {
   return v;
 }
 
+// --------------------------------------------------------------------------
+// ordered prefix of first-touch counts across the banks of one pool
+// --------------------------------------------------------------------------
+//
+// Every bank publishes its count (an epoch-tagged "aggregate" flag) as soon as
+// its routes are resolved.  Banks form groups of kScanGroup; the last bank of
+// a group publishes the group total.  A bank's exclusive prefix is the sum of
+// the earlier aggregates of its own group plus the earlier group totals: two
+// probes issued together, about one memory round trip, however many banks run
+// at once (no chain of inclusive prefixes).
+constexpr int kScanGroup = 128;
+
+__device__ __forceinline__ uint32_t wait_flag(const uint64_t* p, uint32_t epoch, bool& timed_out) {
+  int spins = 0;
+  while (true) {
+    const uint64_t f = ld_volatile_u64(p);
+    if (static_cast<uint32_t>(f >> 32) == epoch && ((f >> 30) & 3u) != 0u) return static_cast<uint32_t>(f & 0x3fffffffu);
+    if (++spins > kSpinLimit) {
+      timed_out = true;
+      return 0u;
+    }
+    __nanosleep(spins < 64 ? 20 : 200);
+  }
+}
+
+// Sum of the flags [lo, hi) (hi - lo <= 32 * kLookbackPerLane per probe),
+// each lane waiting on its own flags; the first loads of all lanes go out
+// together.
+__device__ __forceinline__ int sum_flags(const uint64_t* f, int64_t lo, int64_t hi, uint32_t epoch, int lane,
+                                         bool& timed_out) {
+  int total = 0;
+  for (int64_t base = lo; base < hi; base += 32 * kLookbackPerLane) {
+    uint64_t first[kLookbackPerLane];
+#pragma unroll
+    for (int j = 0; j < kLookbackPerLane; ++j) {
+      const int64_t i = base + kLookbackPerLane * lane + j;
+      first[j] = i < hi ? ld_volatile_u64(f + i) : 0;
+    }
+    int part = 0;
+#pragma unroll
+    for (int j = 0; j < kLookbackPerLane; ++j) {
+      const int64_t i = base + kLookbackPerLane * lane + j;
+      if (i < hi) {
+        const uint64_t x = first[j];
+        const bool ready = static_cast<uint32_t>(x >> 32) == epoch && ((x >> 30) & 3u) != 0u;
+        part += static_cast<int>(ready ? static_cast<uint32_t>(x & 0x3fffffffu) : wait_flag(f + i, epoch, timed_out));
+      }
+    }
+    total += warp_sum(part);
+  }
+  return total;
+}
+
+// Exclusive prefix for `bank` (warp-uniform result).  `bank_flags` / `group_flags`
+// are this pool's regions; the bank's own aggregate must already be published.
+__device__ __forceinline__ int pool_prefix(const uint64_t* bank_flags, uint64_t* group_flags, int64_t bank, int count,
+                                           uint32_t epoch, int lane, bool& timed_out) {
+  const int64_t group = bank / kScanGroup, gstart = group * kScanGroup;
+  const int in_group = sum_flags(bank_flags, gstart, bank, epoch, lane, timed_out);
+  if (bank - gstart == kScanGroup - 1 && lane == 0) {
+    *reinterpret_cast<volatile uint64_t*>(group_flags + group) =
+        pack_flag(epoch, kFlagInclusive, static_cast<uint32_t>(in_group + count));
+  }
+  return in_group + sum_flags(group_flags, 0, group, epoch, lane, timed_out);
+}
+
 // Load the W write routes and R read routes of one bank into the warp's
 // metadata.  Returns a warp-uniform "bad" flag (an index out of range or a
 // repeated write address); `first_mask` has bit w set for first touches.
@@ -179,11 +257,19 @@ __device__ __forceinline__ int warp_sum(int v) {
 // Every index and weight is loaded in one round, every map entry in a second:
 // two dependent memory round trips in all.  Lane l holds write slot l and read
 // slots l, l+32, ... (R <= 32*RC).
+//
+// With `staged` (a per-warp shared buffer of N <= kStageSlots ints, N % 4 == 0)
+// the bank's whole map row is copied into shared memory in the first round,
+// so the map lookups cost no second dependent trip to memory.
 template <bool kDense, int RC>
 __device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, const int32_t* map,
                                             int64_t row, int64_t map_row, int64_t N, int W, int R,
                                             int idx64, int adt, int lane, unsigned& first_mask,
-                                            int& error_bits) {
+                                            int& error_bits, int32_t* staged = nullptr) {
+  if (!kDense && staged != nullptr) {
+    const int4* src = reinterpret_cast<const int4*>(map + map_row * N);
+    for (int i = lane; i < static_cast<int>(N >> 2); i += 32) cp_async16(staged + 4 * i, src + i);
+  }
   int64_t wraw = 0;
   float wwv = 0.f;
   if (lane < W) {
@@ -205,8 +291,14 @@ __device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, co
   const bool wok = lane < W && wraw >= 0 && wraw < N;
   bool bad = lane < W && !wok;
   const int wi = wok ? static_cast<int>(wraw) : 0;
+  const int32_t* mrow = map + map_row * N;
+  if (!kDense && staged != nullptr) {
+    cp_async_wait_all();
+    __syncwarp();
+    mrow = staged;
+  }
   int wp = -1;
-  if (!kDense && lane < W) wp = map[map_row * N + wi];
+  if (!kDense && lane < W) wp = mrow[wi];
   int ri[RC], rp[RC];
 #pragma unroll
   for (int c = 0; c < RC; ++c) {
@@ -216,7 +308,7 @@ __device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, co
     rp[c] = -1;
     if (r < R) {
       bad |= !ok;
-      if (!kDense) rp[c] = map[map_row * N + ri[c]];
+      if (!kDense) rp[c] = mrow[ri[c]];
     }
   }
   // Out-of-range lanes get a unique sentinel so they never count as repeats.

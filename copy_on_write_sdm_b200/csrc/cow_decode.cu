@@ -31,6 +31,7 @@ template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_decode_kernel(const __grid_constant__ DecodeLaunch P) {
   __shared__ WarpMeta s_meta[kBanksPerCta];
+  __shared__ __align__(16) int32_t s_map[kBanksPerCta][kStageSlots];
   __shared__ int s_tile;
 
   const int warp = threadIdx.x >> 5;
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   unsigned first_mask = 0;
   int route_bits = 0;
   const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
-                                                first_mask, route_bits);
+                                                first_mask, route_bits, P.stage_map ? s_map[warp] : nullptr);
   const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
   const bool bad = bad_route || bad_tmpl;
   if (bad) {
@@ -94,17 +95,16 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const int count = __popc(first_mask);
   if (lane == 0) {
     *reinterpret_cast<volatile uint64_t*>(flags + bank) =
-        pack_flag(epoch, bank == 0 ? kFlagInclusive : kFlagAggregate, static_cast<uint32_t>(count));
+        pack_flag(epoch, kFlagAggregate, static_cast<uint32_t>(count));
   }
 
-  // Row traffic and arithmetic; only the placement of first touches waits
-  // for the scan.  Write rows and the first read group are requested together.
+  // Row traffic: the write rows and the first read group are requested
+  // together, then the look-back runs while they are in flight.
   float4 upd[WMAX][CH];
-  float4 acc[CH];
-#pragma unroll
-  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 v0[ReadGroup<CH>::G][CH];
+  float wt0[ReadGroup<CH>::G];
+  const int64_t m0_base = tmpl * N;
   if (!bad) {
-    const int64_t m0_base = tmpl * N;
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W) {
@@ -122,11 +122,34 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 v0[ReadGroup<CH>::G][CH];
-    float wt0[ReadGroup<CH>::G];
     load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
+  }
+
+  // Exclusive prefix of first touches over the preceding banks of this pool
+  // (two-level scan, about one round trip), overlapped with the row loads above.
+  bool timed_out = false;
+  const int excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
+  if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+  if (lane == 0) {
+    const int inclusive = excl + count;
+    if (bank == L.banks - 1) {
+      // Every bank of this pool has published, hence has read the starting
+      // epoch and free count: close the launch for this pool.
+      if (inclusive > 0) {
+        const int remaining = old_free - inclusive;
+        *L.free_count = remaining > 0 ? remaining : 0;
+      }
+      if (P.dynamic_tiles) hdr[0] = 0u;
+      *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+    }
+  }
+
+  // Arithmetic, write-back of rows that were already private, readout.
+  float4 acc[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (!bad) {
     gated_delta<SDT, CH, WMAX>(upd, sm, W, expf(fl), in_g, er_g, val, lane, D);
-    // Rows that already had a private copy are written back in place now.
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W) {
@@ -148,57 +171,6 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   for (int c = 0; c < CH; ++c) {
     const int col = (c * 32 + lane) * 4;
     if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], P.act_dt);
-  }
-
-  // Decoupled look-back over the preceding banks of this pool, 32 at a time.
-  // It always runs, so inclusive prefixes keep successors' look-backs short.
-  int excl = 0;
-  if (bank > 0) {
-    int64_t pred = bank - 1;
-    bool timed_out = false;
-    while (true) {
-      const int64_t idx = pred - lane;
-      uint32_t st = kFlagInclusive, v = 0;
-      if (idx >= 0) {
-        int spins = 0;
-        while (true) {
-          const uint64_t f = ld_volatile_u64(flags + idx);
-          st = (static_cast<uint32_t>(f >> 32) == epoch) ? static_cast<uint32_t>((f >> 30) & 3u) : 0u;
-          v = static_cast<uint32_t>(f & 0x3fffffffu);
-          if (st != 0u) break;
-          if (++spins > kSpinLimit) {
-            timed_out = true;
-            st = kFlagInclusive;
-            v = 0;
-            break;
-          }
-          __nanosleep(spins < 64 ? 20 : 200);
-        }
-      }
-      const unsigned incl = __ballot_sync(kFull, st == kFlagInclusive);
-      const int stop = incl ? __ffs(incl) - 1 : 31;
-      excl += warp_sum(lane <= stop ? static_cast<int>(v) : 0);
-      if (incl) break;
-      pred -= 32;
-    }
-    if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
-  }
-  if (lane == 0) {
-    const int inclusive = excl + count;
-    if (bank > 0) {
-      *reinterpret_cast<volatile uint64_t*>(flags + bank) =
-          pack_flag(epoch, kFlagInclusive, static_cast<uint32_t>(inclusive));
-    }
-    if (bank == L.banks - 1) {
-      // Every bank of this pool has published, hence has read the starting
-      // epoch and free count: close the launch for this pool.
-      if (inclusive > 0) {
-        const int remaining = old_free - inclusive;
-        *L.free_count = remaining > 0 ? remaining : 0;
-      }
-      if (P.dynamic_tiles) hdr[0] = 0u;
-      *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
-    }
   }
 
   // Place the first touches: pop free_rows[old_free - 1 - rank].
@@ -282,6 +254,8 @@ namespace {
 // Blocks of `fn` that fit on the current device at once (cached per device
 // and kernel).  A launch within this bound runs its tiles in block order;
 // beyond it the kernel orders tiles by a ticket instead.
+constexpr int64_t kStageMaxBanks = 148 * 16;
+
 int resident_blocks(const void* fn, int threads) {
   struct Entry {
     int device;
@@ -311,14 +285,17 @@ extern "C" {
 
 int cow_abi_version(void) { return COW_ABI_VERSION; }
 
+
 const char* cow_last_error(void) {
   return cudaGetErrorString(static_cast<cudaError_t>(cowrt::last_cuda_error));
 }
 
 int64_t cow_decode_scratch_bytes(int64_t total_banks, int32_t layers) {
-  // one 8-byte scan flag per bank slot (pools padded to whole 4-bank tiles)
-  const int64_t tiles = (total_banks + kBanksPerCta - 1) / kBanksPerCta + (layers > 0 ? layers : 1);
-  return kScanHeaderBytes + 8 * kBanksPerCta * tiles;
+  // one 8-byte scan flag per bank slot (pools padded to whole 4-bank tiles),
+  // then one per group of kScanGroup banks
+  const int64_t pools = layers > 0 ? layers : 1;
+  const int64_t tiles = (total_banks + kBanksPerCta - 1) / kBanksPerCta + pools;
+  return kScanHeaderBytes + 8 * (kBanksPerCta * tiles + total_banks / kScanGroup + pools);
 }
 
 int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
@@ -358,9 +335,15 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     tiles += L.tiles;
   }
   if (tiles == 0) return COW_OK;
-  if (scratch_bytes < kScanHeaderBytes + 8 * kBanksPerCta * static_cast<int64_t>(tiles)) return COW_ERR_INVALID;
+  int64_t groups = 0;
+  for (int l = 0; l < layers; ++l) {
+    P.layer[l].group_begin = groups;
+    groups += (pools[l].banks + kScanGroup - 1) / kScanGroup;
+  }
+  if (scratch_bytes < kScanHeaderBytes + 8 * (kBanksPerCta * static_cast<int64_t>(tiles) + groups)) return COW_ERR_INVALID;
   P.header = static_cast<uint32_t*>(scan_scratch);
   P.flags = reinterpret_cast<uint64_t*>(static_cast<char*>(scan_scratch) + kScanHeaderBytes);
+  P.group_flags = P.flags + kBanksPerCta * static_cast<int64_t>(tiles);
   P.layers = layers;
   P.width = static_cast<int32_t>(width);
   P.writes = writes;
@@ -372,6 +355,16 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   const int ch = width_chunks(width);
   COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, small_routes(writes, reads), fn);
   P.dynamic_tiles = tiles > resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32) ? 1 : 0;
+  // Latency-bound launches (at most ~16 warps per SM) with small tables stage
+  // each bank's map row in shared memory: N*4 extra bytes per bank buy one
+  // dependent memory round trip less.
+  bool stage = true;
+  int64_t total_banks = 0;
+  for (int l = 0; l < layers; ++l) {
+    stage = stage && pools[l].slots <= kStageSlots && pools[l].slots % 4 == 0 && aligned16(pools[l].map);
+    total_banks += pools[l].banks;
+  }
+  P.stage_map = stage && total_banks <= kStageMaxBanks ? 1 : 0;
   fn<<<tiles, kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();
 }

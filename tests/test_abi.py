@@ -27,8 +27,8 @@ def test_host_only_entry_points():
     lib = _lib.load()
     assert lib.cow_abi_version() == 1
     assert lib.cow_last_error() == b"no error"
-    # scratch sizing: per-pool header (8 pools x 8 B) + one flag per bank slot, pools padded to 4-bank tiles (+ one tile per pool)
-    assert lib.cow_decode_scratch_bytes(64 * 7, 7) == 64 + 8 * 4 * (112 + 7)
+    # scratch sizing: per-pool header (8 pools x 8 B) + one flag per bank slot (pools padded to 4-bank tiles, + one tile per pool), one per 128-bank group
+    assert lib.cow_decode_scratch_bytes(64 * 7, 7) == 64 + 8 * (4 * (112 + 7) + 448 // 128 + 7)
     assert lib.cow_scan_blocks(0) == 8
     assert lib.cow_scan_blocks(2048) == 9
 

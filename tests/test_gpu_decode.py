@@ -128,6 +128,18 @@ def test_many_tiles_lookback_and_int32_indices(dev):
                   idx_dtype=torch.int32)
 
 
+@pytest.mark.parametrize("banks,slots", [(64, 4096), (2500, 256)])
+def test_unstaged_map_paths(dev, banks, slots):
+    # N > 1024, or more banks than a latency-bound launch: map entries read from HBM.
+    _random_trace(dev, banks=banks, slots=slots, width=128, W=4, R=16, steps=5, seed=banks)
+
+
+def test_ten_thousand_blocks_ticket_order(dev):
+    # 40,000 banks = 10,000 blocks: far more than are resident, so tiles are
+    # ordered by ticket and the look-back crosses thousands of banks.
+    _random_trace(dev, banks=40000, slots=64, width=128, W=4, R=16, steps=3, seed=17)
+
+
 @pytest.mark.parametrize("width,W,R", [(8, 2, 4), (64, 3, 5), (256, 8, 24), (512, 12, 40), (128, 32, 256)])
 def test_shape_variants(dev, width, W, R):
     _random_trace(dev, banks=37, slots=max(64, R), width=width, W=W, R=R, steps=4, seed=width + W)
@@ -224,3 +236,4 @@ def test_errors_are_reported_not_trapped(dev):
         st.validate_invariants()
     with pytest.raises(ValueError, match="CPU fallback|sm_100a"):
         packed_sdm_cow_step(st, **step_args([[0, 1], [2, 3]], [[0], [1]]), backend="torch")
+
