@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "cow_sdm.h"
 
 #define COW_ABI_VERSION 1
@@ -134,15 +136,17 @@ constexpr int kStageSlots = 1024;
 // per-warp route metadata (shared memory, broadcast reads)
 // --------------------------------------------------------------------------
 
-struct WarpMeta {
+template <int RMAX>
+struct WarpMetaT {
   int widx[COW_MAX_WRITES];
   int wphys[COW_MAX_WRITES];  // map entry before the step (-1 = shared M0)
   float ww[COW_MAX_WRITES];
-  int ridx[COW_MAX_READS];
-  int rsrc[COW_MAX_READS];  // >= 0 slab row, -1 M0 row, <= -2 forwarded write slot -(w+2)
-  float rw[COW_MAX_READS];
   float fwt[COW_MAX_WRITES];  // summed read weight of reads that hit write slot w this step
+  int ridx[RMAX];
+  int rsrc[RMAX];  // >= 0 slab row, -1 M0 row, <= -2 forwarded write slot -(w+2)
+  float rw[RMAX];
 };
+using WarpMeta = WarpMetaT<COW_MAX_READS>;
 
 struct DecodeLayer {
   const float* m0;
@@ -162,7 +166,7 @@ struct DecodeLaunch {
   uint32_t* header;    // per pool: [ticket, epoch]
   uint64_t* flags;        // one per bank slot, pool-major (tile_begin * 4 + bank)
   uint64_t* group_flags;  // one per group of kScanGroup banks, pool-major (group_begin + group)
-  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, _pad;
+  int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, read_stage_bytes;
 };
 
 constexpr uint32_t kFlagAggregate = 1u;
@@ -261,8 +265,8 @@ __device__ __forceinline__ int pool_prefix(const uint64_t* bank_flags, uint64_t*
 // With `staged` (a per-warp shared buffer of N <= kStageSlots ints, N % 4 == 0)
 // the bank's whole map row is copied into shared memory in the first round,
 // so the map lookups cost no second dependent trip to memory.
-template <bool kDense, int RC>
-__device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, const int32_t* map,
+template <bool kDense, int RC, class M>
+__device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int32_t* map,
                                             int64_t row, int64_t map_row, int64_t N, int W, int R,
                                             int idx64, int adt, int lane, unsigned& first_mask,
                                             int& error_bits, int32_t* staged = nullptr) {
@@ -345,8 +349,8 @@ __device__ __forceinline__ bool load_routes(WarpMeta& sm, const cow_step& st, co
 // Gated-delta update of the W write rows (allocator.py:1489-1501): the rows
 // arrive in `upd` (already loaded), leave as the updated values rounded to
 // the slab dtype.
-template <int SDT, int CH, int WMAX>
-__device__ __forceinline__ void gated_delta(float4 (&upd)[WMAX][CH], const WarpMeta& sm, int W,
+template <int SDT, int CH, int WMAX, class M>
+__device__ __forceinline__ void gated_delta(float4 (&upd)[WMAX][CH], const M& sm, int W,
                                             float alpha, float in_g, float er_g,
                                             const float4 (&val)[CH], int lane, int D) {
   float4 ret[CH];
@@ -390,9 +394,9 @@ struct ReadGroup {
   static constexpr int G = CH >= 4 ? 4 : 16 / CH;
 };
 
-template <int SDT, int CH>
+template <int SDT, int CH, class M>
 __device__ __forceinline__ void load_read_group(float4 (&v)[ReadGroup<CH>::G][CH], float (&wt)[ReadGroup<CH>::G],
-                                                const WarpMeta& sm, int r0, int R, const void* rows,
+                                                const M& sm, int r0, int R, const void* rows,
                                                 int64_t row_base, const float* m0, int64_t m0_base, int lane,
                                                 int D) {
   constexpr int G = ReadGroup<CH>::G;
@@ -425,8 +429,8 @@ __device__ __forceinline__ void accumulate_group(float4 (&acc)[CH], const float4
 }
 
 // Groups after the first: load and accumulate in turn.
-template <int SDT, int CH>
-__device__ __forceinline__ void read_remaining(float4 (&acc)[CH], const WarpMeta& sm, int R, const void* rows,
+template <int SDT, int CH, class M>
+__device__ __forceinline__ void read_remaining(float4 (&acc)[CH], const M& sm, int R, const void* rows,
                                                int64_t row_base, const float* m0, int64_t m0_base, int lane,
                                                int D) {
   constexpr int G = ReadGroup<CH>::G;
@@ -438,8 +442,8 @@ __device__ __forceinline__ void read_remaining(float4 (&acc)[CH], const WarpMeta
   }
 }
 
-template <int CH, int WMAX>
-__device__ __forceinline__ void add_forwarded(float4 (&acc)[CH], const float4 (&upd)[WMAX][CH], const WarpMeta& sm,
+template <int CH, int WMAX, class M>
+__device__ __forceinline__ void add_forwarded(float4 (&acc)[CH], const float4 (&upd)[WMAX][CH], const M& sm,
                                               int W) {
 #pragma unroll
   for (int w = 0; w < WMAX; ++w) {
@@ -505,22 +509,65 @@ inline bool check_step_ptrs(const cow_step& s, int adt) {
 }
 
 // Kernel variants: slab dtype x row chunks (width <= 128/256/512) x route
-// capacity ("small": W <= 8 and R <= 32; otherwise W <= 32 and R <= 256).
-#define COW_VARIANT(KERNEL, SDT_, CH_, SMALL) (SMALL ? KERNEL<SDT_, CH_, 8, 1> : KERNEL<SDT_, CH_, 32, 8>)
-#define COW_SELECT_KERNEL(KERNEL, SDT, CH, SMALL, FN)                                          \
-  do {                                                                                          \
-    if (SDT == COW_F32) {                                                                       \
-      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F32, 1, SMALL)                                     \
-                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F32, 2, SMALL) : COW_VARIANT(KERNEL, COW_F32, 4, SMALL)); \
-    } else if (SDT == COW_BF16) {                                                               \
-      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_BF16, 1, SMALL)                                    \
-                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_BF16, 2, SMALL) : COW_VARIANT(KERNEL, COW_BF16, 4, SMALL)); \
-    } else {                                                                                    \
-      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F16, 1, SMALL)                                     \
-                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F16, 2, SMALL) : COW_VARIANT(KERNEL, COW_F16, 4, SMALL)); \
-    }                                                                                           \
+// capacity (W <= 4 and R <= 32; W <= 8 and R <= 32; W <= 32 and R <= 256).
+#define COW_VARIANT(KERNEL, SDT_, CH_, RV) \
+  (RV == 0 ? KERNEL<SDT_, CH_, 4, 1> : (RV == 1 ? KERNEL<SDT_, CH_, 8, 1> : KERNEL<SDT_, CH_, 32, 8>))
+#define COW_SELECT_KERNEL(KERNEL, SDT, CH, RV, FN)                                                            \
+  do {                                                                                                       \
+    if (SDT == COW_F32) {                                                                                    \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F32, 1, RV)                                                     \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F32, 2, RV) : COW_VARIANT(KERNEL, COW_F32, 4, RV));  \
+    } else if (SDT == COW_BF16) {                                                                            \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_BF16, 1, RV)                                                    \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_BF16, 2, RV) : COW_VARIANT(KERNEL, COW_BF16, 4, RV)); \
+    } else {                                                                                                 \
+      FN = CH == 1 ? COW_VARIANT(KERNEL, COW_F16, 1, RV)                                                     \
+                   : (CH == 2 ? COW_VARIANT(KERNEL, COW_F16, 2, RV) : COW_VARIANT(KERNEL, COW_F16, 4, RV));  \
+    }                                                                                                        \
   } while (0)
 
-inline bool small_routes(int writes, int reads) { return writes <= 8 && reads <= 32; }
+// Route variant: 0 (W <= 4, R <= 32), 1 (W <= 8, R <= 32), 2 (W <= 32, R <= 256).
+inline int route_variant(int writes, int reads) { return reads > 32 || writes > 8 ? 2 : (writes > 4 ? 1 : 0); }
+
+// The common shapes (f32 rows, R <= 32, width <= 128) stage their read rows in shared
+// memory with cp.async instead of registers: dynamic shared memory bytes per
+// block for that staging (0 for other shapes).
+inline size_t read_stage_bytes(int reads, int64_t width, int ch, int rv, int dtype) {
+  return (rv <= 1 && ch == 1 && dtype == COW_F32) ? static_cast<size_t>(kBanksPerCta) * reads * width * sizeof(float) : 0;
+}
+
+// Blocks of `fn` (with `smem` dynamic shared memory) that fit on the current
+// device at once, cached per device / kernel / size; raises the kernel's
+// dynamic shared memory limit when it needs more than the default 48 KiB.
+inline int resident_blocks(const void* fn, int threads, size_t smem) {
+  struct Entry {
+    int device;
+    const void* fn;
+    size_t smem;
+    int blocks;
+  };
+  static Entry cache[128];
+  static int used = 0;
+  static std::mutex mu;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].device == device && cache[i].fn == fn && cache[i].smem == smem) return cache[i].blocks;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int sms = 0, per_sm = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int blocks = sms * per_sm;
+  if (used < 128) cache[used++] = Entry{device, fn, smem, blocks};
+  return blocks;
+}
 
 }  // namespace

@@ -30,9 +30,13 @@ namespace {
 template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_decode_kernel(const __grid_constant__ DecodeLaunch P) {
-  __shared__ WarpMeta s_meta[kBanksPerCta];
-  __shared__ __align__(16) int32_t s_map[kBanksPerCta][kStageSlots];
+  // Common shapes (f32 rows, R <= 32, width <= 128) copy their read rows into
+  // shared memory (cp.async) rather than holding them in registers.
+  constexpr bool kStageReads = RC == 1 && CH == 1 && SDT == COW_F32;
+  __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta];
   __shared__ int s_tile;
+  // dynamic: [read rows, per warp R x D floats (kStageReads)] [map rows, per warp N ints (P.stage_map)]
+  extern __shared__ __align__(16) unsigned char dyn_smem[];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -57,7 +61,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const int64_t bank = static_cast<int64_t>(tile) * kBanksPerCta + warp;
   if (bank >= L.banks) return;
   const int64_t N = L.slots;
-  WarpMeta& sm = s_meta[warp];
+  auto& sm = s_meta[warp];
+  float* const s_reads = reinterpret_cast<float*>(dyn_smem) + static_cast<int64_t>(warp) * R * D;
+  int32_t* const s_mapw = reinterpret_cast<int32_t*>(dyn_smem + P.read_stage_bytes) + static_cast<int64_t>(warp) * N;
   uint64_t* const flags = P.flags + static_cast<int64_t>(L.tile_begin) * kBanksPerCta;
 
   // Round 1: everything that does not depend on the routes.  The epoch and
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   unsigned first_mask = 0;
   int route_bits = 0;
   const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
-                                                first_mask, route_bits, P.stage_map ? s_map[warp] : nullptr);
+                                                first_mask, route_bits, P.stage_map ? s_mapw : nullptr);
   const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
   const bool bad = bad_route || bad_tmpl;
   if (bad) {
@@ -98,13 +104,27 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         pack_flag(epoch, kFlagAggregate, static_cast<uint32_t>(count));
   }
 
-  // Row traffic: the write rows and the first read group are requested
-  // together, then the look-back runs while they are in flight.
+  // Row traffic: every read row (shared memory) or the first read group
+  // (registers) and the write rows are requested together; the prefix scan
+  // then runs while they are in flight.
   float4 upd[WMAX][CH];
-  float4 v0[ReadGroup<CH>::G][CH];
-  float wt0[ReadGroup<CH>::G];
+  float4 v0[kStageReads ? 1 : ReadGroup<CH>::G][CH];
+  float wt0[kStageReads ? 1 : ReadGroup<CH>::G];
   const int64_t m0_base = tmpl * N;
   if (!bad) {
+    if constexpr (kStageReads) {
+      if (lane * 4 < D) {
+        for (int r = 0; r < R; ++r) {
+          const int src = sm.rsrc[r];
+          if (src >= 0) {
+            cp_async16(s_reads + r * D + lane * 4,
+                       static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D + lane * 4);
+          } else if (src == -1) {
+            cp_async16(s_reads + r * D + lane * 4, L.m0 + (m0_base + sm.ridx[r]) * D + lane * 4);
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W) {
@@ -122,7 +142,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
+    if constexpr (!kStageReads) load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
   }
 
   // Exclusive prefix of first touches over the preceding banks of this pool
@@ -163,8 +183,18 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    accumulate_group<CH>(acc, v0, wt0);
-    read_remaining<SDT, CH>(acc, sm, R, L.slab, 0, L.m0, m0_base, lane, D);
+    if constexpr (kStageReads) {
+      // Each lane reads back only the 16-byte chunks it copied itself.
+      cp_async_wait_all();
+      if (lane * 4 < D) {
+        for (int r = 0; r < R; ++r) {
+          if (sm.rsrc[r] >= -1) acc[0] = f4_axpy(sm.rw[r], *reinterpret_cast<const float4*>(s_reads + r * D + lane * 4), acc[0]);
+        }
+      }
+    } else {
+      accumulate_group<CH>(acc, v0, wt0);
+      read_remaining<SDT, CH>(acc, sm, R, L.slab, 0, L.m0, m0_base, lane, D);
+    }
     add_forwarded<CH, WMAX>(acc, upd, sm, W);
   }
 #pragma unroll
@@ -256,28 +286,6 @@ namespace {
 // beyond it the kernel orders tiles by a ticket instead.
 constexpr int64_t kStageMaxBanks = 148 * 16;
 
-int resident_blocks(const void* fn, int threads) {
-  struct Entry {
-    int device;
-    const void* fn;
-    int blocks;
-  };
-  static Entry cache[64];
-  static int used = 0;
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return 0;
-  for (int i = 0; i < used; ++i)
-    if (cache[i].device == device && cache[i].fn == fn) return cache[i].blocks;
-  int sms = 0, per_sm = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  const int blocks = sms * per_sm;
-  if (used < 64) cache[used++] = Entry{device, fn, blocks};
-  return blocks;
-}
 
 }  // namespace
 
@@ -353,8 +361,8 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   P.total_tiles = tiles;
   void (*fn)(DecodeLaunch) = nullptr;
   const int ch = width_chunks(width);
-  COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, small_routes(writes, reads), fn);
-  P.dynamic_tiles = tiles > resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32) ? 1 : 0;
+  const int rv = route_variant(writes, reads);
+  COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, rv, fn);
   // Latency-bound launches (at most ~16 warps per SM) with small tables stage
   // each bank's map row in shared memory: N*4 extra bytes per bank buy one
   // dependent memory round trip less.
@@ -365,7 +373,14 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     total_banks += pools[l].banks;
   }
   P.stage_map = stage && total_banks <= kStageMaxBanks ? 1 : 0;
-  fn<<<tiles, kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
+  P.read_stage_bytes = static_cast<int32_t>(read_stage_bytes(reads, width, ch, rv, sdt));
+  int64_t max_slots = 0;
+  for (int l = 0; l < layers; ++l) max_slots = pools[l].slots > max_slots ? pools[l].slots : max_slots;
+  const size_t smem = P.read_stage_bytes + (P.stage_map ? kBanksPerCta * max_slots * sizeof(int32_t) : 0);
+  const int resident = resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32, smem);
+  if (resident <= 0) return COW_ERR_UNSUPPORTED;
+  P.dynamic_tiles = tiles > resident ? 1 : 0;
+  fn<<<tiles, kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
 }
 

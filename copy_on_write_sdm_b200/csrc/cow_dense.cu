@@ -22,7 +22,9 @@ struct DenseLaunch {
 template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_dense_kernel(const __grid_constant__ DenseLaunch P) {
-  __shared__ WarpMeta s_meta[kBanksPerCta];
+  constexpr bool kStageReads = RC == 1 && CH == 1 && SDT == COW_F32;
+  __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta];
+  extern __shared__ __align__(16) unsigned char dyn_smem[];  // read rows, per warp R x D floats
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t g = static_cast<int64_t>(blockIdx.x) * kBanksPerCta + warp;
@@ -33,7 +35,8 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const int64_t bank = g - L.bank_begin;
   const int D = P.width, W = P.writes, R = P.reads;
   const int64_t N = P.slots;
-  WarpMeta& sm = s_meta[warp];
+  auto& sm = s_meta[warp];
+  float* const s_reads = reinterpret_cast<float*>(dyn_smem) + static_cast<int64_t>(warp) * R * D;
   const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
   const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
   const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
@@ -70,9 +73,19 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    float4 v0[ReadGroup<CH>::G][CH];
-    float wt0[ReadGroup<CH>::G];
-    load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.memory, base, nullptr, 0, lane, D);
+    float4 v0[kStageReads ? 1 : ReadGroup<CH>::G][CH];
+    float wt0[kStageReads ? 1 : ReadGroup<CH>::G];
+    if constexpr (kStageReads) {
+      if (lane * 4 < D) {
+        for (int r = 0; r < R; ++r) {
+          const int src = sm.rsrc[r];
+          if (src >= 0)
+            cp_async16(s_reads + r * D + lane * 4, static_cast<const float*>(L.memory) + (base + src) * D + lane * 4);
+        }
+      }
+    } else {
+      load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.memory, base, nullptr, 0, lane, D);
+    }
     gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -85,8 +98,17 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
         }
       }
     }
-    accumulate_group<CH>(acc, v0, wt0);
-    read_remaining<SDT, CH>(acc, sm, R, L.memory, base, nullptr, 0, lane, D);
+    if constexpr (kStageReads) {
+      cp_async_wait_all();
+      if (lane * 4 < D) {
+        for (int r = 0; r < R; ++r) {
+          if (sm.rsrc[r] >= 0) acc[0] = f4_axpy(sm.rw[r], *reinterpret_cast<const float4*>(s_reads + r * D + lane * 4), acc[0]);
+        }
+      }
+    } else {
+      accumulate_group<CH>(acc, v0, wt0);
+      read_remaining<SDT, CH>(acc, sm, R, L.memory, base, nullptr, 0, lane, D);
+    }
     add_forwarded<CH, WMAX>(acc, upd, sm, W);
   }
 #pragma unroll
@@ -129,9 +151,12 @@ int cow_dense_step(void* const* memories, const int64_t* banks, const cow_step* 
   P.act_dt = act_dtype;
   void (*fn)(DenseLaunch) = nullptr;
   const int ch = width_chunks(width);
-  COW_SELECT_KERNEL(cow_dense_kernel, mem_dtype, ch, small_routes(writes, reads), fn);
+  const int rv = route_variant(writes, reads);
+  COW_SELECT_KERNEL(cow_dense_kernel, mem_dtype, ch, rv, fn);
+  const size_t smem = read_stage_bytes(reads, width, ch, rv, mem_dtype);
+  if (resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32, smem) <= 0) return COW_ERR_UNSUPPORTED;
   const int64_t blocks = (total + kBanksPerCta - 1) / kBanksPerCta;
-  fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
+  fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
 }
 

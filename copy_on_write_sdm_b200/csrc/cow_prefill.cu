@@ -22,14 +22,14 @@ struct PrefillLaunch {
 template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_prefill_kernel(const __grid_constant__ PrefillLaunch P) {
-  __shared__ WarpMeta s_meta[kBanksPerCta];
+  __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t bank = static_cast<int64_t>(blockIdx.x) * kBanksPerCta + warp;
   if (bank >= P.banks) return;
   const int D = P.width, W = P.writes, R = P.reads;
   const int64_t N = P.slots, T = P.time;
-  WarpMeta& sm = s_meta[warp];
+  auto& sm = s_meta[warp];
   const int64_t tmpl = P.templates[bank];
   if (tmpl < 0 || tmpl >= P.template_count) {
     if (lane == 0) atomicOr(P.status, COW_ST_TEMPLATE_RANGE);
@@ -135,7 +135,7 @@ int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t
   P.act_dt = act_dtype;
   void (*fn)(PrefillLaunch) = nullptr;
   const int ch = width_chunks(pool->width);
-  COW_SELECT_KERNEL(cow_prefill_kernel, pool->slab_dtype, ch, small_routes(writes, reads), fn);
+  COW_SELECT_KERNEL(cow_prefill_kernel, pool->slab_dtype, ch, route_variant(writes, reads), fn);
   const int64_t blocks = (pool->banks + kBanksPerCta - 1) / kBanksPerCta;
   fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
   return launch_status();
