@@ -13,9 +13,9 @@ Reported numbers (one JSON line from rank 0):
   CUDA graph of the one fused launch; L2 is flushed (a 256 MiB write) before
   every timed step and the step is timed alone with CUDA events on the
   launching stream, so the pool state starts cold in HBM.
-* ``e2e``: the same metric through the public Python API with host buffers:
-  every step copies its routes from pinned host memory, runs
-  ``packed_sdm_cow_step_layers`` (with the per-step capacity proof) and reads
+* ``e2e``: the same metric through the public runtime API with host buffers:
+  every step copies its packed routes from pinned host memory (one copy), runs
+  ``DecodeSession.step_host`` (capacity proof + one fused launch) and reads
   the readouts back to the host.
 * ``roofline``: algorithmic bytes per launch / mean launch time vs the
   measured HBM copy bandwidth.
@@ -304,27 +304,29 @@ def run_gpu(args, rank, world, device):
         dense_ms = sum(a.elapsed_time(b) for a, b in dev_ev)
         del mems
 
-    # End to end through the public API with host buffers.
-    host = {k: v[Wm:Wm + K].cpu().pin_memory() for k, v in inputs.items()}
-    dev_in = {k: torch.empty_like(v[0]) for k, v in inputs.items()}
-    host_out = torch.empty(LAYERS, banks, WIDTH, pin_memory=True)
-    dev_out = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
-    h2d = sum(v[0].numel() * v.element_size() for v in host.values())
-    d2h = host_out.numel() * host_out.element_size()
+    # End to end through the public runtime API with host buffers: every step
+    # copies its packed routes from pinned host memory (one copy), runs the
+    # capacity proof and the fused launch (DecodeSession), and reads the
+    # readouts back to pinned host memory (one copy).
+    from copy_on_write_sdm_b200 import DecodeSession
+
+    sess = DecodeSession(states, writes=WRITES, reads=READS)
+    host_steps = torch.empty(K, sess.step_bytes, dtype=torch.uint8, pin_memory=True)
+    for i, s in enumerate(range(Wm, Wm + K)):
+        for l in range(LAYERS):
+            for k, v in sess.views[l].items():
+                v.copy_(inputs[k][s, l])
+        host_steps[i].copy_(sess.inputs)
+    torch.cuda.synchronize(device)
+    h2d = sess.step_bytes
+    d2h = sess.host_outputs.numel() * sess.host_outputs.element_size()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(device)
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for s in range(K):
-            for k in dev_in:
-                dev_in[k].copy_(host[k][s], non_blocking=True)
-            for st in states:
-                st.prepare_step_capacity(banks * WRITES)
-            packed_sdm_cow_step_layers(states, [{k: v[l] for k, v in dev_in.items()} for l in range(LAYERS)],
-                                       outputs=dev_out)
-            for l in range(LAYERS):
-                host_out[l].copy_(dev_out[l], non_blocking=True)
+        for i in range(K):
+            sess.step_host(host_steps[i])
         e1.record(stream)
     torch.cuda.synchronize(device)
     barrier()
@@ -463,7 +465,7 @@ def main() -> int:
                      "algorithmic_bytes_per_launch": per_launch, "mean_launch_us": mean_launch_s * 1e6,
                      "kernel": "cow_decode_kernel<f32,1,8>"},
         "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
-                "d2h_bytes_per_step": res["d2h"], "path": "packed_sdm_cow_step_layers, pinned host buffers"},
+                "d2h_bytes_per_step": res["d2h"], "path": "DecodeSession.step_host: one pinned H2D copy, capacity proof + one fused launch, one D2H copy per step"},
         "gpu_launches": K,
         "clocks": res["clocks"],
         "cpu_baseline": cpu,

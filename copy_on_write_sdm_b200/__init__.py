@@ -15,8 +15,10 @@ from .allocator import (
     packed_sdm_cow_step,
     packed_sdm_cow_step_layers,
 )
+from .session import DecodeSession
 
 __all__ = [
+    "DecodeSession",
     "PackedSDMCopyOnWriteState",
     "SDMCopyOnWriteStep",
     "dense_sdm_sparse_step",

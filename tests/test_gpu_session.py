@@ -1,0 +1,56 @@
+"""DecodeSession (packed buffers, one launch per step) against the per-call API."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cow_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda:0")
+
+
+def _pools(dev, layers, banks, slots, width, quantum, seed):
+    from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState
+
+    g = torch.Generator().manual_seed(seed)
+    return [PackedSDMCopyOnWriteState.allocate((0.02 * torch.randn(1, slots, width, generator=g)).to(dev),
+                                               banks=banks, capacity_rows=quantum, growth_quantum_rows=quantum)
+            for _ in range(layers)]
+
+
+def test_session_matches_per_call_api_through_growth(dev):
+    from copy_on_write_sdm_b200 import DecodeSession, packed_sdm_cow_step_layers
+
+    layers, banks, slots, width, W, R = 3, 32, 128, 128, 4, 16
+    quantum = O.growth_quantum_rows(banks, W, 2)
+    ref = _pools(dev, layers, banks, slots, width, quantum, 1)
+    new = _pools(dev, layers, banks, slots, width, quantum, 1)
+    sess = DecodeSession(new, writes=W, reads=R)
+    rng = np.random.default_rng(4)
+    for step in range(12):  # grows several times: pool descriptors are rebuilt
+        xs = [O.synthetic_step_inputs(rng, banks, slots, width, W, R) for _ in range(layers)]
+        for l, x in enumerate(xs):
+            for k, v in x.items():
+                sess.host_views[l][k].copy_(torch.from_numpy(v))
+        sess.step_host()
+        torch.cuda.synchronize(dev)  # the readouts reach host memory asynchronously
+        got = sess.host_outputs.clone()
+        for p in ref:
+            p.prepare_step_capacity(banks * W)
+        want = packed_sdm_cow_step_layers(ref, [{k: torch.from_numpy(v).to(dev) for k, v in x.items()} for x in xs])
+        torch.cuda.synchronize(dev)
+        for l in range(layers):
+            np.testing.assert_allclose(got[l].numpy(), want[l].cpu().numpy(), atol=1e-5, rtol=1e-5)
+    for p, q in zip(ref, new):
+        assert torch.equal(p.logical_to_physical, q.logical_to_physical)
+        assert p.capacity_rows == q.capacity_rows and p.growth_events == q.growth_events > 0
+        q.validate_invariants()
