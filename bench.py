@@ -346,6 +346,198 @@ def run_gpu(args, rank, world, device):
 
 
 # --------------------------------------------------------------------------
+# configuration 4: large-address-space scale-out (--workload scaleout)
+# --------------------------------------------------------------------------
+
+SO_SLOTS, SO_HEADS, SO_REQUESTS, SO_PREFIX, SO_ZIPF = 65536, 8, 1024, 4096, 1.1
+
+
+class ZipfRoutes:
+    """Zipf(s) popularity over a seeded permutation of the N addresses."""
+
+    def __init__(self, n: int, s: float, gen: torch.Generator, device):
+        ranks = torch.arange(1, n + 1, device=device, dtype=torch.float64)
+        p = ranks.pow(-s)
+        p /= p.sum()
+        self.n = n
+        self.cdf = torch.cumsum(p, 0).float()
+        self.logp = p.log().float()
+        self.perm = torch.randperm(n, generator=gen, device=device)
+
+    def with_replacement(self, shape, gen) -> torch.Tensor:
+        u = torch.rand(*shape, generator=gen, device=self.cdf.device)
+        return self.perm[torch.searchsorted(self.cdf, u).clamp_(max=self.n - 1)]
+
+    def distinct(self, rows: int, k: int, gen, chunk: int = 2048) -> torch.Tensor:
+        """``k`` distinct addresses per row, without replacement (Gumbel top-k)."""
+        out = []
+        for r0 in range(0, rows, chunk):
+            r = min(chunk, rows - r0)
+            g = torch.rand(r, self.n, generator=gen, device=self.cdf.device).clamp_(min=1e-20)
+            g.log_().neg_().log_().neg_().add_(self.logp)
+            out.append(self.perm[g.topk(k, dim=-1).indices])
+            del g
+        return torch.cat(out)
+
+
+def scaleout_pool(gen, requests: int, prefix: int, extra_rows: int, device):
+    """Post-prefix pool of one configuration-4 layer.
+
+    The written-address union of ``prefix`` Zipf-routed tokens (W=4 writes each)
+    is marked and packed in ``nonzero()`` order exactly as the prefill handoff
+    does; the touched rows hold M0 instead of the recurrence's values (the
+    4,096-token recurrence over 8,192 banks would dominate the run and its
+    inputs alone are ~17 GB per layer).  Decode traffic does not depend on row
+    contents.  Capacity: the touched rows + ``extra_rows`` (proven, no growth).
+    """
+    from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState, _lib
+
+    lib = _lib.load()
+    banks = requests * SO_HEADS
+    zipf = ZipfRoutes(SO_SLOTS, SO_ZIPF, gen, device)
+    m0 = 0.02 * torch.randn(SO_HEADS, SO_SLOTS, WIDTH, generator=gen, device=device)
+    mapping = torch.full((banks, SO_SLOTS), -1, dtype=torch.int32, device=device)
+    status = torch.zeros((), dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    chunk = 256
+    for t0 in range(0, prefix, chunk):
+        t = min(chunk, prefix - t0)
+        widx = zipf.with_replacement((banks, t, WRITES), gen)
+        _lib.check(lib.cow_prefill_mark(widx.data_ptr(), _lib.I64, banks, t, WRITES, SO_SLOTS, mapping.data_ptr(),
+                                        status.data_ptr(), stream), "cow_prefill_mark")
+        del widx
+    touched = int((mapping >= 0).sum())
+    templates = torch.arange(SO_HEADS, device=device, dtype=torch.int64).repeat(requests)
+    st = PackedSDMCopyOnWriteState._pack_layout(
+        m0, mapping, templates, capacity_rows=touched + extra_rows, state_dtype=torch.float32,
+        maximum_future_allocations=extra_rows, growth_quantum_rows=0, row_source=("m0", None), validate=False)
+    return st, zipf, touched
+
+
+def run_gpu_scaleout(args, rank, world, device):
+    from copy_on_write_sdm_b200 import _lib, allocator
+
+    lib = _lib.load()
+    requests = args.requests // world
+    banks = requests * SO_HEADS
+    K, Wm = args.steps, args.warmup
+    gen = torch.Generator(device=device).manual_seed(4000 + rank)
+    t0 = time.time()
+    states, zipfs, touched = [], [], []
+    for _ in range(LAYERS):
+        st, z, a = scaleout_pool(gen, requests, args.prefix, banks * WRITES * (K + Wm), device)
+        states.append(st)
+        zipfs.append(z)
+        touched.append(a)
+    steps = []
+    for s in range(K + Wm):
+        per = []
+        for l in range(LAYERS):
+            z = zipfs[l]
+            per.append(dict(
+                write_indices=z.distinct(banks, WRITES, gen), read_indices=z.distinct(banks, READS, gen),
+                write_weights=torch.softmax(torch.randn(banks, WRITES, generator=gen, device=device), -1),
+                read_weights=torch.softmax(torch.randn(banks, READS, generator=gen, device=device), -1),
+                values=torch.randn(banks, WIDTH, generator=gen, device=device),
+                input_gate=torch.rand(banks, generator=gen, device=device),
+                forget_log_gate=-torch.rand(banks, generator=gen, device=device)))
+        steps.append(per)
+    torch.cuda.synchronize(device)
+    setup_s = time.time() - t0
+    outputs = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
+    scratch = allocator.decode_scratch(device, banks * LAYERS, LAYERS)
+    pools = (_lib.CowPool * LAYERS)(*[st._pool() for st in states])
+
+    def cstep(x, out):
+        return _lib.CowStep(x["write_indices"].data_ptr(), x["write_weights"].data_ptr(), x["values"].data_ptr(),
+                            x["input_gate"].data_ptr(), x["input_gate"].data_ptr(), x["forget_log_gate"].data_ptr(),
+                            x["read_indices"].data_ptr(), x["read_weights"].data_ptr(), out.data_ptr(), None)
+
+    c_steps = [(_lib.CowStep * LAYERS)(*[cstep(steps[s][l], outputs[l]) for l in range(LAYERS)]) for s in range(K + Wm)]
+    stream = torch.cuda.Stream(device)
+
+    def launch(s):
+        _lib.check(lib.cow_decode_step(pools, c_steps[s], LAYERS, WRITES, READS, _lib.I64, _lib.F32,
+                                       scratch.data_ptr(), scratch.numel(), stream.cuda_stream), "cow_decode_step")
+
+    with torch.cuda.stream(stream):
+        for s in range(Wm):
+            launch(s)
+    torch.cuda.synchronize(device)
+    free_before = sum(int(st.free_count) for st in states)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    with ClockSampler(device.index) as clocks:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        with torch.cuda.stream(stream):
+            for i in range(K):
+                ev[i][0].record(stream)
+                launch(Wm + i)
+                ev[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    first = free_before - sum(int(st.free_count) for st in states)
+    for st in states:
+        st.validate_invariants()
+    state_bytes = {}
+    for st in states:
+        for k, v in st.storage_bytes().items():
+            state_bytes[k] = state_bytes.get(k, 0) + v
+    return dict(total_ms=sum(step_ms), step_ms=step_ms, first_touches=first, clocks=clocks.summary(),
+                setup_s=setup_s, state_bytes=state_bytes, requests=requests, banks=banks,
+                mean_touched_rows_per_bank=sum(touched) / (LAYERS * banks))
+
+
+def cpu_scaleout_rate(seconds: float, requests: int, prefix: int) -> dict:
+    """Oracle packed step on 8 requests (64 banks) of one configuration-4 layer,
+    extrapolated to ``requests`` x 7 layers per decode step (bank-steps are
+    independent, so CPU time scales with their number)."""
+    from oracle import cow_oracle as O
+
+    rng = np.random.default_rng(11)
+    sample_req = 8
+    banks = sample_req * SO_HEADS
+    ranks = np.arange(1, SO_SLOTS + 1, dtype=np.float64)
+    p = ranks ** -SO_ZIPF
+    p /= p.sum()
+    cdf = np.cumsum(p)
+    perm = rng.permutation(SO_SLOTS)
+    touched = np.zeros((banks, SO_SLOTS), bool)
+    for b in range(banks):
+        touched[b, perm[np.minimum(np.searchsorted(cdf, rng.random(prefix * WRITES)), SO_SLOTS - 1)]] = True
+    m0 = (0.02 * rng.standard_normal((SO_HEADS, SO_SLOTS, WIDTH))).astype(np.float32)
+    st = O.allocate(m0, banks=banks, capacity_rows=int(touched.sum()) + banks * WRITES * 64,
+                    template_indices=np.tile(np.arange(SO_HEADS), sample_req))
+    bank, slot = np.nonzero(touched)
+    st.logical_to_physical[bank, slot] = np.arange(bank.size, dtype=np.int32)
+    cap = st.capacity_rows
+    st.free_rows[: cap - bank.size] = np.arange(bank.size, cap, dtype=np.int32)
+    st.free_count = cap - bank.size
+
+    def draw(k):
+        keys = np.log(p)[None, :] - np.log(-np.log(rng.random((banks, SO_SLOTS))))
+        return perm[np.argpartition(-keys, k, axis=1)[:, :k]]
+
+    xs = []
+    for _ in range(4):
+        x = O.synthetic_step_inputs(rng, banks, 16, WIDTH, WRITES, READS)
+        x["write_indices"], x["read_indices"] = draw(WRITES), draw(READS)
+        xs.append(x)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        O.packed_step(st, **xs[n % len(xs)])
+        n += 1
+    per_bank_step = (time.perf_counter() - t0) / (n * banks)
+    step_s = per_bank_step * requests * SO_HEADS * LAYERS
+    return {"value": requests / step_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} oracle steps of {banks} banks (8 requests x 8 heads, N=65536, Zipf 1.1, prefix {prefix}) "
+                      f"on one layer, extrapolated to {requests} requests x {LAYERS} layers per decode step"}
+
+
+# --------------------------------------------------------------------------
 # CPU arms (the reference's algorithm, restated in oracle/)
 # --------------------------------------------------------------------------
 
@@ -406,6 +598,10 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="screen", choices=["screen", "scaleout"],
+                    help="screen: configuration 3 (default, the headline); scaleout: configuration 4")
+    ap.add_argument("--requests", type=int, default=SO_REQUESTS, help="scaleout: requests over all GPUs")
+    ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -433,6 +629,8 @@ def main() -> int:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     torch.backends.cuda.matmul.allow_tf32 = False
+    if args.workload == "scaleout":
+        return main_scaleout(args, rank, world, device)
     res = run_gpu(args, rank, world, device)
 
     from copy_on_write_sdm_b200.sharding import reduce_over_ranks
@@ -482,6 +680,46 @@ def main() -> int:
         "retained_state": {"allocated_rows": res["allocated_rows"], "capacity_rows": res["capacity_rows"],
                            "live_value_bytes": res["live_value_bytes"], **res["state_bytes"]},
         "first_touches_in_timed_steps": res["first_touches"],
+        "setup_s": res["setup_s"],
+    }
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main_scaleout(args, rank, world, device) -> int:
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    res = run_gpu_scaleout(args, rank, world, device)
+    (total_ms,) = reduce_over_ranks([res["total_ms"]], op="max", device=device)
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return 0
+    K = args.steps
+    tokens = res["requests"] * world * K
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = (json.load(open(peaks_path))["hbm_gbs"], "measured") if os.path.exists(peaks_path) else (6650.0, "fallback")
+    per_launch = algorithmic_bytes(res["banks"] * LAYERS, res["first_touches"] // max(K, 1))
+    mean_s = res["total_ms"] / K / 1e3
+    achieved = per_launch / mean_s / 1e9
+    line = {
+        "metric": METRIC, "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 4 large-address-space scale-out: 7 SDM pools, N=65536, D=128, H=8, "
+                               "top-16/top-4, Zipf(1.1) routes over a seeded address permutation",
+                   "global_batch": args.requests, "requests_per_gpu": res["requests"], "prefix": args.prefix,
+                   "parallelism": f"requests sharded over {world} GPU(s), no collective",
+                   "prefix_state": "written-address union of the Zipf prefix packed in nonzero() order, rows from M0",
+                   "l2": "pool state (>100 GB at 1 GPU) far exceeds L2; steps timed back to back"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_src, "algorithmic_bytes_per_launch": per_launch,
+                     "mean_launch_us": mean_s * 1e6, "kernel": "cow_decode_kernel<f32,1,4,1>"},
+        "e2e": None, "gpu_launches": K, "clocks": res["clocks"],
+        "cpu_baseline": cpu_scaleout_rate(args.cpu_seconds, res["requests"] * world, args.prefix),
+        "mean_touched_rows_per_bank": res["mean_touched_rows_per_bank"],
+        "first_touches_in_timed_steps": res["first_touches"], "retained_state": res["state_bytes"],
         "setup_s": res["setup_s"],
     }
     print(json.dumps(line))
