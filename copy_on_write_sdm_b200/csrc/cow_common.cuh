@@ -159,6 +159,7 @@ struct DecodeLayer {
   cow_step step;
   int64_t banks, slots, capacity, template_count, group_begin;
   int32_t tile_begin, tiles;
+  int32_t count_block_begin, count_blocks;  // two-pass launches: blocks of cow_count_kernel
 };
 
 struct DecodeLaunch {
@@ -167,6 +168,7 @@ struct DecodeLaunch {
   uint64_t* flags;        // one per bank slot, pool-major (tile_begin * 4 + bank)
   uint64_t* group_flags;  // one per group of kScanGroup banks, pool-major (group_begin + group)
   int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, read_stage_bytes;
+  int32_t two_pass, _pad;
 };
 
 constexpr uint32_t kFlagAggregate = 1u;
@@ -237,6 +239,35 @@ __device__ __forceinline__ int sum_flags(const uint64_t* f, int64_t lo, int64_t 
     total += warp_sum(part);
   }
   return total;
+}
+
+// Block-wide exclusive prefix sum of one int per thread (kThreads threads,
+// multiple of 32, at most 1024); `total` receives the block sum.
+template <int kThreads>
+__device__ __forceinline__ int block_exclusive_scan_n(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kThreads / 32 ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kThreads / 32) s_warp[lane] = w;
+  }
+  __syncthreads();
+  total = s_warp[kThreads / 32 - 1];
+  const int before = warp > 0 ? s_warp[warp - 1] : 0;
+  __syncthreads();
+  return before + x - v;
 }
 
 // Exclusive prefix for `bank` (warp-uniform result).  `bank_flags` / `group_flags`

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const DecodeLayer& L = P.layer[l];
   uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
   int tile;
-  if (P.dynamic_tiles) {
+  if (P.dynamic_tiles && !P.two_pass) {
     // More blocks than can be resident at once: a ticket orders the tiles by
     // start time, so a warp only ever waits on warps that are running.
     if (threadIdx.x == 0) s_tile = static_cast<int>(atomicAdd(&hdr[0], 1u));
@@ -71,10 +71,17 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   // last bank rewrites them only after every bank has published, so all
   // banks see the launch's starting values.
   uint32_t epoch = 0;
-  int old_free = 0;
+  int old_free = 0, excl_given = 0;
   if (lane == 0) {
-    epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
-    old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
+    if (P.two_pass) {
+      // cow_count_kernel already produced this bank's prefix and the pool's
+      // starting free count: plain inputs, no waiting.
+      excl_given = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(L.tile_begin) * kBanksPerCta + bank];
+      old_free = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(P.total_tiles) * kBanksPerCta + l];
+    } else {
+      epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
+      old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
+    }
   }
   const int64_t tmpl = L.templates[bank];
   const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
@@ -99,7 +106,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   epoch = __shfl_sync(kFull, epoch, 0);
   old_free = __shfl_sync(kFull, old_free, 0);
   const int count = __popc(first_mask);
-  if (lane == 0) {
+  if (lane == 0 && !P.two_pass) {
     *reinterpret_cast<volatile uint64_t*>(flags + bank) =
         pack_flag(epoch, kFlagAggregate, static_cast<uint32_t>(count));
   }
@@ -147,20 +154,25 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 
   // Exclusive prefix of first touches over the preceding banks of this pool
   // (two-level scan, about one round trip), overlapped with the row loads above.
-  bool timed_out = false;
-  const int excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
-  if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
-  if (lane == 0) {
-    const int inclusive = excl + count;
-    if (bank == L.banks - 1) {
-      // Every bank of this pool has published, hence has read the starting
-      // epoch and free count: close the launch for this pool.
-      if (inclusive > 0) {
-        const int remaining = old_free - inclusive;
-        *L.free_count = remaining > 0 ? remaining : 0;
+  int excl;
+  if (P.two_pass) {
+    excl = __shfl_sync(kFull, excl_given, 0);
+  } else {
+    bool timed_out = false;
+    excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
+    if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+    if (lane == 0) {
+      const int inclusive = excl + count;
+      if (bank == L.banks - 1) {
+        // Every bank of this pool has published, hence has read the starting
+        // epoch and free count: close the launch for this pool.
+        if (inclusive > 0) {
+          const int remaining = old_free - inclusive;
+          *L.free_count = remaining > 0 ? remaining : 0;
+        }
+        if (P.dynamic_tiles) hdr[0] = 0u;
+        *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
       }
-      if (P.dynamic_tiles) hdr[0] = 0u;
-      *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
     }
   }
 
@@ -234,6 +246,91 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   }
 }
 
+// --------------------------------------------------------------------------
+// first-touch prefix pass for large launches
+// --------------------------------------------------------------------------
+//
+// With thousands of banks per pool, warps of the fused kernel would wait on one
+// another's first-touch counts with their rows already loaded.  Large launches
+// therefore compute every bank's exclusive prefix first: one thread per bank
+// reads only its route indices and W map entries (same validity rules as the
+// decode kernel: an out-of-range index, a repeated write address or a bad
+// template makes the bank allocate nothing), a block scan covers 256 banks, and
+// each block adds the aggregates of the pool's earlier blocks.  Results: the
+// prefix of every bank slot and the pool's starting free count (in the scan
+// flag region, read as int32), and the pool's new free count.
+
+constexpr int kCountThreads = 256;
+
+__global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_constant__ DecodeLaunch P) {
+  __shared__ int s_warp[kCountThreads / 32];
+  __shared__ int s_blk, s_base;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_old;
+  const int tid = threadIdx.x, lane = tid & 31;
+  int l = 0;
+  while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l].count_block_begin + P.layer[l].count_blocks) ++l;
+  const DecodeLayer& L = P.layer[l];
+  uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
+  if (tid == 0) {
+    s_blk = P.dynamic_tiles ? static_cast<int>(atomicAdd(&hdr[0], 1u))
+                            : static_cast<int>(blockIdx.x) - L.count_block_begin;
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
+    s_old = *reinterpret_cast<volatile int32_t*>(L.free_count);
+  }
+  __syncthreads();
+  const int blk = s_blk;
+  const uint32_t epoch = s_epoch;
+  const int64_t bank = static_cast<int64_t>(blk) * kCountThreads + tid;
+  const int64_t N = L.slots;
+  const int W = P.writes, R = P.reads;
+  int count = 0;
+  if (bank < L.banks) {
+    const cow_step& st = L.step;
+    int wi[COW_MAX_WRITES];
+    bool bad = false;
+    for (int w = 0; w < W; ++w) {
+      const int64_t raw = ld_index(st.write_indices, bank * W + w, P.idx64);
+      const bool ok = raw >= 0 && raw < N;
+      wi[w] = ok ? static_cast<int>(raw) : -1 - w;
+      bad |= !ok;
+    }
+    for (int a = 1; a < W; ++a)
+      for (int b = 0; b < a; ++b) bad |= wi[a] == wi[b];
+    for (int r = 0; r < R; ++r) {
+      const int64_t raw = ld_index(st.read_indices, bank * R + r, P.idx64);
+      bad |= raw < 0 || raw >= N;
+    }
+    const int64_t tmpl = L.templates[bank];
+    bad |= tmpl < 0 || tmpl >= L.template_count;
+    if (!bad)
+      for (int w = 0; w < W; ++w) count += L.map[bank * N + wi[w]] < 0 ? 1 : 0;
+  }
+  int total;
+  const int local = block_exclusive_scan_n<kCountThreads>(count, s_warp, total);
+  uint64_t* const bflags = P.group_flags + L.group_begin;  // one aggregate per count block
+  if (tid == 0) *reinterpret_cast<volatile uint64_t*>(bflags + blk) = pack_flag(epoch, kFlagAggregate, total);
+  if (tid < 32) {
+    bool timed_out = false;
+    const int base = sum_flags(bflags, 0, blk, epoch, lane, timed_out);
+    if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+    if (lane == 0) s_base = base;
+  }
+  __syncthreads();
+  int32_t* const excl = reinterpret_cast<int32_t*>(P.flags);
+  if (bank < L.banks) excl[static_cast<int64_t>(L.tile_begin) * kBanksPerCta + bank] = s_base + local;
+  if (tid == 0 && blk == L.count_blocks - 1) {
+    // Every block of this pool has published, hence has read the starting
+    // epoch and free count: record it for the decode pass and close the pool.
+    const int inclusive = s_base + total;
+    excl[static_cast<int64_t>(P.total_tiles) * kBanksPerCta + l] = s_old;
+    const int remaining = s_old - inclusive;
+    *L.free_count = remaining > 0 ? remaining : 0;
+    if (P.dynamic_tiles) hdr[0] = 0u;
+    *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+  }
+}
+
 }  // namespace
 
 namespace cowrt {
@@ -285,6 +382,9 @@ namespace {
 // and kernel).  A launch within this bound runs its tiles in block order;
 // beyond it the kernel orders tiles by a ticket instead.
 constexpr int64_t kStageMaxBanks = 148 * 16;
+// Launches with at least this many banks compute the first-touch prefix in a
+// separate pass (cow_count_kernel) before the decode pass.
+constexpr int64_t kTwoPassMinBanks = 12288;
 
 
 }  // namespace
@@ -379,7 +479,24 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   const size_t smem = P.read_stage_bytes + (P.stage_map ? kBanksPerCta * max_slots * sizeof(int32_t) : 0);
   const int resident = resident_blocks(reinterpret_cast<const void*>(fn), kBanksPerCta * 32, smem);
   if (resident <= 0) return COW_ERR_UNSUPPORTED;
-  P.dynamic_tiles = tiles > resident ? 1 : 0;
+  if (total_banks >= kTwoPassMinBanks) {
+    // Large launch: prefix pass first, then the decode pass with no waits.
+    int32_t blocks = 0;
+    for (int l = 0; l < layers; ++l) {
+      P.layer[l].count_block_begin = blocks;
+      P.layer[l].count_blocks = static_cast<int32_t>((pools[l].banks + kCountThreads - 1) / kCountThreads);
+      blocks += P.layer[l].count_blocks;
+    }
+    const int count_resident = resident_blocks(reinterpret_cast<const void*>(cow_count_kernel), kCountThreads, 0);
+    if (count_resident <= 0) return COW_ERR_UNSUPPORTED;
+    P.dynamic_tiles = blocks > count_resident ? 1 : 0;
+    cow_count_kernel<<<blocks, kCountThreads, 0, as_stream(stream)>>>(P);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+    P.two_pass = 1;
+    P.dynamic_tiles = 0;
+  } else {
+    P.dynamic_tiles = tiles > resident ? 1 : 0;
+  }
   fn<<<tiles, kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
 }

@@ -237,3 +237,30 @@ def test_errors_are_reported_not_trapped(dev):
     with pytest.raises(ValueError, match="CPU fallback|sm_100a"):
         packed_sdm_cow_step(st, **step_args([[0, 1], [2, 3]], [[0], [1]]), backend="torch")
 
+
+
+def test_two_pass_launch_reports_bad_bank_and_keeps_others_exact(dev):
+    """A large launch (prefix pass + decode pass): one bank repeats a write address.
+
+    The bad bank allocates nothing and the step reports it; every other bank's
+    placement is exactly the oracle's with that bank contributing no first touches.
+    """
+    from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState, packed_sdm_cow_step
+
+    rng = np.random.default_rng(21)
+    banks, slots, width, W, R = 16384, 64, 128, 4, 16
+    m0 = (0.02 * rng.standard_normal((1, slots, width))).astype(np.float32)
+    st = PackedSDMCopyOnWriteState.allocate(cu(m0, dev), banks=banks, capacity_rows=banks * slots)
+    x = O.synthetic_step_inputs(rng, banks, slots, width, W, R)
+    x["write_indices"][1000, 1] = x["write_indices"][1000, 0]
+    with pytest.raises(ValueError, match="write one logical slot twice"):
+        packed_sdm_cow_step(st, **{k: cu(v, dev) for k, v in x.items()})
+    # oracle: the same step with bank 1000 writing slots that are already private
+    ref = O.allocate(m0, banks=banks, capacity_rows=banks * slots)
+    ok = {k: v.copy() for k, v in x.items()}
+    ok["write_indices"][1000] = np.arange(W)
+    ref.logical_to_physical[1000, :W] = 0  # pretend private: no first touches for bank 1000
+    O.packed_step(ref, **ok)
+    ref.logical_to_physical[1000] = -1
+    np.testing.assert_array_equal(st.logical_to_physical.cpu().numpy(), ref.logical_to_physical)
+    assert int(st.free_count) == ref.free_count
