@@ -255,12 +255,12 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 // therefore compute every bank's exclusive prefix first: one thread per bank
 // reads only its route indices and W map entries (same validity rules as the
 // decode kernel: an out-of-range index, a repeated write address or a bad
-// template makes the bank allocate nothing), a block scan covers 256 banks, and
+// template makes the bank allocate nothing), a block scan covers 128 banks, and
 // each block adds the aggregates of the pool's earlier blocks.  Results: the
 // prefix of every bank slot and the pool's starting free count (in the scan
 // flag region, read as int32), and the pool's new free count.
 
-constexpr int kCountThreads = 256;
+constexpr int kCountThreads = kScanGroup;  // one count block per 128-bank scan group (reuses its flag)
 
 __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_constant__ DecodeLaunch P) {
   __shared__ int s_warp[kCountThreads / 32];
