@@ -538,6 +538,218 @@ def cpu_scaleout_rate(seconds: float, requests: int, prefix: int) -> dict:
 
 
 # --------------------------------------------------------------------------
+# Configuration 5: continuous-batching churn
+# --------------------------------------------------------------------------
+
+CH_SLOTS, CH_HEADS, CH_LIVE, CH_ARRIVALS = 4096, 4, 256, 8.0
+CH_MIN_LEN, CH_MAX_LEN, CH_PROMPT, CH_WARM_PREFIX = 64, 4096, 64, 1024
+
+
+def affine_routes(gen, lead: tuple, k: int, n: int, device) -> torch.Tensor:
+    """``k`` distinct uniform addresses per row: ``(base + stride*j) mod n`` with a
+    uniform base and a uniform odd stride (``n`` is a power of two, so the k
+    addresses are distinct and each is marginally uniform over ``[0, n)``)."""
+    base = torch.randint(0, n, lead + (1,), generator=gen, device=device)
+    stride = 2 * torch.randint(0, n // 2, lead + (1,), generator=gen, device=device) + 1
+    return (base + stride * torch.arange(k, device=device)) % n
+
+
+def churn_prompts(gen, requests: int, tokens: int, device) -> list[dict]:
+    """Seeded prompt routes, values and gates of ``requests`` requests, one dict per layer."""
+    banks = requests * CH_HEADS
+    return [dict(
+        write_indices=affine_routes(gen, (banks, tokens), WRITES, CH_SLOTS, device),
+        write_weights=torch.softmax(torch.randn(banks, tokens, WRITES, generator=gen, device=device), -1),
+        values=torch.randn(banks, tokens, WIDTH, generator=gen, device=device),
+        input_gate=torch.rand(banks, tokens, generator=gen, device=device),
+        forget_log_gate=-torch.rand(banks, tokens, generator=gen, device=device),
+        read_indices=affine_routes(gen, (banks, tokens), READS, CH_SLOTS, device),
+        read_weights=torch.softmax(torch.randn(banks, tokens, READS, generator=gen, device=device), -1))
+        for _ in range(LAYERS)]
+
+
+def churn_prefill(m0s, prompts: list[dict], first: int, requests: int, quantum: int):
+    """Prefilled cohort of requests ``first .. first+requests-1`` of ``prompts`` (all
+    layers in one sparse-prefill call), as ``FaithfulSDMDecodeState``."""
+    from copy_on_write_sdm_b200.allocator import from_prefix_routes_layers
+    from copy_on_write_sdm_b200.inference import FaithfulSDMDecodeState
+
+    lo, hi = first * CH_HEADS, (first + requests) * CH_HEADS
+    device = m0s[0].device
+    templates = torch.arange(CH_HEADS, device=device, dtype=torch.int64).repeat(requests)
+    states, _ = from_prefix_routes_layers(m0s, [{k: v[lo:hi] for k, v in x.items()} for x in prompts],
+                                          template_indices=templates, growth_quantum_rows=quantum)
+    tokens = prompts[0]["values"].shape[1]
+    return FaithfulSDMDecodeState(
+        layout="B" * LAYERS, position=tokens, capacity=0, activation_dtype=torch.float32,
+        active_sequences=torch.ones(requests, dtype=torch.bool, device=device),
+        sdm_layer_positions=tuple(range(LAYERS)), sdm_states=tuple(states), dense_keys=(), dense_values=())
+
+
+def run_gpu_churn(args, rank, world, device):
+    """Continuous batching over 256 live slots per GPU.
+
+    Every step: requests whose decode length ran out are released and the
+    batch compacted (``release_and_compact``), a cohort of the same size is
+    prefilled (64-token prompts, sparse prefill) and admitted (``admit``),
+    the slab is trimmed every ``--trim-every`` steps if asked, each pool's
+    capacity proof is renewed (``prepare_step_capacity``, growing by whole
+    quanta), and one fused decode launch covers the 7 pools.  Arrivals are
+    Poisson(8) per step into a FIFO queue; with mean length 2,080 tokens the
+    queue never drains, so the batch stays full and admissions equal
+    completions.  The initial batch starts from a 1,024-token prefix (about
+    2,600 private rows per bank, near the steady-state mean) with residual
+    lengths drawn uniformly below each request's length.
+    """
+    from copy_on_write_sdm_b200 import allocator
+
+    rng = np.random.default_rng(5000 + rank)
+    gen = torch.Generator(device=device).manual_seed(5000 + rank)
+    live = CH_LIVE
+    banks = live * CH_HEADS
+    quantum = max(16, banks * WRITES * args.quantum_steps)
+    K, Wm = args.steps, args.warmup
+    t0 = time.time()
+    m0s = [0.02 * torch.randn(CH_HEADS, CH_SLOTS, WIDTH, generator=gen, device=device) for _ in range(LAYERS)]
+    state = churn_prefill(m0s, churn_prompts(gen, live, args.churn_warm_prefix, device), 0, live, quantum)
+    ring_requests = 64
+    prompts = churn_prompts(gen, ring_requests, CH_PROMPT, device)
+    next_prompt = 0
+    lengths = rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=live)
+    remaining = np.array([rng.integers(1, n + 1) for n in lengths])
+    ring = []
+    for _ in range(16):
+        ring.append([dict(
+            write_indices=affine_routes(gen, (banks,), WRITES, CH_SLOTS, device),
+            read_indices=affine_routes(gen, (banks,), READS, CH_SLOTS, device),
+            write_weights=torch.softmax(torch.randn(banks, WRITES, generator=gen, device=device), -1),
+            read_weights=torch.softmax(torch.randn(banks, READS, generator=gen, device=device), -1),
+            values=torch.randn(banks, WIDTH, generator=gen, device=device),
+            input_gate=torch.rand(banks, generator=gen, device=device),
+            forget_log_gate=-torch.rand(banks, generator=gen, device=device)) for _ in range(LAYERS)])
+    outputs = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
+    scratch = allocator.decode_scratch(device, banks * LAYERS, LAYERS)
+    torch.cuda.synchronize(device)
+    setup_s = time.time() - t0
+    stats = dict(completions=0, released_rows=0, trimmed_rows=0, queue=0)
+    admitted_rows = []  # device counts, read after the timed region
+    stream = torch.cuda.current_stream(device)
+
+    def one_step(s, timed, ev):
+        nonlocal remaining, next_prompt
+        if timed:
+            ev[0].record(stream)
+        stats["queue"] += int(rng.poisson(CH_ARRIVALS))
+        done = np.nonzero(remaining == 0)[0]
+        if done.size:
+            stats["completions"] += done.size
+            stats["queue"] -= done.size
+            stats["released_rows"] += state.release_and_compact(done.tolist())
+            if next_prompt + done.size > ring_requests:
+                next_prompt = 0
+            cohort = churn_prefill(m0s, prompts, next_prompt, int(done.size), quantum)
+            next_prompt += int(done.size)
+            admitted_rows.append(torch.stack([st.allocated_rows_tensor() for st in cohort.sdm_states]).sum())
+            state.admit(cohort)
+            remaining = np.concatenate([remaining[remaining > 0],
+                                        rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=done.size)])
+        if args.trim_every and s % args.trim_every == args.trim_every - 1:
+            stats["trimmed_rows"] += state.trim_sdm_pools(headroom_rows=banks * WRITES)
+        for st in state.sdm_states:
+            st.prepare_step_capacity(banks * WRITES)
+        if timed:
+            ev[1].record(stream)
+        allocator.packed_sdm_cow_step_layers(state.sdm_states, ring[s % len(ring)], outputs=outputs,
+                                             scratch=scratch)
+        if timed:
+            ev[2].record(stream)
+        remaining = remaining - 1
+
+    for s in range(Wm):
+        one_step(s, False, None)
+    torch.cuda.synchronize(device)
+    growth0 = [(st.growth_events, st.growth_rows_added, st.growth_rows_copied) for st in state.sdm_states]
+    for k in stats:
+        stats[k] = 0
+    admitted_rows.clear()
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(K)]
+    with ClockSampler(device.index) as clocks:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        for i in range(K):
+            one_step(Wm + i, True, ev[i])
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+    stats["admitted_rows"] = int(sum(int(x) for x in admitted_rows))
+    life_ms = [a.elapsed_time(b) for a, b, _ in ev]
+    dec_ms = [b.elapsed_time(c) for _, b, c in ev]
+    for st in state.sdm_states:
+        st.validate_invariants()
+    growth = [tuple(x - y for x, y in zip((st.growth_events, st.growth_rows_added, st.growth_rows_copied), g0))
+              for st, g0 in zip(state.sdm_states, growth0)]
+    return dict(total_ms=sum(life_ms) + sum(dec_ms), decode_ms=sum(dec_ms), lifecycle_ms=sum(life_ms),
+                clocks=clocks.summary(), setup_s=setup_s, stats=stats, quantum=quantum,
+                growth_events=sum(g[0] for g in growth), growth_rows_added=sum(g[1] for g in growth),
+                growth_rows_copied=sum(g[2] for g in growth),
+                allocated_rows=sum(int(st.allocated_rows_tensor()) for st in state.sdm_states),
+                capacity_rows=sum(st.capacity_rows for st in state.sdm_states),
+                storage=state.storage_bytes(), banks=banks, live=live)
+
+
+def cpu_churn_rate(seconds: float, quantum_steps: int) -> dict:
+    """The oracle's churn loop on 8 live slots (32 banks) of one layer: decode
+    steps with release -> retain -> sparse-prefill cohort -> append on
+    completion, extrapolated to 256 slots x 7 layers per step (banks are
+    independent, so CPU time scales with their number)."""
+    from oracle import cow_oracle as O
+
+    rng = np.random.default_rng(12)
+    live = 8
+    banks = live * CH_HEADS
+    q = O.growth_quantum_rows(banks, WRITES, quantum_steps)
+    m0 = (0.02 * rng.standard_normal((CH_HEADS, CH_SLOTS, WIDTH))).astype(np.float32)
+
+    def prefill(requests, tokens):
+        b = requests * CH_HEADS
+        routes = lambda k: np.stack([O.uniform_routes(rng, b, CH_SLOTS, k) for _ in range(tokens)], 1)
+        st, _ = O.sparse_prefill(
+            m0, np.tile(np.arange(CH_HEADS), requests), routes(WRITES),
+            O.softmax(rng.standard_normal((b, tokens, WRITES), dtype=np.float32)),
+            rng.standard_normal((b, tokens, WIDTH), dtype=np.float32), rng.random((b, tokens), dtype=np.float32),
+            -rng.random((b, tokens), dtype=np.float32), routes(READS),
+            O.softmax(rng.standard_normal((b, tokens, READS), dtype=np.float32)), growth_quantum_rows=q)
+        return st
+
+    st = prefill(live, CH_WARM_PREFIX // 16)
+    remaining = rng.integers(1, CH_MAX_LEN + 1, size=live)
+    xs = [O.synthetic_step_inputs(rng, banks, CH_SLOTS, WIDTH, WRITES, READS) for _ in range(4)]
+    n = completions = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        done = np.nonzero(remaining == 0)[0]
+        if done.size:
+            completions += done.size
+            released = (done[:, None] * CH_HEADS + np.arange(CH_HEADS)).reshape(-1)
+            O.release(st, released)
+            O.retain_banks(st, np.setdiff1d(np.arange(st.banks), released))
+            O.append_banks_from(st, prefill(int(done.size), CH_PROMPT))
+            remaining = np.concatenate([remaining[remaining > 0],
+                                        rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=done.size)])
+        O.prepare_step_capacity(st, banks * WRITES)
+        O.packed_step(st, **xs[n % len(xs)])
+        remaining = remaining - 1
+        n += 1
+    dt = time.perf_counter() - t0
+    step_s = dt / n * (CH_LIVE / live) * LAYERS
+    return {"value": CH_LIVE / step_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} oracle churn steps of {banks} banks (8 live slots x 4 heads, N={CH_SLOTS}), "
+                      f"{completions} completions with release/retain/prefill/append, one layer, {dt:.1f} s, "
+                      f"extrapolated to {CH_LIVE} slots x {LAYERS} layers per step"}
+
+
+# --------------------------------------------------------------------------
 # CPU arms (the reference's algorithm, restated in oracle/)
 # --------------------------------------------------------------------------
 
@@ -598,10 +810,15 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="screen", choices=["screen", "scaleout"],
-                    help="screen: configuration 3 (default, the headline); scaleout: configuration 4")
+    ap.add_argument("--workload", default="screen", choices=["screen", "scaleout", "churn"],
+                    help="screen: configuration 3 (default, the headline); scaleout: configuration 4; "
+                         "churn: configuration 5")
     ap.add_argument("--requests", type=int, default=SO_REQUESTS, help="scaleout: requests over all GPUs")
     ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
+    ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
+    ap.add_argument("--trim-every", type=int, default=0, help="churn: trim the pools every this many steps")
+    ap.add_argument("--churn-warm-prefix", type=int, default=CH_WARM_PREFIX,
+                    help="churn: prefix tokens of the initial batch")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -631,6 +848,8 @@ def main() -> int:
     torch.backends.cuda.matmul.allow_tf32 = False
     if args.workload == "scaleout":
         return main_scaleout(args, rank, world, device)
+    if args.workload == "churn":
+        return main_churn(args, rank, world, device)
     res = run_gpu(args, rank, world, device)
 
     from copy_on_write_sdm_b200.sharding import reduce_over_ranks
@@ -720,6 +939,46 @@ def main_scaleout(args, rank, world, device) -> int:
         "cpu_baseline": cpu_scaleout_rate(args.cpu_seconds, res["requests"] * world, args.prefix),
         "mean_touched_rows_per_bank": res["mean_touched_rows_per_bank"],
         "first_touches_in_timed_steps": res["first_touches"], "retained_state": res["state_bytes"],
+        "setup_s": res["setup_s"],
+    }
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main_churn(args, rank, world, device) -> int:
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    res = run_gpu_churn(args, rank, world, device)
+    (total_ms,) = reduce_over_ranks([res["total_ms"]], op="max", device=device)
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return 0
+    K = args.steps
+    tokens = res["live"] * world * K
+    line = {
+        "metric": METRIC, "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 5 continuous-batching churn: 7 SDM pools, N=4096, D=128, H=4, top-16/top-4, "
+                               "256 live slots, Poisson(8) arrivals, lengths U[64,4096], 64-token prompts "
+                               "(sparse prefill), release -> compact -> admit on completion",
+                   "live_slots_per_gpu": res["live"], "global_batch": res["live"] * world,
+                   "growth_quantum_steps": args.quantum_steps, "growth_quantum_rows": res["quantum"],
+                   "trim_every": args.trim_every, "initial_prefix": args.churn_warm_prefix,
+                   "parallelism": f"requests sharded, {res['live']} slots per GPU x {world} GPU(s), no collective",
+                   "l2": "pool state (>10 GB) exceeds L2; steps timed back to back"},
+        "decode_ms_per_step": res["decode_ms"] / K, "lifecycle_ms_per_step": res["lifecycle_ms"] / K,
+        "lifecycle": {**res["stats"], "growth_events": res["growth_events"],
+                      "growth_rows_added": res["growth_rows_added"], "growth_rows_copied": res["growth_rows_copied"]},
+        "retained_state": {"allocated_rows": res["allocated_rows"], "capacity_rows": res["capacity_rows"],
+                           **res["storage"]},
+        "e2e": None, "gpu_launches": K,
+        "gpu_launches_note": "fused decode launches; lifecycle kernels (release, retain, prefill, append, grow) "
+                             "vary with completions and are not counted",
+        "clocks": res["clocks"],
+        "cpu_baseline": cpu_churn_rate(args.cpu_seconds, args.quantum_steps),
         "setup_s": res["setup_s"],
     }
     print(json.dumps(line))

@@ -288,74 +288,43 @@ class PackedSDMCopyOnWriteState:
         the prefix readings ``[banks,T,D]`` (the reference's readings).
         """
 
-        shared_initial_memory = cls._normalise_m0(shared_initial_memory)
-        if write_indices.ndim != 3 or read_indices.ndim != 3:
-            raise ValueError("prefix routes must be [banks,T,K]")
-        banks, time, writes = write_indices.shape
-        reads = read_indices.shape[2]
-        width = shared_initial_memory.shape[2]
-        slots = shared_initial_memory.shape[1]
-        if (
-            write_weights.shape != write_indices.shape
-            or read_weights.shape != read_indices.shape
-            or read_indices.shape[:2] != (banks, time)
-            or values.shape != (banks, time, width)
-            or input_gate.shape != (banks, time)
-            or forget_log_gate.shape != (banks, time)
-            or (erase_gate is not None and erase_gate.shape != (banks, time))
-            or template_indices.shape != (banks,)
-        ):
-            raise ValueError("SDM prefix routes, values and gates do not align")
-        if time <= 0:
-            raise ValueError("prefill requires at least one token")
-        _lib.require_cuda(write_indices, "prefix write indices")
-        lib = _lib.load()
-        device = write_indices.device
-        stream = _lib.stream_of(device)
-        step = _StepArgs.make(write_indices.reshape(banks * time, writes),
-                              write_weights.reshape(banks * time, writes),
-                              values.reshape(banks * time, width),
-                              input_gate.reshape(-1), forget_log_gate.reshape(-1),
-                              read_indices.reshape(banks * time, reads),
-                              read_weights.reshape(banks * time, reads),
-                              None if erase_gate is None else erase_gate.reshape(-1),
-                              collect=False)
-        mapping = torch.full((banks, slots), -1, device=device, dtype=torch.int32)
-        status = torch.zeros((), device=device, dtype=torch.int32)
-        _lib.check(lib.cow_prefill_mark(step.widx.data_ptr(), step.idx_code, banks, time, writes,
-                                        slots, mapping.data_ptr(), status.data_ptr(), stream),
-                   "cow_prefill_mark")
-        bits = int(status)
-        if bits:
-            raise ValueError(_lib.status_text(bits))
-        state = cls._pack_layout(
-            shared_initial_memory, mapping, template_indices,
-            capacity_rows=capacity_rows, state_dtype=state_dtype,
+        states, readings = from_prefix_routes_layers(
+            [shared_initial_memory],
+            [dict(write_indices=write_indices, write_weights=write_weights, values=values,
+                  input_gate=input_gate, forget_log_gate=forget_log_gate, read_indices=read_indices,
+                  read_weights=read_weights, erase_gate=erase_gate)],
+            template_indices=template_indices, capacity_rows=capacity_rows, state_dtype=state_dtype,
             maximum_future_allocations=maximum_future_allocations,
-            growth_quantum_rows=growth_quantum_rows, row_source=("m0", None), validate=False,
-        )
-        pool = state._pool()
-        _lib.check(lib.cow_prefill_recurrence(ctypes.byref(pool), ctypes.byref(step.struct), time,
-                                              writes, reads, step.idx_code, step.act_code, stream),
-                   "cow_prefill_recurrence")
-        bits = int(state.overflow_flag)
-        if bits:
-            raise ValueError(_lib.status_text(bits))
-        state.validate_invariants()
-        return state, step.output.reshape(banks, time, width)
+            growth_quantum_rows=growth_quantum_rows)
+        return states[0], readings[0]
 
     @classmethod
     def _pack_layout(cls, m0, mapping, template_indices, *, capacity_rows, state_dtype,
                      maximum_future_allocations, growth_quantum_rows, row_source, validate=True):
         """nonzero()-order layout of ``mapping >= 0`` (allocator.py:624-689)."""
+        device = mapping.device
+        scan = _scan_scratch(device, mapping.numel())
+        _lib.check(_lib.load().cow_pack_count(mapping.data_ptr(), mapping.numel(), scan.data_ptr(),
+                                              _lib.stream_of(device)), "cow_pack_count")
+        templates = template_indices.to(torch.int64).contiguous()
+        active_count, lo, hi = _read_counts_and_range([scan[0]], templates)
+        _check_template_range(lo, hi, m0)
+        state = cls._pack_finish(m0, mapping, templates, scan, active_count[0], capacity_rows=capacity_rows,
+                                 state_dtype=state_dtype, maximum_future_allocations=maximum_future_allocations,
+                                 growth_quantum_rows=growth_quantum_rows, row_source=row_source)
+        if validate:
+            state.validate_invariants()
+        return state
+
+    @classmethod
+    def _pack_finish(cls, m0, mapping, templates, scan, active_count, *, capacity_rows, state_dtype,
+                     maximum_future_allocations, growth_quantum_rows, row_source):
+        """Size and build the packed pool once ``cow_pack_count`` has run on ``mapping``."""
         lib = _lib.load()
         device = mapping.device
         stream = _lib.stream_of(device)
         banks, slots = mapping.shape
         n = banks * slots
-        scan = _scan_scratch(device, n)
-        _lib.check(lib.cow_pack_count(mapping.data_ptr(), n, scan.data_ptr(), stream), "cow_pack_count")
-        active_count = int(scan[0])
         if capacity_rows is None and growth_quantum_rows:
             q = growth_quantum_rows
             selected = max(q, ((active_count + q - 1) // q) * q)
@@ -371,11 +340,6 @@ class PackedSDMCopyOnWriteState:
                 raise ValueError("SDM physical capacity cannot cover the declared decode trace")
         else:
             possible = 0
-        templates = template_indices.to(torch.int64).contiguous()
-        if templates.numel():
-            lo, hi = torch.aminmax(templates)
-            if int(lo) < 0 or int(hi) >= m0.shape[0]:
-                raise ValueError("template index lies outside shared initial memory")
         state = cls._empty(m0, templates, banks=banks, capacity_rows=selected,
                            state_dtype=state_dtype, growth_quantum_rows=growth_quantum_rows,
                            init=False, mapping=mapping)
@@ -398,8 +362,6 @@ class PackedSDMCopyOnWriteState:
                                              stream), "cow_copy_rows")
         state.capacity_is_proven = maximum_future_allocations is not None
         state.proven_maximum_additional_allocations = possible
-        if validate:
-            state.validate_invariants()
         return state
 
     # ---------------- plumbing ----------------
@@ -519,6 +481,12 @@ class PackedSDMCopyOnWriteState:
     def append_banks_from(self, other: "PackedSDMCopyOnWriteState") -> int:
         """Admit another cohort's banks; copy only live rows (allocator.py:842-915)."""
 
+        scan = self._append_count(other)
+        (active_count, free_count), _, _ = _read_counts_and_range([scan[0], self.free_count], None)
+        return self._append_apply(other, scan, active_count, free_count)
+
+    def _append_count(self, other: "PackedSDMCopyOnWriteState") -> torch.Tensor:
+        """Admission, phase 1: compatibility checks and the live-row count of ``other``."""
         if (
             other.slots != self.slots
             or other.width != self.width
@@ -532,17 +500,22 @@ class PackedSDMCopyOnWriteState:
             and not torch.equal(other.shared_initial_memory, self.shared_initial_memory)
         ):
             raise ValueError("admitted SDM banks use different learned initial memory")
+        n = other.banks * other.slots
+        scan = _scan_scratch(self.values.device, n)
+        _lib.check(_lib.load().cow_pack_count(other.logical_to_physical.data_ptr(), n, scan.data_ptr(),
+                                              self._stream()), "cow_pack_count")
+        return scan
+
+    def _append_apply(self, other: "PackedSDMCopyOnWriteState", scan: torch.Tensor, active_count: int,
+                      free_count: int) -> int:
+        """Admission, phase 2: grow if needed, pop and copy rows, extend map and templates.
+        ``active_count`` / ``free_count`` are the host values of phase 1's count and this
+        pool's free count."""
         lib = _lib.load()
         stream = self._stream()
         device = self.values.device
-        n = other.banks * other.slots
-        scan = _scan_scratch(device, n)
-        _lib.check(lib.cow_pack_count(other.logical_to_physical.data_ptr(), n, scan.data_ptr(), stream),
-                   "cow_pack_count")
-        active_count = int(scan[0])
-        free_count = int(self.free_count.item())
         if free_count < active_count:
-            self.grow_capacity(self.capacity_rows + active_count - free_count)
+            free_count += self.grow_capacity(self.capacity_rows + active_count - free_count)
         admitted = torch.empty(other.banks, self.slots, device=device, dtype=torch.int32)
         src_rows = torch.empty(max(active_count, 1), device=device, dtype=torch.int32)
         dst_rows = torch.empty(max(active_count, 1), device=device, dtype=torch.int32)
@@ -559,8 +532,9 @@ class PackedSDMCopyOnWriteState:
         self.logical_to_physical = torch.cat((self.logical_to_physical, admitted), dim=0).contiguous()
         self.template_indices = torch.cat((self.template_indices, other.template_indices), dim=0).contiguous()
         if self.growth_quantum_rows:
+            # free_count on the device is now free_count - active_count
             self.proven_maximum_additional_allocations = min(
-                self.proven_maximum_additional_allocations, int(self.free_count.item())
+                self.proven_maximum_additional_allocations, free_count - active_count
             )
         else:
             self.capacity_is_proven = False
@@ -571,6 +545,10 @@ class PackedSDMCopyOnWriteState:
     def retain_banks(self, bank_indices: torch.Tensor) -> None:
         """Compact already-released banks; live rows do not move (allocator.py:917-943)."""
 
+        pending = self._retain_launch(bank_indices)
+        self._retain_commit(pending, int(pending[2]))
+
+    def _retain_launch(self, bank_indices: torch.Tensor):
         if (
             bank_indices.ndim != 1
             or bank_indices.dtype not in (torch.int32, torch.int64)
@@ -588,13 +566,18 @@ class PackedSDMCopyOnWriteState:
         self._call("cow_retain", ctypes.byref(pool), indices.data_ptr() if count else None, count,
                    new_map.data_ptr(), new_templates.data_ptr(), selected.data_ptr(),
                    status.data_ptr(), self._stream())
-        bits = int(status)
+        return new_map, new_templates, status
+
+    @staticmethod
+    def _retain_check(bits: int) -> None:
         if bits & _lib.ST_BAD_BANK_LIST:
             raise ValueError("retained bank index is invalid or duplicated")
         if bits & _lib.ST_DISCARD_LIVE:
             raise ValueError("discarded SDM banks must be released before compaction")
-        self.logical_to_physical = new_map
-        self.template_indices = new_templates
+
+    def _retain_commit(self, pending, bits: int) -> None:
+        self._retain_check(bits)
+        self.logical_to_physical, self.template_indices = pending[0], pending[1]
 
     @property
     def banks(self) -> int:
@@ -697,25 +680,28 @@ class PackedSDMCopyOnWriteState:
     def validate_invariants(self) -> dict[str, Any]:
         """Live rows and the free stack partition ``[0, C)`` (allocator.py:1070-1096); synchronises."""
 
+        return validate_layers([self])[0]
+
+    def _validate_launch(self) -> torch.Tensor:
         device = self.values.device
         counts = torch.empty(max(self.capacity_rows, 1), device=device, dtype=torch.int32)
         status = torch.zeros((), device=device, dtype=torch.int32)
         pool = self._pool()
         self._call("cow_validate", ctypes.byref(pool), counts.data_ptr(), status.data_ptr(),
                    self._stream())
-        flag = int(self.overflow_flag.item())
+        return status
+
+    def _validate_result(self, flag: int, bits: int, free: int) -> dict[str, Any]:
         if flag & _lib.ST_SLAB_EXHAUSTED:
             raise AssertionError("SDM COW allocator recorded a slab overflow")
         if flag:
             raise AssertionError(f"SDM COW allocator recorded an error: {_lib.status_text(flag)}")
-        bits = int(status.item())
         if bits & _lib.ST_MULTI_OWNER:
             raise AssertionError("one physical SDM row has multiple logical owners")
         if bits & _lib.ST_FREE_DUPLICATE:
             raise AssertionError("free SDM row stack contains duplicates")
         if bits & (_lib.ST_NOT_COVERED | _lib.ST_ROW_RANGE):
             raise AssertionError("active and free SDM rows do not partition the slab")
-        free = int(self.free_count.item())
         return {
             "capacity_rows": self.capacity_rows,
             "allocated_rows": self.capacity_rows - free,
@@ -727,6 +713,180 @@ class PackedSDMCopyOnWriteState:
         """Synchronously read the device status word (0 = healthy)."""
 
         return int(self.overflow_flag.item())
+
+
+# --------------------------------------------------------------------------
+# several pools at once (the SDM layers of one serving batch)
+# --------------------------------------------------------------------------
+
+
+def _read_counts_and_range(values: Sequence[torch.Tensor], templates: torch.Tensor | None):
+    """One host synchronisation for several 0-d device integers and, optionally,
+    the (min, max) of a template-index vector.  Returns ``(ints, lo, hi)``."""
+    parts = [torch.stack([v.reshape(()).to(torch.int64) for v in values])] if values else []
+    if templates is not None and templates.numel():
+        lo, hi = torch.aminmax(templates)
+        parts.append(torch.stack((lo, hi)))
+    host = torch.cat(parts).tolist() if parts else []
+    k = len(values)
+    if templates is not None and templates.numel():
+        return host[:k], host[k], host[k + 1]
+    return host[:k], None, None
+
+
+def _check_template_range(lo, hi, m0: torch.Tensor) -> None:
+    if lo is not None and (lo < 0 or hi >= m0.shape[0]):
+        raise ValueError("template index lies outside shared initial memory")
+
+
+@torch.no_grad()
+def validate_layers(states: Sequence[PackedSDMCopyOnWriteState]) -> list[dict[str, Any]]:
+    """``validate_invariants`` of several pools with one host synchronisation."""
+    if not states:
+        return []
+    statuses = [st._validate_launch() for st in states]
+    flat = torch.stack([torch.stack((st.overflow_flag, bits, st.free_count)) for st, bits in zip(states, statuses)])
+    host = flat.tolist()
+    return [st._validate_result(*row) for st, row in zip(states, host)]
+
+
+@torch.no_grad()
+def release_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> int:
+    """``release`` on several pools; one host synchronisation for the total count."""
+    counts = [st.release(idx) for st, idx in zip(states, bank_indices)]
+    return int(torch.stack(counts).sum()) if counts else 0
+
+
+@torch.no_grad()
+def retain_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> None:
+    """``retain_banks`` on several pools; one host synchronisation.  Nothing
+    changes unless every pool's selection is valid."""
+    pending = [st._retain_launch(idx) for st, idx in zip(states, bank_indices)]
+    if not pending:
+        return
+    bits = torch.stack([p[2] for p in pending]).tolist()
+    for b in bits:
+        PackedSDMCopyOnWriteState._retain_check(b)
+    for st, p, b in zip(states, pending, bits):
+        st._retain_commit(p, b)
+
+
+@torch.no_grad()
+def append_layers(states: Sequence[PackedSDMCopyOnWriteState],
+                  others: Sequence[PackedSDMCopyOnWriteState]) -> list[int]:
+    """``append_banks_from`` on several pools; one host synchronisation."""
+    if len(states) != len(others):
+        raise ValueError("one admitted pool per destination pool")
+    scans = [st._append_count(o) for st, o in zip(states, others)]
+    if not scans:
+        return []
+    vals = []
+    for st, scan in zip(states, scans):
+        vals += [scan[0], st.free_count]
+    host, _, _ = _read_counts_and_range(vals, None)
+    return [st._append_apply(o, scan, host[2 * i], host[2 * i + 1])
+            for i, (st, o, scan) in enumerate(zip(states, others, scans))]
+
+
+@torch.no_grad()
+def from_prefix_routes_layers(
+    shared_initial_memories: Sequence[torch.Tensor],
+    prefixes: Sequence[dict],
+    *,
+    template_indices: torch.Tensor,
+    capacity_rows: int | None = None,
+    state_dtype: torch.dtype = torch.float32,
+    maximum_future_allocations: int | None = None,
+    growth_quantum_rows: int = 0,
+) -> tuple[list[PackedSDMCopyOnWriteState], list[torch.Tensor]]:
+    """Sparse prefill handoff of several independent pools (``from_prefix_routes``
+    per pool) with one recurrence launch and two host synchronisations.
+
+    ``prefixes[l]`` holds pool l's ``write_indices``, ``write_weights``,
+    ``values``, ``input_gate``, ``forget_log_gate``, ``read_indices``,
+    ``read_weights`` and optionally ``erase_gate`` (shapes ``[banks,T,W|R]``,
+    ``[banks,T,D]``, ``[banks,T]``); every pool has the same banks, T, W, R,
+    width and dtypes and uses ``template_indices``.
+    """
+    n = len(prefixes)
+    if len(shared_initial_memories) != n or not 1 <= n <= _lib.MAX_LAYERS:
+        raise ValueError(f"between 1 and {_lib.MAX_LAYERS} pools per prefill")
+    lib = _lib.load()
+    m0s, steps, shape = [], [], None
+    for m0, x in zip(shared_initial_memories, prefixes):
+        m0 = PackedSDMCopyOnWriteState._normalise_m0(m0)
+        write_indices, read_indices = x["write_indices"], x["read_indices"]
+        erase_gate = x.get("erase_gate")
+        if write_indices.ndim != 3 or read_indices.ndim != 3:
+            raise ValueError("prefix routes must be [banks,T,K]")
+        banks, time, writes = write_indices.shape
+        reads = read_indices.shape[2]
+        width, slots = m0.shape[2], m0.shape[1]
+        if (
+            x["write_weights"].shape != write_indices.shape
+            or x["read_weights"].shape != read_indices.shape
+            or read_indices.shape[:2] != (banks, time)
+            or x["values"].shape != (banks, time, width)
+            or x["input_gate"].shape != (banks, time)
+            or x["forget_log_gate"].shape != (banks, time)
+            or (erase_gate is not None and erase_gate.shape != (banks, time))
+            or template_indices.shape != (banks,)
+        ):
+            raise ValueError("SDM prefix routes, values and gates do not align")
+        if time <= 0:
+            raise ValueError("prefill requires at least one token")
+        _lib.require_cuda(write_indices, "prefix write indices")
+        step = _StepArgs.make(write_indices.reshape(banks * time, writes),
+                              x["write_weights"].reshape(banks * time, writes),
+                              x["values"].reshape(banks * time, width),
+                              x["input_gate"].reshape(-1), x["forget_log_gate"].reshape(-1),
+                              read_indices.reshape(banks * time, reads),
+                              x["read_weights"].reshape(banks * time, reads),
+                              None if erase_gate is None else erase_gate.reshape(-1),
+                              collect=False)
+        key = (banks, time, writes, reads, width, slots, step.idx_code, step.act_code)
+        if shape is not None and key != shape:
+            raise ValueError("pools prefilled together must share banks, T, W, R, width and dtypes")
+        shape = key
+        m0s.append(m0)
+        steps.append(step)
+    banks, time, writes, reads, width, slots, idx_code, act_code = shape
+    device = steps[0].widx.device
+    stream = _lib.stream_of(device)
+    templates = template_indices.to(torch.int64).contiguous()
+    status = torch.zeros(n, device=device, dtype=torch.int32)
+    maps, scans = [], []
+    for l, step in enumerate(steps):
+        mapping = torch.full((banks, slots), -1, device=device, dtype=torch.int32)
+        _lib.check(lib.cow_prefill_mark(step.widx.data_ptr(), step.idx_code, banks, time, writes, slots,
+                                        mapping.data_ptr(), status[l:].data_ptr(), stream), "cow_prefill_mark")
+        scan = _scan_scratch(device, banks * slots)
+        _lib.check(lib.cow_pack_count(mapping.data_ptr(), banks * slots, scan.data_ptr(), stream), "cow_pack_count")
+        maps.append(mapping)
+        scans.append(scan)
+    host, lo, hi = _read_counts_and_range(list(status) + [s[0] for s in scans], templates)
+    for bits in host[:n]:
+        if bits:
+            raise ValueError(_lib.status_text(bits))
+    _check_template_range(lo, hi, m0s[0])
+    states = [PackedSDMCopyOnWriteState._pack_finish(
+        m0s[l], maps[l], templates, scans[l], host[n + l], capacity_rows=capacity_rows, state_dtype=state_dtype,
+        maximum_future_allocations=maximum_future_allocations, growth_quantum_rows=growth_quantum_rows,
+        row_source=("m0", None)) for l in range(n)]
+    pools = (_lib.CowPool * n)(*[st._pool() for st in states])
+    structs = (_lib.CowStep * n)(*[step.struct for step in steps])
+    _lib.check(lib.cow_prefill_recurrence_layers(pools, structs, n, time, writes, reads, idx_code, act_code,
+                                                 stream), "cow_prefill_recurrence_layers")
+    # Route errors met during the walk are ValueErrors (as in the single-pool
+    # prefill); anything else is an invariant failure.
+    vstat = [st._validate_launch() for st in states]
+    flat = torch.stack([torch.stack((st.overflow_flag, b, st.free_count)) for st, b in zip(states, vstat)]).tolist()
+    for flag, _, _ in flat:
+        if flag:
+            raise ValueError(_lib.status_text(flag))
+    for st, row in zip(states, flat):
+        st._validate_result(*row)
+    return states, [step.output.reshape(banks, time, width) for step in steps]
 
 
 # --------------------------------------------------------------------------

@@ -21,7 +21,8 @@ from typing import TYPE_CHECKING, Sequence
 
 import torch
 
-from .allocator import PackedSDMCopyOnWriteState, dense_sdm_sparse_step, packed_sdm_cow_step
+from .allocator import (PackedSDMCopyOnWriteState, append_layers, dense_sdm_sparse_step, packed_sdm_cow_step,
+                        release_layers, retain_layers)
 from .sdm import SparseDeltaMemory
 
 if TYPE_CHECKING:
@@ -100,9 +101,8 @@ class FaithfulSDMDecodeState:
         if (min(host) < 0 or max(host) >= self.batch or len(set(host)) != len(host)
                 or not bool(self.active_sequences[chosen].all())):
             raise ValueError("released sequence is invalid, duplicated, or inactive")
-        total = 0
-        for state in self.sdm_states:
-            total += int(state.release(_banks_of(chosen, self._heads(state, self.batch))))
+        total = release_layers(self.sdm_states, [_banks_of(chosen, self._heads(state, self.batch))
+                                                 for state in self.sdm_states])
         self.active_sequences[chosen] = False
         return total
 
@@ -111,11 +111,19 @@ class FaithfulSDMDecodeState:
         """Drop released request slots; live rows stay where they are (inference.py:116-159)."""
         before = self.batch
         keep = self.active_sequences.nonzero().flatten()
+        if keep.numel() == before:
+            # Nothing was released: every gather below would be the identity,
+            # so only the checks and the position update remain.
+            for state in self.sdm_states:
+                self._heads(state, before)
+            if not before:
+                self.position = 0
+            elif self.positions is not None:
+                self.position = int(self.positions.max().item())
+            return keep
         positions = self.current_positions()
-        for state in self.sdm_states:
-            heads = self._heads(state, before)
-            if before:
-                state.retain_banks(_banks_of(keep, heads))
+        if before:
+            retain_layers(self.sdm_states, [_banks_of(keep, self._heads(state, before)) for state in self.sdm_states])
         self.dense_keys = tuple(t[keep].contiguous() for t in self.dense_keys)
         self.dense_values = tuple(t[keep].contiguous() for t in self.dense_values)
         kept_positions = positions[keep].contiguous()
@@ -139,8 +147,7 @@ class FaithfulSDMDecodeState:
         )
         if not compatible:
             raise ValueError("admitted faithful-SDM state is incompatible")
-        for mine, theirs in zip(self.sdm_states, incoming.sdm_states):
-            mine.append_banks_from(theirs)
+        append_layers(self.sdm_states, incoming.sdm_states)
         self.dense_keys = tuple(torch.cat(p, dim=0).contiguous() for p in zip(self.dense_keys, incoming.dense_keys))
         self.dense_values = tuple(torch.cat(p, dim=0).contiguous()
                                   for p in zip(self.dense_values, incoming.dense_values))

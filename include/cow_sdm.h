@@ -191,6 +191,13 @@ int cow_copy_rows(void* dst, int32_t dst_dtype, const int32_t* dst_rows, const v
 int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t time,
                            int32_t writes, int32_t reads, int32_t index_dtype,
                            int32_t act_dtype, void* stream);
+/* The same recurrence for `layers` independent pools (one prefix per pool,
+ * same width, slots, W, R and dtypes) in one launch, so the serial token walks
+ * of every SDM layer of a prefilled cohort run side by side
+ * (prefill_faithful_sdm_stack, inference.py:369-456, prefills all layers). */
+int cow_prefill_recurrence_layers(const cow_pool* pools, const cow_step* prefixes, int32_t layers,
+                                  int64_t time, int32_t writes, int32_t reads, int32_t index_dtype,
+                                  int32_t act_dtype, void* stream);
 
 /* grow_capacity (allocator.py:692-744): copy rows [0,old_cap) into the new
  * slab, the old free stack below arange(old_cap,new_cap) in the new stack,
