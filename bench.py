@@ -593,15 +593,16 @@ def run_gpu_churn(args, rank, world, device):
     batch compacted (``release_and_compact``), a cohort of the same size is
     prefilled (64-token prompts, sparse prefill) and admitted (``admit``),
     the slab is trimmed every ``--trim-every`` steps if asked, each pool's
-    capacity proof is renewed (``prepare_step_capacity``, growing by whole
-    quanta), and one fused decode launch covers the 7 pools.  Arrivals are
+    then ``DecodeSession.step`` renews each pool's capacity proof
+    (``prepare_step_capacity``, growing by whole quanta) and runs one fused
+    decode launch over the 7 pools.  Arrivals are
     Poisson(8) per step into a FIFO queue; with mean length 2,080 tokens the
     queue never drains, so the batch stays full and admissions equal
     completions.  The initial batch starts from a 1,024-token prefix (about
     2,600 private rows per bank, near the steady-state mean) with residual
     lengths drawn uniformly below each request's length.
     """
-    from copy_on_write_sdm_b200 import allocator
+    from copy_on_write_sdm_b200 import DecodeSession
 
     rng = np.random.default_rng(5000 + rank)
     gen = torch.Generator(device=device).manual_seed(5000 + rank)
@@ -617,18 +618,22 @@ def run_gpu_churn(args, rank, world, device):
     next_prompt = 0
     lengths = rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=live)
     remaining = np.array([rng.integers(1, n + 1) for n in lengths])
+    # Decode runs through a DecodeSession over the state's pools (the objects
+    # persist through release/compact/admit/trim; the session re-reads their
+    # tensors when they change).  Each step's routes are one device copy from
+    # a ring of 16 pre-generated steps into the session's input buffer.
+    session = DecodeSession(state.sdm_states, writes=WRITES, reads=READS)
     ring = []
     for _ in range(16):
-        ring.append([dict(
-            write_indices=affine_routes(gen, (banks,), WRITES, CH_SLOTS, device),
-            read_indices=affine_routes(gen, (banks,), READS, CH_SLOTS, device),
-            write_weights=torch.softmax(torch.randn(banks, WRITES, generator=gen, device=device), -1),
-            read_weights=torch.softmax(torch.randn(banks, READS, generator=gen, device=device), -1),
-            values=torch.randn(banks, WIDTH, generator=gen, device=device),
-            input_gate=torch.rand(banks, generator=gen, device=device),
-            forget_log_gate=-torch.rand(banks, generator=gen, device=device)) for _ in range(LAYERS)])
-    outputs = [torch.empty(banks, WIDTH, device=device) for _ in range(LAYERS)]
-    scratch = allocator.decode_scratch(device, banks * LAYERS, LAYERS)
+        for v in session.views:
+            v["write_indices"].copy_(affine_routes(gen, (banks,), WRITES, CH_SLOTS, device))
+            v["read_indices"].copy_(affine_routes(gen, (banks,), READS, CH_SLOTS, device))
+            v["write_weights"].copy_(torch.softmax(torch.randn(banks, WRITES, generator=gen, device=device), -1))
+            v["read_weights"].copy_(torch.softmax(torch.randn(banks, READS, generator=gen, device=device), -1))
+            v["values"].copy_(torch.randn(banks, WIDTH, generator=gen, device=device))
+            v["input_gate"].copy_(torch.rand(banks, generator=gen, device=device))
+            v["forget_log_gate"].copy_(-torch.rand(banks, generator=gen, device=device))
+        ring.append(session.inputs.clone())
     torch.cuda.synchronize(device)
     setup_s = time.time() - t0
     stats = dict(completions=0, released_rows=0, trimmed_rows=0, queue=0)
@@ -655,12 +660,10 @@ def run_gpu_churn(args, rank, world, device):
                                         rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=done.size)])
         if args.trim_every and s % args.trim_every == args.trim_every - 1:
             stats["trimmed_rows"] += state.trim_sdm_pools(headroom_rows=banks * WRITES)
-        for st in state.sdm_states:
-            st.prepare_step_capacity(banks * WRITES)
         if timed:
             ev[1].record(stream)
-        allocator.packed_sdm_cow_step_layers(state.sdm_states, ring[s % len(ring)], outputs=outputs,
-                                             scratch=scratch)
+        session.inputs.copy_(ring[s % len(ring)])
+        session.step()
         if timed:
             ev[2].record(stream)
         remaining = remaining - 1

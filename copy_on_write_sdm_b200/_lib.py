@@ -103,6 +103,19 @@ _SIGNATURES = {
     "cow_retain": (c_int32, [POINTER(CowPool), P, c_int64, P, P, P, P, P]),
     "cow_validate": (c_int32, [POINTER(CowPool), P, P, P]),
     "cow_materialize": (c_int32, [POINTER(CowPool), P, c_int32, P]),
+    "cow_release_workspace_bytes": (c_int64, [POINTER(CowPool), P, c_int32]),
+    "cow_release_layers": (c_int32, [POINTER(CowPool), P, P, c_int32, P, c_int64, P, P]),
+    "cow_retain_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32]),
+    "cow_retain_layers": (c_int32, [POINTER(CowPool), P, P, c_int32, P, P, P, c_int64, P, P]),
+    "cow_append_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32]),
+    "cow_append_count_layers": (c_int32, [POINTER(CowPool), POINTER(CowPool), c_int32, P, c_int64, P, P]),
+    "cow_append_layers": (c_int32, [POINTER(CowPool), POINTER(CowPool), c_int32, P, P, c_int64, P]),
+    "cow_pack_workspace_bytes": (c_int64, [c_int64, c_int32]),
+    "cow_prefill_mark_count_layers": (c_int32, [P, c_int32, c_int64, c_int64, c_int32, c_int64, P, c_int32, P,
+                                                c_int64, P, P]),
+    "cow_pack_apply_layers": (c_int32, [POINTER(CowPool), c_int32, P, c_int64, P]),
+    "cow_validate_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32]),
+    "cow_validate_layers": (c_int32, [POINTER(CowPool), c_int32, P, c_int64, P, P]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -317,14 +317,11 @@ class PackedSDMCopyOnWriteState:
         return state
 
     @classmethod
-    def _pack_finish(cls, m0, mapping, templates, scan, active_count, *, capacity_rows, state_dtype,
-                     maximum_future_allocations, growth_quantum_rows, row_source):
-        """Size and build the packed pool once ``cow_pack_count`` has run on ``mapping``."""
-        lib = _lib.load()
-        device = mapping.device
-        stream = _lib.stream_of(device)
+    def _pack_state(cls, m0, mapping, templates, active_count, *, capacity_rows, state_dtype,
+                    maximum_future_allocations, growth_quantum_rows):
+        """Capacity choice and tensors of a packed pool holding ``active_count`` live
+        rows (allocator.py:624-689); the caller fills map, stack and rows."""
         banks, slots = mapping.shape
-        n = banks * slots
         if capacity_rows is None and growth_quantum_rows:
             q = growth_quantum_rows
             selected = max(q, ((active_count + q - 1) // q) * q)
@@ -343,6 +340,22 @@ class PackedSDMCopyOnWriteState:
         state = cls._empty(m0, templates, banks=banks, capacity_rows=selected,
                            state_dtype=state_dtype, growth_quantum_rows=growth_quantum_rows,
                            init=False, mapping=mapping)
+        state.capacity_is_proven = maximum_future_allocations is not None
+        state.proven_maximum_additional_allocations = possible
+        return state
+
+    @classmethod
+    def _pack_finish(cls, m0, mapping, templates, scan, active_count, *, capacity_rows, state_dtype,
+                     maximum_future_allocations, growth_quantum_rows, row_source):
+        """Size and build the packed pool once ``cow_pack_count`` has run on ``mapping``."""
+        lib = _lib.load()
+        device = mapping.device
+        stream = _lib.stream_of(device)
+        banks, slots = mapping.shape
+        n = banks * slots
+        state = cls._pack_state(m0, mapping, templates, active_count, capacity_rows=capacity_rows,
+                                state_dtype=state_dtype, maximum_future_allocations=maximum_future_allocations,
+                                growth_quantum_rows=growth_quantum_rows)
         src_index = torch.empty(max(active_count, 1), device=device, dtype=torch.int32)
         pool = state._pool()
         _lib.check(lib.cow_pack_apply(mapping.data_ptr(), n, src_index.data_ptr(), ctypes.byref(pool),
@@ -360,8 +373,6 @@ class PackedSDMCopyOnWriteState:
                                              src_index.data_ptr(), active_count, m0.shape[2], 1,
                                              state._m0_f32.data_ptr(), templates.data_ptr(), slots,
                                              stream), "cow_copy_rows")
-        state.capacity_is_proven = maximum_future_allocations is not None
-        state.proven_maximum_additional_allocations = possible
         return state
 
     # ---------------- plumbing ----------------
@@ -481,12 +492,9 @@ class PackedSDMCopyOnWriteState:
     def append_banks_from(self, other: "PackedSDMCopyOnWriteState") -> int:
         """Admit another cohort's banks; copy only live rows (allocator.py:842-915)."""
 
-        scan = self._append_count(other)
-        (active_count, free_count), _, _ = _read_counts_and_range([scan[0], self.free_count], None)
-        return self._append_apply(other, scan, active_count, free_count)
+        return append_layers([self], [other])[0]
 
-    def _append_count(self, other: "PackedSDMCopyOnWriteState") -> torch.Tensor:
-        """Admission, phase 1: compatibility checks and the live-row count of ``other``."""
+    def _append_check(self, other: "PackedSDMCopyOnWriteState") -> None:
         if (
             other.slots != self.slots
             or other.width != self.width
@@ -500,35 +508,11 @@ class PackedSDMCopyOnWriteState:
             and not torch.equal(other.shared_initial_memory, self.shared_initial_memory)
         ):
             raise ValueError("admitted SDM banks use different learned initial memory")
-        n = other.banks * other.slots
-        scan = _scan_scratch(self.values.device, n)
-        _lib.check(_lib.load().cow_pack_count(other.logical_to_physical.data_ptr(), n, scan.data_ptr(),
-                                              self._stream()), "cow_pack_count")
-        return scan
 
-    def _append_apply(self, other: "PackedSDMCopyOnWriteState", scan: torch.Tensor, active_count: int,
-                      free_count: int) -> int:
-        """Admission, phase 2: grow if needed, pop and copy rows, extend map and templates.
-        ``active_count`` / ``free_count`` are the host values of phase 1's count and this
-        pool's free count."""
-        lib = _lib.load()
-        stream = self._stream()
-        device = self.values.device
-        if free_count < active_count:
-            free_count += self.grow_capacity(self.capacity_rows + active_count - free_count)
-        admitted = torch.empty(other.banks, self.slots, device=device, dtype=torch.int32)
-        src_rows = torch.empty(max(active_count, 1), device=device, dtype=torch.int32)
-        dst_rows = torch.empty(max(active_count, 1), device=device, dtype=torch.int32)
-        dst_pool, src_pool = self._pool(), other._pool()
-        _lib.check(lib.cow_append(ctypes.byref(dst_pool), ctypes.byref(src_pool), admitted.data_ptr(),
-                                  src_rows.data_ptr(), dst_rows.data_ptr(), scan.data_ptr(), stream),
-                   "cow_append")
-        sdt = _lib.dtype_code(self.values.dtype)
-        if active_count:
-            _lib.check(lib.cow_copy_rows(self.values.data_ptr(), sdt, dst_rows.data_ptr(),
-                                         other.values.data_ptr(), sdt, src_rows.data_ptr(),
-                                         active_count, self.width, 0, None, None, self.slots, stream),
-                       "cow_copy_rows")
+    def _append_commit(self, other: "PackedSDMCopyOnWriteState", admitted: torch.Tensor, active_count: int,
+                       free_count: int) -> None:
+        """Extend map and templates after the rows moved.  ``free_count`` is the
+        free count the pop started from (after any growth)."""
         self.logical_to_physical = torch.cat((self.logical_to_physical, admitted), dim=0).contiguous()
         self.template_indices = torch.cat((self.template_indices, other.template_indices), dim=0).contiguous()
         if self.growth_quantum_rows:
@@ -539,34 +523,12 @@ class PackedSDMCopyOnWriteState:
         else:
             self.capacity_is_proven = False
             self.proven_maximum_additional_allocations = 0
-        return active_count
 
     @torch.no_grad()
     def retain_banks(self, bank_indices: torch.Tensor) -> None:
         """Compact already-released banks; live rows do not move (allocator.py:917-943)."""
 
-        pending = self._retain_launch(bank_indices)
-        self._retain_commit(pending, int(pending[2]))
-
-    def _retain_launch(self, bank_indices: torch.Tensor):
-        if (
-            bank_indices.ndim != 1
-            or bank_indices.dtype not in (torch.int32, torch.int64)
-            or bank_indices.device != self.values.device
-        ):
-            raise ValueError("retained bank indices must be integer [S] on device")
-        indices = bank_indices.to(torch.int64).contiguous()
-        count = indices.numel()
-        device = self.values.device
-        new_map = torch.empty(count, self.slots, device=device, dtype=torch.int32)
-        new_templates = torch.empty(count, device=device, dtype=torch.int64)
-        selected = torch.empty(max(self.banks, 1), device=device, dtype=torch.int32)
-        status = torch.zeros((), device=device, dtype=torch.int32)
-        pool = self._pool()
-        self._call("cow_retain", ctypes.byref(pool), indices.data_ptr() if count else None, count,
-                   new_map.data_ptr(), new_templates.data_ptr(), selected.data_ptr(),
-                   status.data_ptr(), self._stream())
-        return new_map, new_templates, status
+        retain_layers([self], [bank_indices])
 
     @staticmethod
     def _retain_check(bits: int) -> None:
@@ -682,15 +644,6 @@ class PackedSDMCopyOnWriteState:
 
         return validate_layers([self])[0]
 
-    def _validate_launch(self) -> torch.Tensor:
-        device = self.values.device
-        counts = torch.empty(max(self.capacity_rows, 1), device=device, dtype=torch.int32)
-        status = torch.zeros((), device=device, dtype=torch.int32)
-        pool = self._pool()
-        self._call("cow_validate", ctypes.byref(pool), counts.data_ptr(), status.data_ptr(),
-                   self._stream())
-        return status
-
     def _validate_result(self, flag: int, bits: int, free: int) -> dict[str, Any]:
         if flag & _lib.ST_SLAB_EXHAUSTED:
             raise AssertionError("SDM COW allocator recorded a slab overflow")
@@ -739,53 +692,152 @@ def _check_template_range(lo, hi, m0: torch.Tensor) -> None:
         raise ValueError("template index lies outside shared initial memory")
 
 
+_WORKSPACE: dict[int, torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device scratch of the multi-pool lifecycle calls (stream-ordered reuse)."""
+    if nbytes < 0:
+        raise ValueError("invalid pools for a multi-pool lifecycle call")
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _WORKSPACE.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes + nbytes // 4, 1 << 16), dtype=torch.uint8, device=device)
+        _WORKSPACE[key] = buf
+    return buf
+
+
+def _chunks(n: int):
+    for a in range(0, n, _lib.MAX_LAYERS):
+        yield a, min(n, a + _lib.MAX_LAYERS)
+
+
+def _pool_array(states) -> ctypes.Array:
+    return (_lib.CowPool * len(states))(*[st._pool() for st in states])
+
+
+def _ptrs(tensors) -> ctypes.Array:
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if t is not None and t.numel() else None
+                                              for t in tensors])
+
+
+def _bank_list(bank_indices: torch.Tensor, device, what: str) -> torch.Tensor:
+    if (
+        bank_indices.ndim != 1
+        or bank_indices.dtype not in (torch.int32, torch.int64)
+        or bank_indices.device != device
+    ):
+        raise ValueError(f"{what} bank indices must be integer [S] on device")
+    return bank_indices.to(torch.int64).contiguous()
+
+
 @torch.no_grad()
 def validate_layers(states: Sequence[PackedSDMCopyOnWriteState]) -> list[dict[str, Any]]:
-    """``validate_invariants`` of several pools with one host synchronisation."""
+    """``validate_invariants`` of several pools: one call per 8 pools, one host synchronisation."""
     if not states:
         return []
-    statuses = [st._validate_launch() for st in states]
-    flat = torch.stack([torch.stack((st.overflow_flag, bits, st.free_count)) for st, bits in zip(states, statuses)])
-    host = flat.tolist()
-    return [st._validate_result(*row) for st, row in zip(states, host)]
+    lib = _lib.load()
+    device = states[0].values.device
+    stream = _lib.stream_of(device)
+    outs = []
+    for a, b in _chunks(len(states)):
+        pools = _pool_array(states[a:b])
+        ws = _workspace(device, lib.cow_validate_workspace_bytes(pools, b - a))
+        out = torch.empty(3 * (b - a), dtype=torch.int32, device=device)
+        _lib.check(lib.cow_validate_layers(pools, b - a, ws.data_ptr(), ws.numel(), out.data_ptr(), stream),
+                   "cow_validate_layers")
+        outs.append(out)
+    host = torch.cat(outs).tolist()
+    return [st._validate_result(*host[3 * i:3 * i + 3]) for i, st in enumerate(states)]
 
 
 @torch.no_grad()
 def release_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> int:
-    """``release`` on several pools; one host synchronisation for the total count."""
-    counts = [st.release(idx) for st, idx in zip(states, bank_indices)]
-    return int(torch.stack(counts).sum()) if counts else 0
+    """``release`` on several pools: one call per 8 pools, one host synchronisation
+    for the total count."""
+    if len(states) != len(bank_indices):
+        raise ValueError("one bank list per pool")
+    if not states:
+        return 0
+    lib = _lib.load()
+    device = states[0].values.device
+    stream = _lib.stream_of(device)
+    idx = [_bank_list(b, st.values.device, "released") for st, b in zip(states, bank_indices)]
+    released = torch.empty(len(states), dtype=torch.int32, device=device)
+    for a, b in _chunks(len(states)):
+        pools = _pool_array(states[a:b])
+        counts = (ctypes.c_int64 * (b - a))(*[t.numel() for t in idx[a:b]])
+        ws = _workspace(device, lib.cow_release_workspace_bytes(pools, counts, b - a))
+        _lib.check(lib.cow_release_layers(pools, _ptrs(idx[a:b]), counts, b - a, ws.data_ptr(), ws.numel(),
+                                          released[a:].data_ptr(), stream), "cow_release_layers")
+    return int(released.sum())
 
 
 @torch.no_grad()
 def retain_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> None:
-    """``retain_banks`` on several pools; one host synchronisation.  Nothing
-    changes unless every pool's selection is valid."""
-    pending = [st._retain_launch(idx) for st, idx in zip(states, bank_indices)]
-    if not pending:
+    """``retain_banks`` on several pools: one call per 8 pools, one host
+    synchronisation.  Nothing changes unless every pool's selection is valid."""
+    if len(states) != len(bank_indices):
+        raise ValueError("one bank list per pool")
+    if not states:
         return
-    bits = torch.stack([p[2] for p in pending]).tolist()
-    for b in bits:
-        PackedSDMCopyOnWriteState._retain_check(b)
-    for st, p, b in zip(states, pending, bits):
-        st._retain_commit(p, b)
+    lib = _lib.load()
+    device = states[0].values.device
+    stream = _lib.stream_of(device)
+    idx = [_bank_list(b, st.values.device, "retained") for st, b in zip(states, bank_indices)]
+    maps = [torch.empty(t.numel(), st.slots, device=device, dtype=torch.int32) for st, t in zip(states, idx)]
+    templates = [torch.empty(t.numel(), device=device, dtype=torch.int64) for t in idx]
+    status = torch.empty(len(states), dtype=torch.int32, device=device)
+    for a, b in _chunks(len(states)):
+        pools = _pool_array(states[a:b])
+        counts = (ctypes.c_int64 * (b - a))(*[t.numel() for t in idx[a:b]])
+        ws = _workspace(device, lib.cow_retain_workspace_bytes(pools, b - a))
+        _lib.check(lib.cow_retain_layers(pools, _ptrs(idx[a:b]), counts, b - a, _ptrs(maps[a:b]),
+                                         _ptrs(templates[a:b]), ws.data_ptr(), ws.numel(),
+                                         status[a:].data_ptr(), stream), "cow_retain_layers")
+    bits = status.tolist()
+    for x in bits:
+        PackedSDMCopyOnWriteState._retain_check(x)
+    for st, m, t, x in zip(states, maps, templates, bits):
+        st._retain_commit((m, t, None), x)
 
 
 @torch.no_grad()
 def append_layers(states: Sequence[PackedSDMCopyOnWriteState],
                   others: Sequence[PackedSDMCopyOnWriteState]) -> list[int]:
-    """``append_banks_from`` on several pools; one host synchronisation."""
+    """``append_banks_from`` on several pools: one host synchronisation (plus the
+    slab growth the reference does when a pool lacks free rows)."""
     if len(states) != len(others):
         raise ValueError("one admitted pool per destination pool")
-    scans = [st._append_count(o) for st, o in zip(states, others)]
-    if not scans:
+    if not states:
         return []
-    vals = []
-    for st, scan in zip(states, scans):
-        vals += [scan[0], st.free_count]
-    host, _, _ = _read_counts_and_range(vals, None)
-    return [st._append_apply(o, scan, host[2 * i], host[2 * i + 1])
-            for i, (st, o, scan) in enumerate(zip(states, others, scans))]
+    for st, o in zip(states, others):
+        st._append_check(o)
+    lib = _lib.load()
+    device = states[0].values.device
+    stream = _lib.stream_of(device)
+    admitted = []
+    for a, b in _chunks(len(states)):
+        dst, oth = states[a:b], others[a:b]
+        other_pools = _pool_array(oth)
+        ws = _workspace(device, lib.cow_append_workspace_bytes(other_pools, b - a))
+        counts = torch.empty(2 * (b - a), dtype=torch.int32, device=device)
+        _lib.check(lib.cow_append_count_layers(_pool_array(dst), other_pools, b - a, ws.data_ptr(), ws.numel(),
+                                               counts.data_ptr(), stream), "cow_append_count_layers")
+        host = counts.tolist()
+        frees = []
+        for i, st in enumerate(dst):
+            active, free = host[2 * i], host[2 * i + 1]
+            if free < active:
+                free += st.grow_capacity(st.capacity_rows + active - free)
+            frees.append(free)
+        maps = [torch.empty(o.banks, st.slots, device=device, dtype=torch.int32) for st, o in zip(dst, oth)]
+        _lib.check(lib.cow_append_layers(_pool_array(dst), other_pools, b - a, _ptrs(maps), ws.data_ptr(),
+                                         ws.numel(), stream), "cow_append_layers")
+        for i, (st, o, m) in enumerate(zip(dst, oth, maps)):
+            st._append_commit(o, m, host[2 * i], frees[i])
+            admitted.append(host[2 * i])
+    return admitted
 
 
 @torch.no_grad()
@@ -799,8 +851,8 @@ def from_prefix_routes_layers(
     maximum_future_allocations: int | None = None,
     growth_quantum_rows: int = 0,
 ) -> tuple[list[PackedSDMCopyOnWriteState], list[torch.Tensor]]:
-    """Sparse prefill handoff of several independent pools (``from_prefix_routes``
-    per pool) with one recurrence launch and two host synchronisations.
+    """Sparse prefill handoff of up to 8 independent pools (``from_prefix_routes``
+    per pool) in one set of launches with two host synchronisations.
 
     ``prefixes[l]`` holds pool l's ``write_indices``, ``write_weights``,
     ``values``, ``input_gate``, ``forget_log_gate``, ``read_indices``,
@@ -854,38 +906,38 @@ def from_prefix_routes_layers(
     device = steps[0].widx.device
     stream = _lib.stream_of(device)
     templates = template_indices.to(torch.int64).contiguous()
-    status = torch.zeros(n, device=device, dtype=torch.int32)
-    maps, scans = [], []
-    for l, step in enumerate(steps):
-        mapping = torch.full((banks, slots), -1, device=device, dtype=torch.int32)
-        _lib.check(lib.cow_prefill_mark(step.widx.data_ptr(), step.idx_code, banks, time, writes, slots,
-                                        mapping.data_ptr(), status[l:].data_ptr(), stream), "cow_prefill_mark")
-        scan = _scan_scratch(device, banks * slots)
-        _lib.check(lib.cow_pack_count(mapping.data_ptr(), banks * slots, scan.data_ptr(), stream), "cow_pack_count")
-        maps.append(mapping)
-        scans.append(scan)
-    host, lo, hi = _read_counts_and_range(list(status) + [s[0] for s in scans], templates)
-    for bits in host[:n]:
-        if bits:
-            raise ValueError(_lib.status_text(bits))
+    maps = [torch.empty(banks, slots, device=device, dtype=torch.int32) for _ in range(n)]
+    ws = _workspace(device, lib.cow_pack_workspace_bytes(banks * slots, n))
+    out = torch.empty(2 * n, device=device, dtype=torch.int32)
+    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), idx_code, banks, time, writes,
+                                                 slots, _ptrs(maps), n, ws.data_ptr(), ws.numel(), out.data_ptr(),
+                                                 stream), "cow_prefill_mark_count_layers")
+    host, lo, hi = _read_counts_and_range(list(out), templates)
+    for l in range(n):
+        if host[2 * l]:
+            raise ValueError(_lib.status_text(host[2 * l]))
     _check_template_range(lo, hi, m0s[0])
-    states = [PackedSDMCopyOnWriteState._pack_finish(
-        m0s[l], maps[l], templates, scans[l], host[n + l], capacity_rows=capacity_rows, state_dtype=state_dtype,
-        maximum_future_allocations=maximum_future_allocations, growth_quantum_rows=growth_quantum_rows,
-        row_source=("m0", None)) for l in range(n)]
-    pools = (_lib.CowPool * n)(*[st._pool() for st in states])
+    states = [PackedSDMCopyOnWriteState._pack_state(
+        m0s[l], maps[l], templates, host[2 * l + 1], capacity_rows=capacity_rows, state_dtype=state_dtype,
+        maximum_future_allocations=maximum_future_allocations, growth_quantum_rows=growth_quantum_rows)
+        for l in range(n)]
+    pools = _pool_array(states)
+    _lib.check(lib.cow_pack_apply_layers(pools, n, ws.data_ptr(), ws.numel(), stream), "cow_pack_apply_layers")
     structs = (_lib.CowStep * n)(*[step.struct for step in steps])
     _lib.check(lib.cow_prefill_recurrence_layers(pools, structs, n, time, writes, reads, idx_code, act_code,
                                                  stream), "cow_prefill_recurrence_layers")
-    # Route errors met during the walk are ValueErrors (as in the single-pool
+    # Route errors met during the walk are ValueErrors (as in the reference's
     # prefill); anything else is an invariant failure.
-    vstat = [st._validate_launch() for st in states]
-    flat = torch.stack([torch.stack((st.overflow_flag, b, st.free_count)) for st, b in zip(states, vstat)]).tolist()
-    for flag, _, _ in flat:
-        if flag:
-            raise ValueError(_lib.status_text(flag))
-    for st, row in zip(states, flat):
-        st._validate_result(*row)
+    vws = _workspace(device, lib.cow_validate_workspace_bytes(pools, n))
+    vout = torch.empty(3 * n, device=device, dtype=torch.int32)
+    _lib.check(lib.cow_validate_layers(pools, n, vws.data_ptr(), vws.numel(), vout.data_ptr(), stream),
+               "cow_validate_layers")
+    flat = vout.tolist()
+    for l in range(n):
+        if flat[3 * l]:
+            raise ValueError(_lib.status_text(flat[3 * l]))
+    for l, st in enumerate(states):
+        st._validate_result(*flat[3 * l:3 * l + 3])
     return states, [step.output.reshape(banks, time, width) for step in steps]
 
 

@@ -1,5 +1,10 @@
 // cow_lifecycle.cu -- allocator lifecycle kernels: init, pack, grow, release, repack,
 // append, retain, validate, materialize.
+//
+// Every multi-step operation runs for up to COW_MAX_LAYERS independent pools in
+// one set of launches: grid.y (or grid.x for the one-CTA-per-pool kernels) is
+// the pool, and the per-pool arguments travel in a __grid_constant__ array.
+// The single-pool entry points are the same code with one pool.
 
 #include "cow_common.cuh"
 
@@ -26,10 +31,19 @@ struct ScanCtx {
   int32_t* src_rows;
   int32_t* dst_rows;
   int32_t* free_rows;
-  int32_t* free_count;
+  int32_t* free_count;       // release / append: updated; pack: only read into free_out
   const int32_t* gate_status;  // release: skip everything when the bank list was bad
   int32_t* scratch;            // [0]=total, [1]=old free count, [kScanHeader..] block offsets
+  int32_t* total_out;          // optional copy of the total
+  int32_t* free_out;           // optional copy of the free count before the operation
 };
+
+struct ScanLaunch {
+  ScanCtx c[COW_MAX_LAYERS];
+  int32_t layers;
+};
+
+__host__ __device__ inline int64_t scan_blocks_of(int64_t n) { return (n + kScanSeg - 1) / kScanSeg; }
 
 __device__ __forceinline__ bool scan_flag(const ScanCtx& c, int64_t i) {
   if (c.op == kOpRelease) {
@@ -66,7 +80,10 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int& tot
   return before + x - v;
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_count_kernel(const __grid_constant__ ScanCtx c) {
+// grid (max blocks over pools, pools); a block past its pool's extent exits whole.
+__global__ void __launch_bounds__(kScanThreads) scan_count_kernel(const __grid_constant__ ScanLaunch L) {
+  const ScanCtx& c = L.c[blockIdx.y];
+  if (static_cast<int64_t>(blockIdx.x) >= scan_blocks_of(c.n)) return;
   __shared__ int s_warp[kScanThreads / 32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanSeg + static_cast<int64_t>(threadIdx.x) * kScanItems;
   int cnt = 0;
@@ -80,9 +97,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_count_kernel(const __grid_c
   if (threadIdx.x == 0) c.scratch[kScanHeader + blockIdx.x] = total;
 }
 
-// Single CTA: exclusive scan of the per-block counts, total, and the free
-// count bookkeeping of release (push) / append (pop).
-__global__ void __launch_bounds__(1024) scan_blocks_kernel(const __grid_constant__ ScanCtx c, int64_t nblocks) {
+// One CTA per pool: exclusive scan of the per-block counts, total, and the
+// free count bookkeeping of release (push) / append (pop).
+__global__ void __launch_bounds__(1024) scan_blocks_kernel(const __grid_constant__ ScanLaunch L) {
+  const ScanCtx& c = L.c[blockIdx.x];
+  const int64_t nblocks = scan_blocks_of(c.n);
   __shared__ int s_part[1024];
   const int64_t per = (nblocks + 1023) / 1024;
   const int64_t b0 = threadIdx.x * per;
@@ -105,16 +124,20 @@ __global__ void __launch_bounds__(1024) scan_blocks_kernel(const __grid_constant
   if (threadIdx.x == 1023) {
     const int total = s_part[1023];
     c.scratch[0] = total;
+    if (c.total_out != nullptr) *c.total_out = total;
     if (c.free_count != nullptr) {
       const int old = *c.free_count;
       c.scratch[1] = old;
+      if (c.free_out != nullptr) *c.free_out = old;
       if (c.op == kOpRelease) *c.free_count = old + total;
       if (c.op == kOpAppend) *c.free_count = old - total;
     }
   }
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const __grid_constant__ ScanCtx c) {
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const __grid_constant__ ScanLaunch L) {
+  const ScanCtx& c = L.c[blockIdx.y];
+  if (static_cast<int64_t>(blockIdx.x) >= scan_blocks_of(c.n)) return;
   __shared__ int s_warp[kScanThreads / 32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanSeg + static_cast<int64_t>(threadIdx.x) * kScanItems;
   bool f[kScanItems];
@@ -165,13 +188,88 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const __grid_c
 }
 
 // --------------------------------------------------------------------------
-// small utility kernels
+// per-pool argument arrays of the small kernels
+// --------------------------------------------------------------------------
+
+template <typename T>
+struct Layers {
+  T c[COW_MAX_LAYERS];
+  int32_t layers;
+};
+
+struct FillFreeCtx {  // free_rows[:cap - A] = arange(A, cap), A = *live
+  int32_t* free_rows;
+  int64_t cap;
+  int32_t* free_count;
+  int32_t* status;
+  const int32_t* live;
+};
+
+struct CopyCtx {  // see copy_rows_kernel
+  void* dst;
+  const int32_t* dst_rows;
+  const void* src;
+  const int32_t* src_rows;
+  const int32_t* count_dev;  // when set, rows [*count_dev, count) are skipped
+  const float* m0;
+  const int64_t* templates;
+  int64_t count, width, slots;
+  int32_t dst_dt, src_dt, mode, _pad;
+};
+
+struct MarkCtx {
+  const void* widx;
+  int32_t* map;
+  int32_t* status;
+};
+
+struct BankListCtx {
+  const int64_t* idx;
+  int64_t count, banks;
+  int32_t* mask;
+  int32_t* status;
+};
+
+struct StatusOrCtx {
+  int32_t* status;
+  const int32_t* bits;
+};
+
+struct RetainCtx {
+  const int32_t* map;
+  const int64_t* templates;
+  const int64_t* idx;
+  int64_t count, slots, banks;
+  const int32_t* mask;
+  int32_t* new_map;
+  int64_t* new_templates;
+  int32_t* status;
+};
+
+struct ValidateCtx {
+  const int32_t* map;
+  int64_t map_n, cap;
+  const int32_t* free_rows;
+  const int32_t* free_count;
+  int32_t* counts;
+  int32_t* status;       // validate bits
+  const int32_t* pool_status;
+  int32_t* out;          // [pool status, validate bits, free count]
+};
+
+#define COW_GRID_STRIDE(i, n)                                                                      \
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,                    \
+               i##_stride = static_cast<int64_t>(gridDim.x) * blockDim.x;                          \
+       i < (n); i += i##_stride)
+
+// --------------------------------------------------------------------------
+// small kernels (grid.y = pool)
 // --------------------------------------------------------------------------
 
 __global__ void init_pool_kernel(int32_t* map, int64_t map_n, int32_t* free_rows, int64_t cap,
                                  int32_t* free_count, int32_t* status) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < map_n || i < cap; i += stride) {
+  const int64_t m = map_n > cap ? map_n : cap;
+  COW_GRID_STRIDE(i, m) {
     if (i < map_n) map[i] = -1;
     if (i < cap) free_rows[i] = static_cast<int32_t>(i);
   }
@@ -181,70 +279,66 @@ __global__ void init_pool_kernel(int32_t* map, int64_t map_n, int32_t* free_rows
   }
 }
 
-__global__ void fill_free_kernel(int32_t* free_rows, int64_t cap, int32_t* free_count, int32_t* status,
-                                 const int32_t* scratch) {
-  // free_rows[:cap - A] = arange(A, cap), A = scratch[0] (the live row count)
-  const int64_t a = scratch[0];
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < cap - a; j += stride) {
-    free_rows[j] = static_cast<int32_t>(a + j);
-  }
+__global__ void fill_free_kernel(const __grid_constant__ Layers<FillFreeCtx> L) {
+  const FillFreeCtx& c = L.c[blockIdx.y];
+  const int64_t a = *c.live;
+  COW_GRID_STRIDE(j, c.cap - a) { c.free_rows[j] = static_cast<int32_t>(a + j); }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    *free_count = static_cast<int32_t>(cap - a);
-    if (status != nullptr) *status = 0;
+    *c.free_count = static_cast<int32_t>(c.cap - a);
+    if (c.status != nullptr) *c.status = 0;
   }
 }
 
 __global__ void mask_to_map_kernel(const uint8_t* active, int64_t n, int32_t* map) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
-    map[i] = active[i] ? 0 : -1;
+  COW_GRID_STRIDE(i, n) { map[i] = active[i] ? 0 : -1; }
 }
 
-__global__ void prefill_mark_kernel(const void* widx, int idx64, int64_t banks, int64_t time, int writes,
-                                    int64_t slots, int32_t* map, int32_t* status) {
-  const int64_t n = banks * time * writes;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+__global__ void prefill_mark_kernel(const __grid_constant__ Layers<MarkCtx> L, int idx64, int64_t banks, int64_t time,
+                                    int writes, int64_t slots) {
+  const MarkCtx& c = L.c[blockIdx.y];
+  COW_GRID_STRIDE(i, banks * time * writes) {
     const int64_t bank = i / (time * writes);
-    const int64_t s = ld_index(widx, i, idx64);
+    const int64_t s = ld_index(c.widx, i, idx64);
     if (s < 0 || s >= slots) {
-      atomicOr(status, COW_ST_INDEX_RANGE);
+      atomicOr(c.status, COW_ST_INDEX_RANGE);
       continue;
     }
-    map[bank * slots + s] = 0;
+    c.map[bank * slots + s] = 0;
   }
 }
 
-// One warp per row; 16-byte vectors when both dtypes allow it.
-__global__ void copy_rows_kernel(void* dst, int dst_dt, const int32_t* dst_rows, const void* src, int src_dt,
-                                 const int32_t* src_rows, int64_t count, int64_t width, int mode,
-                                 const float* m0, const int64_t* templates, int64_t slots) {
+// One warp per row; 16-byte vectors when both dtypes allow it.  mode 0: row
+// src_rows[k] of src; mode 1: src_rows[k] is a flat bank*slots+slot index and
+// the row comes from m0[templates[bank], slot].
+__global__ void copy_rows_kernel(const __grid_constant__ Layers<CopyCtx> L) {
+  const CopyCtx& c = L.c[blockIdx.y];
   const int lane = threadIdx.x & 31;
+  const int64_t count = c.count_dev != nullptr ? min(c.count, static_cast<int64_t>(*c.count_dev)) : c.count;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t width = c.width;
   for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); k < count; k += warps) {
-    const int64_t d = dst_rows ? dst_rows[k] : k;
-    const void* sbase = src;
-    int sdt = src_dt;
+    const int64_t d = c.dst_rows ? c.dst_rows[k] : k;
+    const void* sbase = c.src;
+    int sdt = c.src_dt;
     int64_t s;
-    if (mode == 1) {
-      const int64_t flat = src_rows[k];
-      s = templates[flat / slots] * slots + flat % slots;
-      sbase = m0;
+    if (c.mode == 1) {
+      const int64_t flat = c.src_rows[k];
+      s = c.templates[flat / c.slots] * c.slots + flat % c.slots;
+      sbase = c.m0;
       sdt = COW_F32;
     } else {
-      s = src_rows ? src_rows[k] : k;
+      s = c.src_rows ? c.src_rows[k] : k;
     }
     if ((width & 3) == 0) {
       for (int64_t e = lane * 4; e < width; e += 128) {
-        st4_rt(dst, d * width + e, ld4_rt(sbase, s * width + e, sdt), dst_dt);
+        st4_rt(c.dst, d * width + e, ld4_rt(sbase, s * width + e, sdt), c.dst_dt);
       }
     } else {
       for (int64_t e = lane; e < width; e += 32) {
         const float v = ld1_rt(sbase, s * width + e, sdt);
-        if (dst_dt == COW_F32) static_cast<float*>(dst)[d * width + e] = v;
-        else if (dst_dt == COW_BF16) static_cast<__nv_bfloat16*>(dst)[d * width + e] = __float2bfloat16_rn(v);
-        else static_cast<__half*>(dst)[d * width + e] = __float2half_rn(v);
+        if (c.dst_dt == COW_F32) static_cast<float*>(c.dst)[d * width + e] = v;
+        else if (c.dst_dt == COW_BF16) static_cast<__nv_bfloat16*>(c.dst)[d * width + e] = __float2bfloat16_rn(v);
+        else static_cast<__half*>(c.dst)[d * width + e] = __float2half_rn(v);
       }
     }
   }
@@ -255,21 +349,19 @@ __global__ void grow_kernel(const void* old_slab, const int32_t* old_free_rows, 
                             int32_t* status) {
   // Byte copy of the old slab (16-byte words; row_bytes*old_cap is a multiple
   // of 16 whenever width*elem is), then the free stack.
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t bytes = row_bytes * old_cap;
   if ((bytes & 15) == 0) {
     const int4* s = static_cast<const int4*>(old_slab);
     int4* d = static_cast<int4*>(new_slab);
-    for (int64_t i = tid; i < bytes / 16; i += stride) d[i] = s[i];
+    COW_GRID_STRIDE(i, bytes / 16) { d[i] = s[i]; }
   } else {
     const uint8_t* s = static_cast<const uint8_t*>(old_slab);
     uint8_t* d = static_cast<uint8_t*>(new_slab);
-    for (int64_t i = tid; i < bytes; i += stride) d[i] = s[i];
+    COW_GRID_STRIDE(i, bytes) { d[i] = s[i]; }
   }
   const int64_t old_free = *free_count;
   const int64_t added = new_cap - old_cap;
-  for (int64_t i = tid; i < old_free + added; i += stride) {
+  COW_GRID_STRIDE(i, old_free + added) {
     new_free_rows[i] = i < old_free ? old_free_rows[i] : static_cast<int32_t>(old_cap + (i - old_free));
   }
 }
@@ -279,79 +371,89 @@ __global__ void grow_finish_kernel(int32_t* free_count, int64_t added, int32_t* 
   *status = 0;
 }
 
-__global__ void bank_list_kernel(const int64_t* idx, int64_t count, int64_t banks, int32_t* mask, int32_t* status) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < count; s += stride) {
-    const int64_t b = idx[s];
-    if (b < 0 || b >= banks) {
-      atomicOr(status, COW_ST_BAD_BANK_LIST);
+__global__ void bank_list_kernel(const __grid_constant__ Layers<BankListCtx> L) {
+  const BankListCtx& c = L.c[blockIdx.y];
+  COW_GRID_STRIDE(s, c.count) {
+    const int64_t b = c.idx[s];
+    if (b < 0 || b >= c.banks) {
+      atomicOr(c.status, COW_ST_BAD_BANK_LIST);
       continue;
     }
-    if (atomicAdd(&mask[b], 1) != 0) atomicOr(status, COW_ST_BAD_BANK_LIST);
+    if (atomicAdd(&c.mask[b], 1) != 0) atomicOr(c.status, COW_ST_BAD_BANK_LIST);
   }
 }
 
-__global__ void status_or_kernel(int32_t* status, const int32_t* bits) { atomicOr(status, *bits); }
+__global__ void status_or_kernel(const __grid_constant__ Layers<StatusOrCtx> L) {
+  const StatusOrCtx& c = L.c[blockIdx.y];
+  if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(c.status, *c.bits);
+}
 
-__global__ void retain_check_kernel(const int32_t* map, int64_t banks, int64_t slots, const int32_t* mask,
-                                    int32_t* status) {
-  const int64_t n = banks * slots;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
-    if (map[i] >= 0 && mask[i / slots] == 0) atomicOr(status, COW_ST_DISCARD_LIVE);
+__global__ void retain_check_kernel(const __grid_constant__ Layers<RetainCtx> L) {
+  const RetainCtx& c = L.c[blockIdx.y];
+  COW_GRID_STRIDE(i, c.banks * c.slots) {
+    if (c.map[i] >= 0 && c.mask[i / c.slots] == 0) atomicOr(c.status, COW_ST_DISCARD_LIVE);
   }
 }
 
-__global__ void retain_gather_kernel(const int32_t* map, const int64_t* templates, const int64_t* idx, int64_t count,
-                                     int64_t slots, int64_t banks, int32_t* new_map, int64_t* new_templates) {
-  const int64_t n = count * slots;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
-    const int64_t s = i / slots;
-    int64_t b = idx[s];
-    b = b < 0 ? 0 : (b >= banks ? banks - 1 : b);
-    new_map[i] = map[b * slots + i % slots];
-    if (i % slots == 0) new_templates[s] = templates[b];
+__global__ void retain_gather_kernel(const __grid_constant__ Layers<RetainCtx> L) {
+  const RetainCtx& c = L.c[blockIdx.y];
+  if (c.banks == 0) return;
+  COW_GRID_STRIDE(i, c.count * c.slots) {
+    const int64_t s = i / c.slots;
+    int64_t b = c.idx[s];
+    b = b < 0 ? 0 : (b >= c.banks ? c.banks - 1 : b);
+    c.new_map[i] = c.map[b * c.slots + i % c.slots];
+    if (i % c.slots == 0) c.new_templates[s] = c.templates[b];
   }
 }
 
-__global__ void validate_count_kernel(const int32_t* map, int64_t map_n, const int32_t* free_rows,
-                                      const int32_t* free_count, int64_t cap, int32_t* counts, int32_t* status) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t fc = *free_count;
-  if (blockIdx.x == 0 && threadIdx.x == 0 && (fc < 0 || fc > cap)) atomicOr(status, COW_ST_ROW_RANGE);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < map_n; i += stride) {
-    const int32_t v = map[i];
+__global__ void validate_count_kernel(const __grid_constant__ Layers<ValidateCtx> L) {
+  const ValidateCtx& c = L.c[blockIdx.y];
+  const int64_t fc = *c.free_count;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && (fc < 0 || fc > c.cap)) atomicOr(c.status, COW_ST_ROW_RANGE);
+  COW_GRID_STRIDE(i, c.map_n) {
+    const int32_t v = c.map[i];
     if (v < 0) continue;
-    if (v >= cap) {
-      atomicOr(status, COW_ST_ROW_RANGE);
+    if (v >= c.cap) {
+      atomicOr(c.status, COW_ST_ROW_RANGE);
       continue;
     }
-    atomicAdd(&counts[v], 1);
+    atomicAdd(&c.counts[v], 1);
   }
-  const int64_t fcl = fc < 0 ? 0 : (fc > cap ? cap : fc);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < fcl; i += stride) {
-    const int32_t v = free_rows[i];
-    if (v < 0 || v >= cap) {
-      atomicOr(status, COW_ST_ROW_RANGE);
+  const int64_t fcl = fc < 0 ? 0 : (fc > c.cap ? c.cap : fc);
+  COW_GRID_STRIDE(i, fcl) {
+    const int32_t v = c.free_rows[i];
+    if (v < 0 || v >= c.cap) {
+      atomicOr(c.status, COW_ST_ROW_RANGE);
       continue;
     }
-    atomicAdd(&counts[v], 1 << 16);
+    atomicAdd(&c.counts[v], 1 << 16);
   }
 }
 
-__global__ void validate_check_kernel(const int32_t* counts, int64_t cap, int32_t* status) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+__global__ void validate_check_kernel(const __grid_constant__ Layers<ValidateCtx> L) {
+  const ValidateCtx& c = L.c[blockIdx.y];
   int bits = 0;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < cap; i += stride) {
-    const int c = counts[i];
-    const int a = c & 0xffff, f = c >> 16;
+  COW_GRID_STRIDE(i, c.cap) {
+    const int v = c.counts[i];
+    const int a = v & 0xffff, f = v >> 16;
     if (a > 1) bits |= COW_ST_MULTI_OWNER;
     if (f > 1) bits |= COW_ST_FREE_DUPLICATE;
     if (a + f == 0) bits |= COW_ST_NOT_COVERED;
     if (a >= 1 && f >= 1) bits |= COW_ST_NOT_COVERED;
   }
-  if (bits) atomicOr(status, bits);
+  if (bits) atomicOr(c.status, bits);
+}
+
+// After the checks: [pool status, validate bits, free count] per pool.
+__global__ void validate_report_kernel(const __grid_constant__ Layers<ValidateCtx> L) {
+  if (threadIdx.x >= L.layers) return;
+  const ValidateCtx& c = L.c[threadIdx.x];
+  if (c.out != nullptr) {
+    c.out[0] = *c.pool_status;
+    c.out[1] = *c.status;
+    c.out[2] = *c.free_count;
+  }
 }
 
 __global__ void materialize_kernel(const float* m0, const int64_t* templates, const void* slab, int slab_dt,
@@ -371,28 +473,70 @@ __global__ void materialize_kernel(const float* m0, const int64_t* templates, co
   }
 }
 
-int run_scan_count(ScanCtx& c, cudaStream_t st) {
-  const int64_t nb = (c.n + kScanSeg - 1) / kScanSeg;
+// --------------------------------------------------------------------------
+// launch helpers
+// --------------------------------------------------------------------------
+
+dim3 layer_grid(int64_t max_n, int threads, int layers) {
+  return dim3(static_cast<unsigned>(grid_for(max_n, threads)), static_cast<unsigned>(layers));
+}
+
+int run_scan_count(const ScanLaunch& L, cudaStream_t st) {
+  int64_t nb = 0;
+  for (int l = 0; l < L.layers; ++l) nb = std::max<int64_t>(nb, scan_blocks_of(L.c[l].n));
   if (nb > 0) {
-    scan_count_kernel<<<static_cast<unsigned>(nb), kScanThreads, 0, st>>>(c);
+    scan_count_kernel<<<dim3(static_cast<unsigned>(nb), L.layers), kScanThreads, 0, st>>>(L);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
-  scan_blocks_kernel<<<1, 1024, 0, st>>>(c, nb);
+  scan_blocks_kernel<<<L.layers, 1024, 0, st>>>(L);
   return launch_status();
 }
 
-int run_scan_apply(ScanCtx& c, cudaStream_t st) {
-  const int64_t nb = (c.n + kScanSeg - 1) / kScanSeg;
+int run_scan_apply(const ScanLaunch& L, cudaStream_t st) {
+  int64_t nb = 0;
+  for (int l = 0; l < L.layers; ++l) nb = std::max<int64_t>(nb, scan_blocks_of(L.c[l].n));
   if (nb == 0) return COW_OK;
-  scan_apply_kernel<<<static_cast<unsigned>(nb), kScanThreads, 0, st>>>(c);
+  scan_apply_kernel<<<dim3(static_cast<unsigned>(nb), L.layers), kScanThreads, 0, st>>>(L);
   return launch_status();
+}
+
+int run_copy_rows(const Layers<CopyCtx>& L, cudaStream_t st) {
+  int64_t m = 0;
+  for (int l = 0; l < L.layers; ++l) m = std::max<int64_t>(m, L.c[l].count);
+  if (m == 0) return COW_OK;
+  copy_rows_kernel<<<layer_grid(m * 32, 256, L.layers), 256, 0, st>>>(L);
+  return launch_status();
+}
+
+bool copy_args_ok(const CopyCtx& c) {
+  if (c.count == 0) return true;
+  if (!c.dst || c.count < 0 || c.width < 1 || !valid_dtype(c.dst_dt)) return false;
+  if (c.mode == 1)
+    return c.m0 && c.templates && c.src_rows && c.slots >= 1 && c.width % 4 == 0 && aligned16(c.m0);
+  if (c.mode != 0 || !c.src || !valid_dtype(c.src_dt)) return false;
+  return c.width % 4 != 0 || (row_aligned(c.src, c.src_dt) && row_aligned(c.dst, c.dst_dt));
+}
+
+// Workspace layouts, in int32 words, every region rounded up to 16 bytes.
+inline int64_t words16(int64_t words) { return (words + 3) / 4 * 4; }
+inline int64_t scan_words(int64_t n) { return words16(scan_blocks_of(n) + kScanHeader); }
+
+bool layers_ok(const cow_pool* pools, int32_t layers) {
+  if (!pools || layers < 1 || layers > COW_MAX_LAYERS) return false;
+  for (int l = 0; l < layers; ++l)
+    if (pools[l].banks < 0 || pools[l].slots < 1 || pools[l].capacity < 0) return false;
+  return true;
+}
+
+bool workspace_ok(const void* ws, int64_t have, int64_t need) {
+  return ws != nullptr && aligned16(ws) && have >= need;
 }
 
 }  // namespace
 
 extern "C" {
 
-int64_t cow_scan_blocks(int64_t n) { return (n + kScanSeg - 1) / kScanSeg + kScanHeader; }
+int64_t cow_scan_blocks(int64_t n) { return scan_blocks_of(n) + kScanHeader; }
 
 int cow_init_pool(const cow_pool* p, void* stream) {
   if (!p || !p->map || !p->free_rows || !p->free_count || !p->status || p->capacity < 0 || p->banks < 0)
@@ -409,8 +553,11 @@ int cow_prefill_mark(const void* write_indices, int32_t index_dtype, int64_t ban
   if (!write_indices || !map || !status || banks < 0 || time < 0 || writes < 1 || slots < 1) return COW_ERR_INVALID;
   const int64_t n = banks * time * writes;
   if (n == 0) return COW_OK;
-  prefill_mark_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(write_indices, index_dtype == COW_I64, banks,
-                                                                      time, writes, slots, map, status);
+  Layers<MarkCtx> L{};
+  L.c[0] = MarkCtx{write_indices, map, status};
+  L.layers = 1;
+  prefill_mark_kernel<<<layer_grid(n, 256, 1), 256, 0, as_stream(stream)>>>(L, index_dtype == COW_I64, banks, time,
+                                                                         writes, slots);
   return launch_status();
 }
 
@@ -423,19 +570,23 @@ int cow_mask_to_map(const uint8_t* active, int64_t n, int32_t* map, void* stream
 
 int cow_pack_count(const int32_t* map, int64_t n, int32_t* flags_scratch, void* stream) {
   if ((!map && n > 0) || !flags_scratch || n < 0) return COW_ERR_INVALID;
-  ScanCtx c{};
+  ScanLaunch L{};
+  L.layers = 1;
+  ScanCtx& c = L.c[0];
   c.op = kOpPack;
   c.n = n;
   c.slots = 1;
   c.map = map;
   c.scratch = flags_scratch;
-  return run_scan_count(c, as_stream(stream));
+  return run_scan_count(L, as_stream(stream));
 }
 
 int cow_pack_apply(int32_t* map, int64_t n, int32_t* src_index, const cow_pool* pool, int32_t* flags_scratch,
                    void* stream) {
   if ((!map && n > 0) || !pool || !flags_scratch || !src_index) return COW_ERR_INVALID;
-  ScanCtx c{};
+  ScanLaunch L{};
+  L.layers = 1;
+  ScanCtx& c = L.c[0];
   c.op = kOpPack;
   c.n = n;
   c.slots = 1;
@@ -444,29 +595,24 @@ int cow_pack_apply(int32_t* map, int64_t n, int32_t* src_index, const cow_pool* 
   c.src_rows = src_index;
   c.scratch = flags_scratch;
   cudaStream_t st = as_stream(stream);
-  int rc = run_scan_apply(c, st);
+  int rc = run_scan_apply(L, st);
   if (rc != COW_OK) return rc;
-  fill_free_kernel<<<grid_for(pool->capacity, 256), 256, 0, st>>>(pool->free_rows, pool->capacity,
-                                                                 pool->free_count, pool->status, flags_scratch);
+  Layers<FillFreeCtx> F{};
+  F.c[0] = FillFreeCtx{pool->free_rows, pool->capacity, pool->free_count, pool->status, flags_scratch};
+  F.layers = 1;
+  fill_free_kernel<<<layer_grid(pool->capacity, 256, 1), 256, 0, st>>>(F);
   return launch_status();
 }
 
 int cow_copy_rows(void* dst, int32_t dst_dtype, const int32_t* dst_rows, const void* src, int32_t src_dtype,
                   const int32_t* src_rows, int64_t count, int64_t width, int32_t mode, const float* m0,
                   const int64_t* templates, int64_t slots, void* stream) {
-  if (count == 0) return COW_OK;
-  if (!dst || count < 0 || width < 1 || !valid_dtype(dst_dtype)) return COW_ERR_INVALID;
-  if (mode == 1) {
-    if (!m0 || !templates || !src_rows || slots < 1 || width % 4 != 0 || !aligned16(m0)) return COW_ERR_INVALID;
-  } else if (mode == 0) {
-    if (!src || !valid_dtype(src_dtype)) return COW_ERR_INVALID;
-    if (width % 4 == 0 && (!row_aligned(src, src_dtype) || !row_aligned(dst, dst_dtype))) return COW_ERR_INVALID;
-  } else {
-    return COW_ERR_INVALID;
-  }
-  copy_rows_kernel<<<grid_for(count * 32, 256), 256, 0, as_stream(stream)>>>(
-      dst, dst_dtype, dst_rows, src, src_dtype, src_rows, count, width, mode, m0, templates, slots);
-  return launch_status();
+  Layers<CopyCtx> L{};
+  L.c[0] = CopyCtx{dst, dst_rows, src, src_rows, nullptr, m0, templates, count, width, slots,
+                   dst_dtype, src_dtype, mode, 0};
+  L.layers = 1;
+  if (!copy_args_ok(L.c[0])) return COW_ERR_INVALID;
+  return run_copy_rows(L, as_stream(stream));
 }
 
 int cow_grow(const void* old_slab, const int32_t* old_free_rows, int64_t old_capacity, void* new_slab,
@@ -485,6 +631,65 @@ int cow_grow(const void* old_slab, const int32_t* old_free_rows, int64_t old_cap
   return launch_status();
 }
 
+// ---- release ---------------------------------------------------------------
+
+int64_t cow_release_workspace_bytes(const cow_pool* pools, const int64_t* counts, int32_t layers) {
+  if (!layers_ok(pools, layers) || !counts) return -1;
+  int64_t words = 0;
+  for (int l = 0; l < layers; ++l)
+    words += words16(pools[l].banks > 0 ? pools[l].banks : 1) + scan_words(counts[l] * pools[l].slots);
+  return words * 4;
+}
+
+int cow_release_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts,
+                       int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* released, void* stream) {
+  if (!layers_ok(pools, layers) || !bank_indices || !counts || !released) return COW_ERR_INVALID;
+  const int64_t need = cow_release_workspace_bytes(pools, counts, layers);
+  if (!workspace_ok(workspace, workspace_bytes, need)) return COW_ERR_INVALID;
+  for (int l = 0; l < layers; ++l)
+    if (counts[l] < 0 || (counts[l] > 0 && !bank_indices[l])) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  // Zero the masks and scan headers; flags[2] of each pool gates its release
+  // (a bad bank list releases nothing).
+  if (cudaMemsetAsync(workspace, 0, static_cast<size_t>(need), st) != cudaSuccess) return COW_ERR_CUDA;
+  Layers<BankListCtx> B{};
+  Layers<StatusOrCtx> S{};
+  ScanLaunch C{};
+  B.layers = S.layers = C.layers = layers;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  int64_t max_count = 0;
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& p = pools[l];
+    int32_t* mask = w;
+    w += words16(p.banks > 0 ? p.banks : 1);
+    int32_t* flags = w;
+    w += scan_words(counts[l] * p.slots);
+    B.c[l] = BankListCtx{bank_indices[l], counts[l], p.banks, mask, flags + 2};
+    S.c[l] = StatusOrCtx{p.status, flags + 2};
+    ScanCtx& c = C.c[l];
+    c.op = kOpRelease;
+    c.n = counts[l] * p.slots;
+    c.slots = p.slots;
+    c.bank_idx = bank_indices[l];
+    c.pool_map = p.map;
+    c.free_rows = p.free_rows;
+    c.free_count = p.free_count;
+    c.gate_status = flags + 2;
+    c.scratch = flags;
+    c.total_out = released + l;
+    max_count = std::max(max_count, counts[l]);
+  }
+  if (max_count > 0) {
+    bank_list_kernel<<<layer_grid(max_count, 256, layers), 256, 0, st>>>(B);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+    status_or_kernel<<<dim3(1, layers), 32, 0, st>>>(S);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  }
+  int rc = run_scan_count(C, st);
+  if (rc != COW_OK) return rc;
+  return run_scan_apply(C, st);
+}
+
 int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count, int32_t* bank_mask,
                 int32_t* flags_scratch, int32_t* released, void* stream) {
   if (!pool || !bank_mask || !flags_scratch || !released || count < 0 || (count > 0 && !bank_indices))
@@ -493,15 +698,21 @@ int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count
   if (cudaMemsetAsync(bank_mask, 0, sizeof(int32_t) * (pool->banks > 0 ? pool->banks : 1), st) != cudaSuccess ||
       cudaMemsetAsync(flags_scratch, 0, sizeof(int32_t) * kScanHeader, st) != cudaSuccess)
     return COW_ERR_CUDA;
-  // flags_scratch[2] gates the release: a bad bank list releases nothing.
   if (count > 0) {
-    bank_list_kernel<<<grid_for(count, 256), 256, 0, st>>>(bank_indices, count, pool->banks, bank_mask,
-                                                         flags_scratch + 2);
+    Layers<BankListCtx> B{};
+    B.c[0] = BankListCtx{bank_indices, count, pool->banks, bank_mask, flags_scratch + 2};
+    B.layers = 1;
+    bank_list_kernel<<<layer_grid(count, 256, 1), 256, 0, st>>>(B);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
-    status_or_kernel<<<1, 1, 0, st>>>(pool->status, flags_scratch + 2);
+    Layers<StatusOrCtx> S{};
+    S.c[0] = StatusOrCtx{pool->status, flags_scratch + 2};
+    S.layers = 1;
+    status_or_kernel<<<1, 32, 0, st>>>(S);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
-  ScanCtx c{};
+  ScanLaunch C{};
+  C.layers = 1;
+  ScanCtx& c = C.c[0];
   c.op = kOpRelease;
   c.n = count * pool->slots;
   c.slots = pool->slots;
@@ -511,20 +722,21 @@ int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count
   c.free_count = pool->free_count;
   c.gate_status = flags_scratch + 2;
   c.scratch = flags_scratch;
-  int rc = run_scan_count(c, st);
+  c.total_out = released;
+  int rc = run_scan_count(C, st);
   if (rc != COW_OK) return rc;
-  rc = run_scan_apply(c, st);
-  if (rc != COW_OK) return rc;
-  return cudaMemcpyAsync(released, flags_scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) == cudaSuccess
-             ? COW_OK
-             : COW_ERR_CUDA;
+  return run_scan_apply(C, st);
 }
+
+// ---- trim ------------------------------------------------------------------
 
 int cow_repack(const cow_pool* pool, int32_t* new_map, void* new_slab, int32_t* new_free_rows, int64_t new_capacity,
                int32_t* src_rows, int32_t* flags_scratch, void* stream) {
   if (!pool || !new_map || !new_slab || !new_free_rows || !src_rows || !flags_scratch) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
-  ScanCtx c{};
+  ScanLaunch C{};
+  C.layers = 1;
+  ScanCtx& c = C.c[0];
   c.op = kOpRepack;
   c.n = pool->banks * pool->slots;
   c.slots = pool->slots;
@@ -532,18 +744,24 @@ int cow_repack(const cow_pool* pool, int32_t* new_map, void* new_slab, int32_t* 
   c.out_map = new_map;
   c.src_rows = src_rows;
   c.scratch = flags_scratch;
-  int rc = run_scan_apply(c, st);
+  int rc = run_scan_apply(C, st);
   if (rc != COW_OK) return rc;
-  fill_free_kernel<<<grid_for(new_capacity, 256), 256, 0, st>>>(new_free_rows, new_capacity, pool->free_count,
-                                                               pool->status, flags_scratch);
+  Layers<FillFreeCtx> F{};
+  F.c[0] = FillFreeCtx{new_free_rows, new_capacity, pool->free_count, pool->status, flags_scratch};
+  F.layers = 1;
+  fill_free_kernel<<<layer_grid(new_capacity, 256, 1), 256, 0, st>>>(F);
   return launch_status();
 }
+
+// ---- admission ---------------------------------------------------------------
 
 int cow_append(const cow_pool* dst, const cow_pool* other, int32_t* admitted_map, int32_t* src_rows,
                int32_t* dst_rows, int32_t* flags_scratch, void* stream) {
   if (!dst || !other || !admitted_map || !src_rows || !dst_rows || !flags_scratch) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
-  ScanCtx c{};
+  ScanLaunch C{};
+  C.layers = 1;
+  ScanCtx& c = C.c[0];
   c.op = kOpAppend;
   c.n = other->banks * other->slots;
   c.slots = other->slots;
@@ -556,10 +774,88 @@ int cow_append(const cow_pool* dst, const cow_pool* other, int32_t* admitted_map
   c.scratch = flags_scratch;
   // The count phase (run by the caller through cow_pack_count) did not touch
   // free_count; redo it here with the append bookkeeping.
-  int rc = run_scan_count(c, st);
+  int rc = run_scan_count(C, st);
   if (rc != COW_OK) return rc;
-  return run_scan_apply(c, st);
+  return run_scan_apply(C, st);
 }
+
+int64_t cow_append_workspace_bytes(const cow_pool* others, int32_t layers) {
+  if (!layers_ok(others, layers)) return -1;
+  int64_t words = 0;
+  for (int l = 0; l < layers; ++l) {
+    const int64_t n = others[l].banks * others[l].slots;
+    words += scan_words(n) + 2 * words16(n > 0 ? n : 1);
+  }
+  return words * 4;
+}
+
+int cow_append_count_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, void* workspace,
+                            int64_t workspace_bytes, int32_t* counts, void* stream) {
+  if (!layers_ok(dsts, layers) || !layers_ok(others, layers) || !counts) return COW_ERR_INVALID;
+  if (!workspace_ok(workspace, workspace_bytes, cow_append_workspace_bytes(others, layers))) return COW_ERR_INVALID;
+  ScanLaunch C{};
+  C.layers = layers;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  for (int l = 0; l < layers; ++l) {
+    const int64_t n = others[l].banks * others[l].slots;
+    if (!dsts[l].free_count || (n > 0 && !others[l].map)) return COW_ERR_INVALID;
+    ScanCtx& c = C.c[l];
+    c.op = kOpPack;  // counting only; free_count is read, not changed
+    c.n = n;
+    c.slots = others[l].slots;
+    c.map = others[l].map;
+    c.free_count = dsts[l].free_count;
+    c.scratch = w;
+    c.total_out = counts + 2 * l;
+    c.free_out = counts + 2 * l + 1;
+    w += scan_words(n) + 2 * words16(n > 0 ? n : 1);
+  }
+  return run_scan_count(C, as_stream(stream));
+}
+
+int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, int32_t* const* admitted_maps,
+                      void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!layers_ok(dsts, layers) || !layers_ok(others, layers) || !admitted_maps) return COW_ERR_INVALID;
+  if (!workspace_ok(workspace, workspace_bytes, cow_append_workspace_bytes(others, layers))) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  ScanLaunch C{};
+  Layers<CopyCtx> K{};
+  C.layers = K.layers = layers;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& d = dsts[l];
+    const cow_pool& o = others[l];
+    const int64_t n = o.banks * o.slots;
+    if (o.slots != d.slots || o.width != d.width || o.slab_dtype != d.slab_dtype || !d.free_rows ||
+        !d.free_count || !d.slab || (n > 0 && (!o.map || !o.slab || !admitted_maps[l])))
+      return COW_ERR_INVALID;
+    int32_t* flags = w;
+    int32_t* src_rows = flags + scan_words(n);
+    int32_t* dst_rows = src_rows + words16(n > 0 ? n : 1);
+    w = dst_rows + words16(n > 0 ? n : 1);
+    ScanCtx& c = C.c[l];
+    c.op = kOpAppend;
+    c.n = n;
+    c.slots = o.slots;
+    c.map = o.map;
+    c.out_map = admitted_maps[l];
+    c.src_rows = src_rows;
+    c.dst_rows = dst_rows;
+    c.free_rows = d.free_rows;
+    c.free_count = d.free_count;
+    c.scratch = flags;
+    K.c[l] = CopyCtx{d.slab, dst_rows, o.slab, src_rows, flags, nullptr, nullptr, n, d.width, d.slots,
+                     d.slab_dtype, o.slab_dtype, 0, 0};
+    if (!copy_args_ok(K.c[l])) return COW_ERR_INVALID;
+  }
+  int rc = run_scan_count(C, st);
+  if (rc != COW_OK) return rc;
+  rc = run_scan_apply(C, st);
+  if (rc != COW_OK) return rc;
+  return run_copy_rows(K, st);
+}
+
+// ---- compaction --------------------------------------------------------------
 
 int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count, int32_t* new_map,
                int64_t* new_templates, int32_t* selected, int32_t* status, void* stream) {
@@ -568,22 +864,158 @@ int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count,
   cudaStream_t st = as_stream(stream);
   if (cudaMemsetAsync(selected, 0, sizeof(int32_t) * (pool->banks > 0 ? pool->banks : 1), st) != cudaSuccess)
     return COW_ERR_CUDA;
+  Layers<BankListCtx> B{};
+  Layers<RetainCtx> R{};
+  B.layers = R.layers = 1;
+  B.c[0] = BankListCtx{bank_indices, count, pool->banks, selected, status};
+  R.c[0] = RetainCtx{pool->map, pool->templates, bank_indices, count, pool->slots, pool->banks, selected,
+                     new_map, new_templates, status};
   if (count > 0) {
-    bank_list_kernel<<<grid_for(count, 256), 256, 0, st>>>(bank_indices, count, pool->banks, selected, status);
+    bank_list_kernel<<<layer_grid(count, 256, 1), 256, 0, st>>>(B);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
-  const int64_t n = pool->banks * pool->slots;
-  if (n > 0) {
-    retain_check_kernel<<<grid_for(n, 256), 256, 0, st>>>(pool->map, pool->banks, pool->slots, selected, status);
+  if (pool->banks * pool->slots > 0) {
+    retain_check_kernel<<<layer_grid(pool->banks * pool->slots, 256, 1), 256, 0, st>>>(R);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   if (count > 0 && pool->banks > 0) {
-    retain_gather_kernel<<<grid_for(count * pool->slots, 256), 256, 0, st>>>(
-        pool->map, pool->templates, bank_indices, count, pool->slots, pool->banks, new_map, new_templates);
+    retain_gather_kernel<<<layer_grid(count * pool->slots, 256, 1), 256, 0, st>>>(R);
     return launch_status();
   }
   return COW_OK;
 }
+
+int64_t cow_retain_workspace_bytes(const cow_pool* pools, int32_t layers) {
+  if (!layers_ok(pools, layers)) return -1;
+  int64_t words = 0;
+  for (int l = 0; l < layers; ++l) words += words16(pools[l].banks > 0 ? pools[l].banks : 1);
+  return words * 4;
+}
+
+int cow_retain_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts, int32_t layers,
+                      int32_t* const* new_maps, int64_t* const* new_templates, void* workspace,
+                      int64_t workspace_bytes, int32_t* status, void* stream) {
+  if (!layers_ok(pools, layers) || !bank_indices || !counts || !new_maps || !new_templates || !status)
+    return COW_ERR_INVALID;
+  const int64_t need = cow_retain_workspace_bytes(pools, layers);
+  if (!workspace_ok(workspace, workspace_bytes, need)) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  if (cudaMemsetAsync(workspace, 0, static_cast<size_t>(need), st) != cudaSuccess ||
+      cudaMemsetAsync(status, 0, sizeof(int32_t) * layers, st) != cudaSuccess)
+    return COW_ERR_CUDA;
+  Layers<BankListCtx> B{};
+  Layers<RetainCtx> R{};
+  B.layers = R.layers = layers;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  int64_t max_count = 0, max_map = 0, max_gather = 0;
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& p = pools[l];
+    const int64_t cnt = counts[l];
+    if (cnt < 0 || (cnt > 0 && (!bank_indices[l] || !new_maps[l] || !new_templates[l]))) return COW_ERR_INVALID;
+    B.c[l] = BankListCtx{bank_indices[l], cnt, p.banks, w, status + l};
+    R.c[l] = RetainCtx{p.map, p.templates, bank_indices[l], cnt, p.slots, p.banks, w, new_maps[l],
+                       new_templates[l], status + l};
+    w += words16(p.banks > 0 ? p.banks : 1);
+    max_count = std::max(max_count, cnt);
+    max_map = std::max(max_map, p.banks * p.slots);
+    if (p.banks > 0) max_gather = std::max(max_gather, cnt * p.slots);
+  }
+  if (max_count > 0) {
+    bank_list_kernel<<<layer_grid(max_count, 256, layers), 256, 0, st>>>(B);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  }
+  if (max_map > 0) {
+    retain_check_kernel<<<layer_grid(max_map, 256, layers), 256, 0, st>>>(R);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  }
+  if (max_gather > 0) {
+    retain_gather_kernel<<<layer_grid(max_gather, 256, layers), 256, 0, st>>>(R);
+    return launch_status();
+  }
+  return COW_OK;
+}
+
+// ---- prefill packing ---------------------------------------------------------
+
+int64_t cow_pack_workspace_bytes(int64_t n, int32_t layers) {
+  if (n < 0 || layers < 1 || layers > COW_MAX_LAYERS) return -1;
+  return (scan_words(n) + words16(n > 0 ? n : 1)) * 4 * static_cast<int64_t>(layers);
+}
+
+int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t index_dtype, int64_t banks, int64_t time,
+                                  int32_t writes, int64_t slots, int32_t* const* maps, int32_t layers,
+                                  void* workspace, int64_t workspace_bytes, int32_t* out, void* stream) {
+  if (!write_indices || !maps || !out || layers < 1 || layers > COW_MAX_LAYERS || banks < 0 || time < 0 ||
+      writes < 1 || slots < 1)
+    return COW_ERR_INVALID;
+  const int64_t n = banks * slots;
+  if (!workspace_ok(workspace, workspace_bytes, cow_pack_workspace_bytes(n, layers))) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  if (cudaMemsetAsync(out, 0, sizeof(int32_t) * 2 * layers, st) != cudaSuccess) return COW_ERR_CUDA;
+  Layers<MarkCtx> M{};
+  ScanLaunch C{};
+  M.layers = C.layers = layers;
+  const int64_t stride = scan_words(n) + words16(n > 0 ? n : 1);
+  for (int l = 0; l < layers; ++l) {
+    if ((n > 0 && !maps[l]) || (banks * time > 0 && !write_indices[l])) return COW_ERR_INVALID;
+    if (n > 0 && cudaMemsetAsync(maps[l], 0xff, sizeof(int32_t) * n, st) != cudaSuccess) return COW_ERR_CUDA;
+    M.c[l] = MarkCtx{write_indices[l], maps[l], out + 2 * l};
+    ScanCtx& c = C.c[l];
+    c.op = kOpPack;
+    c.n = n;
+    c.slots = 1;
+    c.map = maps[l];
+    c.scratch = static_cast<int32_t*>(workspace) + stride * l;
+    c.total_out = out + 2 * l + 1;
+  }
+  if (banks * time * writes > 0) {
+    prefill_mark_kernel<<<layer_grid(banks * time * writes, 256, layers), 256, 0, st>>>(M, index_dtype == COW_I64,
+                                                                                     banks, time, writes, slots);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  }
+  return run_scan_count(C, st);
+}
+
+int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
+  if (!layers_ok(pools, layers)) return COW_ERR_INVALID;
+  const int64_t n = pools[0].banks * pools[0].slots;
+  if (!workspace_ok(workspace, workspace_bytes, cow_pack_workspace_bytes(n, layers))) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  ScanLaunch C{};
+  Layers<FillFreeCtx> F{};
+  Layers<CopyCtx> K{};
+  C.layers = F.layers = K.layers = layers;
+  const int64_t stride = scan_words(n) + words16(n > 0 ? n : 1);
+  int64_t max_cap = 0;
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& p = pools[l];
+    if (p.banks * p.slots != n || !p.map || !p.free_rows || !p.free_count || !p.slab || !p.m0 || !p.templates)
+      return COW_ERR_INVALID;
+    int32_t* flags = static_cast<int32_t*>(workspace) + stride * l;
+    int32_t* src_index = flags + scan_words(n);
+    ScanCtx& c = C.c[l];
+    c.op = kOpPack;
+    c.n = n;
+    c.slots = 1;
+    c.map = p.map;
+    c.out_map = p.map;
+    c.src_rows = src_index;
+    c.scratch = flags;
+    F.c[l] = FillFreeCtx{p.free_rows, p.capacity, p.free_count, p.status, flags};
+    K.c[l] = CopyCtx{p.slab, nullptr, nullptr, src_index, flags, p.m0, p.templates, std::min(n, p.capacity),
+                     p.width, p.slots, p.slab_dtype, COW_F32, 1, 0};
+    if (!copy_args_ok(K.c[l])) return COW_ERR_INVALID;
+    max_cap = std::max(max_cap, p.capacity);
+  }
+  int rc = run_scan_apply(C, st);
+  if (rc != COW_OK) return rc;
+  fill_free_kernel<<<layer_grid(max_cap, 256, layers), 256, 0, st>>>(F);
+  if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  return run_copy_rows(K, st);
+}
+
+// ---- validation --------------------------------------------------------------
 
 int cow_validate(const cow_pool* pool, int32_t* counts, int32_t* status, void* stream) {
   if (!pool || !counts || !status) return COW_ERR_INVALID;
@@ -591,16 +1023,56 @@ int cow_validate(const cow_pool* pool, int32_t* counts, int32_t* status, void* s
   if (pool->capacity > 0 &&
       cudaMemsetAsync(counts, 0, sizeof(int32_t) * pool->capacity, st) != cudaSuccess)
     return COW_ERR_CUDA;
+  Layers<ValidateCtx> V{};
+  V.layers = 1;
   const int64_t n = pool->banks * pool->slots;
-  const int64_t m = n > pool->capacity ? n : pool->capacity;
-  validate_count_kernel<<<grid_for(m, 256), 256, 0, st>>>(pool->map, n, pool->free_rows, pool->free_count,
-                                                        pool->capacity, counts, status);
+  V.c[0] = ValidateCtx{pool->map, n, pool->capacity, pool->free_rows, pool->free_count, counts, status,
+                       pool->status, nullptr};
+  validate_count_kernel<<<layer_grid(std::max(n, pool->capacity), 256, 1), 256, 0, st>>>(V);
   if (launch_status() != COW_OK) return COW_ERR_CUDA;
   if (pool->capacity > 0) {
-    validate_check_kernel<<<grid_for(pool->capacity, 256), 256, 0, st>>>(counts, pool->capacity, status);
+    validate_check_kernel<<<layer_grid(pool->capacity, 256, 1), 256, 0, st>>>(V);
     return launch_status();
   }
   return COW_OK;
+}
+
+int64_t cow_validate_workspace_bytes(const cow_pool* pools, int32_t layers) {
+  if (!layers_ok(pools, layers)) return -1;
+  int64_t words = 0;
+  for (int l = 0; l < layers; ++l) words += words16(pools[l].capacity + 1);
+  return words * 4;
+}
+
+int cow_validate_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* out,
+                        void* stream) {
+  if (!layers_ok(pools, layers) || !out) return COW_ERR_INVALID;
+  const int64_t need = cow_validate_workspace_bytes(pools, layers);
+  if (!workspace_ok(workspace, workspace_bytes, need)) return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  if (cudaMemsetAsync(workspace, 0, static_cast<size_t>(need), st) != cudaSuccess) return COW_ERR_CUDA;
+  Layers<ValidateCtx> V{};
+  V.layers = layers;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  int64_t max_work = 0, max_cap = 0;
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& p = pools[l];
+    if (!p.map || !p.free_rows || !p.free_count || !p.status) return COW_ERR_INVALID;
+    const int64_t n = p.banks * p.slots;
+    // the last word of each region holds that pool's validate bits
+    V.c[l] = ValidateCtx{p.map, n, p.capacity, p.free_rows, p.free_count, w, w + p.capacity, p.status, out + 3 * l};
+    w += words16(p.capacity + 1);
+    max_work = std::max(max_work, std::max(n, p.capacity));
+    max_cap = std::max(max_cap, p.capacity);
+  }
+  validate_count_kernel<<<layer_grid(max_work, 256, layers), 256, 0, st>>>(V);
+  if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  if (max_cap > 0) {
+    validate_check_kernel<<<layer_grid(max_cap, 256, layers), 256, 0, st>>>(V);
+    if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  }
+  validate_report_kernel<<<1, 32, 0, st>>>(V);
+  return launch_status();
 }
 
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream) {

@@ -239,6 +239,62 @@ int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count,
  * int32 [capacity] scratch; result bits are OR-ed into `status`. */
 int cow_validate(const cow_pool* pool, int32_t* counts, int32_t* status, void* stream);
 
+/* ---- several pools per call ---------------------------------------------
+ * The SDM layers of one serving batch change together: release, compaction,
+ * admission and prefill touch every layer's pool.  These entry points do one
+ * operation for up to COW_MAX_LAYERS pools with one set of launches (the pool
+ * is a grid dimension), writing every per-pool result the host needs into one
+ * small device array so that a single synchronisation reads them all.  Each
+ * takes a caller-owned, 16-byte aligned `workspace` of at least the matching
+ * *_workspace_bytes() (a negative size means the arguments are invalid); the
+ * workspace is free again when the call's work has run on `stream`.
+ * Per-pool pointer arguments are host arrays of device pointers. */
+
+/* release for each pool l of counts[l] banks bank_indices[l][*]; released[l]
+ * (device int32) receives pool l's count. */
+int64_t cow_release_workspace_bytes(const cow_pool* pools, const int64_t* counts, int32_t layers);
+int cow_release_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts,
+                       int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* released, void* stream);
+
+/* retain_banks for each pool; status[l] (device int32) receives pool l's
+ * COW_ST_BAD_BANK_LIST / COW_ST_DISCARD_LIVE bits (zero = the new map and
+ * templates in new_maps[l] / new_templates[l] are valid). */
+int64_t cow_retain_workspace_bytes(const cow_pool* pools, int32_t layers);
+int cow_retain_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts, int32_t layers,
+                      int32_t* const* new_maps, int64_t* const* new_templates, void* workspace,
+                      int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* append_banks_from for each pair (dsts[l], others[l]).  Phase 1 writes
+ * counts[2l] = live rows of others[l] and counts[2l+1] = free rows of dsts[l]
+ * (device int32) so that the host can grow dsts[l] first; phase 2 (same
+ * workspace, untouched in between) pops, copies the rows and writes the
+ * admitted map rows into admitted_maps[l] [others[l].banks, slots]. */
+int64_t cow_append_workspace_bytes(const cow_pool* others, int32_t layers);
+int cow_append_count_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, void* workspace,
+                            int64_t workspace_bytes, int32_t* counts, void* stream);
+int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, int32_t* const* admitted_maps,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Sparse prefill layout for each pool.  Phase 1 sets maps[l] [banks,slots] to
+ * -1, marks the written slots of write_indices[l] [banks,T,W] and counts them:
+ * out[2l] = status bits (COW_ST_INDEX_RANGE), out[2l+1] = live rows.  Phase 2
+ * (same workspace; pools[l].map = maps[l], slab and stack sized by the host)
+ * assigns rows 0..A-1 in nonzero() order, fills the free stack with
+ * arange(A, capacity) and copies each live row from m0.  n = banks*slots. */
+int64_t cow_pack_workspace_bytes(int64_t n, int32_t layers);
+int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t index_dtype, int64_t banks, int64_t time,
+                                  int32_t writes, int64_t slots, int32_t* const* maps, int32_t layers,
+                                  void* workspace, int64_t workspace_bytes, int32_t* out, void* stream);
+int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,
+                          void* stream);
+
+/* validate_invariants for each pool: out[3l..3l+2] (device int32) = the
+ * pool's status word, the partition bits (COW_ST_MULTI_OWNER,
+ * COW_ST_FREE_DUPLICATE, COW_ST_NOT_COVERED, COW_ST_ROW_RANGE), free count. */
+int64_t cow_validate_workspace_bytes(const cow_pool* pools, int32_t layers);
+int cow_validate_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* out,
+                        void* stream);
+
 /* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
 
