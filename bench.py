@@ -753,6 +753,144 @@ def cpu_churn_rate(seconds: float, quantum_steps: int) -> dict:
 
 
 # --------------------------------------------------------------------------
+# Configuration 2: whole-model decode
+# --------------------------------------------------------------------------
+
+M_VOCAB, M_MAXLEN, M_LAYOUT, M_WIDTH, M_HEADS, M_BATCH, M_PREFIX = 50257, 512, "BBBBBBBA", 128, 4, 16, 256
+
+
+def run_gpu_model(args, rank, world, device):
+    """Random-init 8-layer model (7 SDM layers + 1 attention layer), batch 16 per
+    GPU, prefix 256 through the prefill handoff, then ``LanguageModel.decode``
+    steps on seeded synthetic token ids.  Every timed step is one public
+    decode token of the whole model (controller, fused packed step per SDM
+    layer, K/V-cache attention, MLPs, vocabulary head), replayed as one CUDA
+    graph by ``GraphedDecode``; the eager ``LanguageModel.decode`` is timed
+    beside it.  The e2e leg also copies the step's ids from pinned host memory
+    and reads the greedy next ids back."""
+    from copy_on_write_sdm_b200.graph import GraphedDecode
+    from copy_on_write_sdm_b200.model import LanguageModel
+
+    K, Wm = args.steps, args.warmup
+    if M_PREFIX + K + Wm > M_MAXLEN:
+        raise SystemExit(f"model workload: prefix {M_PREFIX} + steps + warmup must fit {M_MAXLEN} positions")
+    torch.manual_seed(0)
+    model = LanguageModel(vocab_size=M_VOCAB, maximum_sequence_length=M_MAXLEN, layout=M_LAYOUT, width=M_WIDTH,
+                          heads=M_HEADS, slots=SLOTS, reads=READS, writes=WRITES, memory_heads=HEADS,
+                          activation_dtype=torch.float32)
+    model.initialize_role_keyed(0)
+    model = model.to(device).eval()
+    gen = torch.Generator().manual_seed(100 + rank)
+    ids = torch.randint(0, M_VOCAB, (M_BATCH, M_PREFIX + 2 * (K + Wm)), generator=gen)
+    ids_dev = ids.to(device)
+    t0 = time.time()
+    _, state = model.prefill(ids_dev[:, :M_PREFIX], capacity=M_MAXLEN)
+    torch.cuda.synchronize(device)
+    setup_s = time.time() - t0
+    stream = torch.cuda.current_stream(device)
+    pos = M_PREFIX
+    for _ in range(Wm):
+        model.decode(ids_dev[:, pos:pos + 1], state)
+        pos += 1
+    torch.cuda.synchronize(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    with ClockSampler(device.index) as clocks:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        for i in range(K):
+            ev[i][0].record(stream)
+            model.decode(ids_dev[:, pos:pos + 1], state)
+            ev[i][1].record(stream)
+            pos += 1
+        torch.cuda.synchronize(device)
+    eager_ms = sum(a.elapsed_time(b) for a, b in ev)
+    # The same steps by CUDA-graph replay (GraphedDecode) on a fresh prefill of the same prompts.
+    _, state = model.prefill(ids_dev[:, :M_PREFIX], capacity=M_MAXLEN)
+    runner = GraphedDecode(model, state)
+    pos = M_PREFIX
+    for _ in range(Wm):
+        runner.step(ids_dev[:, pos:pos + 1])
+        pos += 1
+    torch.cuda.synchronize(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    with ClockSampler(device.index) as clocks:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        for i in range(K):
+            ev[i][0].record(stream)
+            runner.step(ids_dev[:, pos:pos + 1])
+            ev[i][1].record(stream)
+            pos += 1
+        torch.cuda.synchronize(device)
+    dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    # e2e: a fresh prefill, then K graphed steps fed from pinned host ids, greedy ids read back
+    _, state = model.prefill(ids_dev[:, :M_PREFIX], capacity=M_MAXLEN)
+    runner = GraphedDecode(model, state)
+    host_ids = ids[:, M_PREFIX:].contiguous().pin_memory()
+    nxt = torch.empty(M_BATCH, 1, dtype=torch.int64).pin_memory()
+    for i in range(Wm):
+        runner.step(host_ids[:, i:i + 1].to(device, non_blocking=True))
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(Wm, Wm + K):
+        logits = runner.step(host_ids[:, i:i + 1].to(device, non_blocking=True))
+        nxt.copy_(logits.argmax(-1), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    state_bytes = state.storage_bytes()
+    return dict(total_ms=dev_ms, eager_ms=eager_ms, e2e_ms=e0.elapsed_time(e1), clocks=clocks.summary(),
+                setup_s=setup_s, captures=runner.captures,
+                state_bytes=state_bytes, h2d=host_ids[:, :1].numel() * 8, d2h=nxt.numel() * 8)
+
+
+def main_model(args, rank, world, device) -> int:
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    res = run_gpu_model(args, rank, world, device)
+    total_ms, e2e_ms, eager_ms = reduce_over_ranks([res["total_ms"], res["e2e_ms"], res["eager_ms"]], op="max",
+                                                   device=device)
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return 0
+    K = args.steps
+    tokens = M_BATCH * world * K
+    line = {
+        "metric": METRIC, "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic token ids, random-init weights (seed 0)",
+        "config": {"workload": "config 2 whole-model decode: LanguageModel vocab 50257, max_len 512, layout "
+                               "BBBBBBBA, width 128, 4 attention heads, SDM N=256 D=128 H=1 top-16/top-4, "
+                               "FP32 activations and SDM state",
+                   "batch_per_gpu": M_BATCH, "global_batch": M_BATCH * world, "prefix": M_PREFIX,
+                   "parallelism": f"requests sharded, {M_BATCH} per GPU x {world} GPU(s), no collective",
+                   "l2": "model and state (~60 MB) stay L2-resident; steps timed back to back"},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
+                "d2h_bytes_per_step": res["d2h"],
+                "path": "GraphedDecode.step per step with ids copied from pinned host memory and the greedy "
+                        "next ids copied back"},
+        "eager": {"value": tokens / (eager_ms / 1e3), "unit": "tokens/s", "ms_per_step": eager_ms / K,
+                  "path": "LanguageModel.decode (the reference's eager call sequence)"},
+        "graph_captures": res["captures"],
+        "gpu_launches": None,
+        "gpu_launches_note": "one fused cow_decode_step launch per SDM layer per step (7 per step); the "
+                             "controller, attention, MLP and vocabulary head run as PyTorch kernels",
+        "clocks": res["clocks"],
+        "cpu_baseline": None,
+        "cpu_baseline_note": "the CPU port covers the SDM step and allocator, not the whole model",
+        "retained_state": res["state_bytes"], "setup_s": res["setup_s"],
+    }
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+# --------------------------------------------------------------------------
 # CPU arms (the reference's algorithm, restated in oracle/)
 # --------------------------------------------------------------------------
 
@@ -813,9 +951,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="screen", choices=["screen", "scaleout", "churn"],
-                    help="screen: configuration 3 (default, the headline); scaleout: configuration 4; "
-                         "churn: configuration 5")
+    ap.add_argument("--workload", default="screen", choices=["screen", "model", "scaleout", "churn"],
+                    help="screen: configuration 3 (default, the headline); model: configuration 2; "
+                         "scaleout: configuration 4; churn: configuration 5")
     ap.add_argument("--requests", type=int, default=SO_REQUESTS, help="scaleout: requests over all GPUs")
     ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
     ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
@@ -853,6 +991,8 @@ def main() -> int:
         return main_scaleout(args, rank, world, device)
     if args.workload == "churn":
         return main_churn(args, rank, world, device)
+    if args.workload == "model":
+        return main_model(args, rank, world, device)
     res = run_gpu(args, rank, world, device)
 
     from copy_on_write_sdm_b200.sharding import reduce_over_ranks

@@ -673,15 +673,20 @@ class PackedSDMCopyOnWriteState:
 # --------------------------------------------------------------------------
 
 
-def _read_counts_and_range(values: Sequence[torch.Tensor], templates: torch.Tensor | None):
-    """One host synchronisation for several 0-d device integers and, optionally,
+def _read_counts_and_range(values: torch.Tensor | Sequence[torch.Tensor], templates: torch.Tensor | None):
+    """One host synchronisation for device integers (a vector or several 0-d
+    tensors) and, optionally,
     the (min, max) of a template-index vector.  Returns ``(ints, lo, hi)``."""
-    parts = [torch.stack([v.reshape(()).to(torch.int64) for v in values])] if values else []
+    if isinstance(values, torch.Tensor):
+        parts = [values.reshape(-1).to(torch.int64)]
+        k = values.numel()
+    else:
+        parts = [torch.stack([v.reshape(()).to(torch.int64) for v in values])] if values else []
+        k = len(values)
     if templates is not None and templates.numel():
         lo, hi = torch.aminmax(templates)
         parts.append(torch.stack((lo, hi)))
     host = torch.cat(parts).tolist() if parts else []
-    k = len(values)
     if templates is not None and templates.numel():
         return host[:k], host[k], host[k + 1]
     return host[:k], None, None
@@ -912,7 +917,7 @@ def from_prefix_routes_layers(
     _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), idx_code, banks, time, writes,
                                                  slots, _ptrs(maps), n, ws.data_ptr(), ws.numel(), out.data_ptr(),
                                                  stream), "cow_prefill_mark_count_layers")
-    host, lo, hi = _read_counts_and_range(list(out), templates)
+    host, lo, hi = _read_counts_and_range(out, templates)
     for l in range(n):
         if host[2 * l]:
             raise ValueError(_lib.status_text(host[2 * l]))

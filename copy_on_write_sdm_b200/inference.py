@@ -38,6 +38,12 @@ def _banks_of(requests: torch.Tensor, heads: int) -> torch.Tensor:
     return (requests[:, None] * heads + torch.arange(heads, device=requests.device)[None, :]).reshape(-1)
 
 
+def _banks_per_state(requests: torch.Tensor, heads: Sequence[int]) -> list[torch.Tensor]:
+    """``_banks_of`` for every pool, computed once per distinct head count."""
+    cache: dict[int, torch.Tensor] = {}
+    return [cache[h] if h in cache else cache.setdefault(h, _banks_of(requests, h)) for h in heads]
+
+
 @dataclass
 class FaithfulSDMDecodeState:
     """Retained state of one batch of independent requests (reference inference.py:26-276).
@@ -101,8 +107,8 @@ class FaithfulSDMDecodeState:
         if (min(host) < 0 or max(host) >= self.batch or len(set(host)) != len(host)
                 or not bool(self.active_sequences[chosen].all())):
             raise ValueError("released sequence is invalid, duplicated, or inactive")
-        total = release_layers(self.sdm_states, [_banks_of(chosen, self._heads(state, self.batch))
-                                                 for state in self.sdm_states])
+        total = release_layers(self.sdm_states,
+                               _banks_per_state(chosen, [self._heads(st, self.batch) for st in self.sdm_states]))
         self.active_sequences[chosen] = False
         return total
 
@@ -123,7 +129,8 @@ class FaithfulSDMDecodeState:
             return keep
         positions = self.current_positions()
         if before:
-            retain_layers(self.sdm_states, [_banks_of(keep, self._heads(state, before)) for state in self.sdm_states])
+            retain_layers(self.sdm_states,
+                          _banks_per_state(keep, [self._heads(st, before) for st in self.sdm_states]))
         self.dense_keys = tuple(t[keep].contiguous() for t in self.dense_keys)
         self.dense_values = tuple(t[keep].contiguous() for t in self.dense_values)
         kept_positions = positions[keep].contiguous()
