@@ -12,8 +12,9 @@
 // exactly with a single-pass decoupled look-back scan over tiles of banks,
 // ordered by a dynamic ticket so a tile only ever waits on tiles that already
 // started.  First touches depend only on the pre-step map, so every row load
-// and all arithmetic run before the scan resolves; only the placement of the
-// first-touch rows waits for it.  Every wait is bounded and reports
+// is in flight before the scan resolves, and banks without first touches
+// (other than the banks that publish totals) never wait on it; only the
+// placement of first-touch rows needs it.  Every wait is bounded and reports
 // COW_ST_WAIT_TIMEOUT instead of hanging.
 
 
@@ -153,10 +154,16 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   }
 
   // Exclusive prefix of first touches over the preceding banks of this pool
-  // (two-level scan, about one round trip), overlapped with the row loads above.
+  // (two-level scan, about one round trip), overlapped with the row loads
+  // above.  Only banks that place rows, close the pool or publish a scan
+  // group's total need it.
   int excl;
   if (P.two_pass) {
     excl = __shfl_sync(kFull, excl_given, 0);
+  } else if (count == 0 && bank != L.banks - 1 && bank % kScanGroup != kScanGroup - 1) {
+    // Nothing to place, not the bank that closes the pool and not the bank
+    // that publishes its scan group's total: the prefix is not needed.
+    excl = 0;
   } else {
     bool timed_out = false;
     excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
