@@ -301,9 +301,18 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
                                             int64_t row, int64_t map_row, int64_t N, int W, int R,
                                             int idx64, int adt, int lane, unsigned& first_mask,
                                             int& error_bits, int32_t* staged = nullptr) {
+  // The first 256 map entries come through registers (their latency is the
+  // route loads' latency), any further ones through cp.async.
+  constexpr int kRegStage = 2;
+  int4 mtmp[kRegStage];
   if (!kDense && staged != nullptr) {
     const int4* src = reinterpret_cast<const int4*>(map + map_row * N);
-    for (int i = lane; i < static_cast<int>(N >> 2); i += 32) cp_async16(staged + 4 * i, src + i);
+#pragma unroll
+    for (int k = 0; k < kRegStage; ++k) {
+      const int i = lane + 32 * k;
+      if (i < static_cast<int>(N >> 2)) mtmp[k] = __ldcg(src + i);
+    }
+    for (int i = lane + 32 * kRegStage; i < static_cast<int>(N >> 2); i += 32) cp_async16(staged + 4 * i, src + i);
   }
   int64_t wraw = 0;
   float wwv = 0.f;
@@ -328,7 +337,12 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
   const int wi = wok ? static_cast<int>(wraw) : 0;
   const int32_t* mrow = map + map_row * N;
   if (!kDense && staged != nullptr) {
-    cp_async_wait_all();
+#pragma unroll
+    for (int k = 0; k < kRegStage; ++k) {
+      const int i = lane + 32 * k;
+      if (i < static_cast<int>(N >> 2)) reinterpret_cast<int4*>(staged)[i] = mtmp[k];
+    }
+    if (N > 128 * kRegStage) cp_async_wait_all();
     __syncwarp();
     mrow = staged;
   }
@@ -358,12 +372,21 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
   // Reads of a slot written this step see the updated row (read-after-write,
   // allocator.py:1503-1517); its value is still in registers, so those reads
   // are folded into one weight per write slot (fwt) instead of reloading it.
+  // Write slot of each read slot, if any: write slot w's address comes from
+  // lane w by shuffle.
+  int fwv[RC];
+#pragma unroll
+  for (int c = 0; c < RC; ++c) fwv[c] = -1;
+  for (int w = 0; w < W; ++w) {
+    const int waddr = __shfl_sync(kFull, wi, w);
+#pragma unroll
+    for (int c = 0; c < RC; ++c) fwv[c] = waddr == ri[c] ? w : fwv[c];
+  }
 #pragma unroll
   for (int c = 0; c < RC; ++c) {
     const int r = c * 32 + lane;
     if (r < R) {
-      int fw = -1;
-      for (int w = 0; w < W; ++w) fw = (sm.widx[w] == ri[c]) ? w : fw;
+      const int fw = fwv[c];
       sm.ridx[r] = ri[c];
       sm.rsrc[r] = fw >= 0 ? -(fw + 2) : (rp[c] >= 0 ? rp[c] : -1);
       sm.rw[r] = rwv[c];

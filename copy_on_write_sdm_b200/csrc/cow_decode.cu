@@ -120,19 +120,8 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   float wt0[kStageReads ? 1 : ReadGroup<CH>::G];
   const int64_t m0_base = tmpl * N;
   if (!bad) {
-    if constexpr (kStageReads) {
-      if (lane * 4 < D) {
-        for (int r = 0; r < R; ++r) {
-          const int src = sm.rsrc[r];
-          if (src >= 0) {
-            cp_async16(s_reads + r * D + lane * 4,
-                       static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D + lane * 4);
-          } else if (src == -1) {
-            cp_async16(s_reads + r * D + lane * 4, L.m0 + (m0_base + sm.ridx[r]) * D + lane * 4);
-          }
-        }
-      }
-    }
+    // Write rows first (registers), then the read rows (shared memory): the
+    // issue loop of the read copies runs under the write rows' latency.
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W) {
@@ -147,6 +136,20 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
                          : Elem<SDT>::ld4(L.slab, static_cast<int64_t>(phys) * D + col);
           }
           upd[w][c] = x;
+        }
+      }
+    }
+    if constexpr (kStageReads) {
+      if (lane * 4 < D) {
+#pragma unroll 4
+        for (int r = 0; r < R; ++r) {
+          const int src = sm.rsrc[r];
+          if (src >= 0) {
+            cp_async16(s_reads + r * D + lane * 4,
+                       static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D + lane * 4);
+          } else if (src == -1) {
+            cp_async16(s_reads + r * D + lane * 4, L.m0 + (m0_base + sm.ridx[r]) * D + lane * 4);
+          }
         }
       }
     }
