@@ -52,6 +52,14 @@ METRIC = "packed-SDM decode tokens/s at batch 64, 1/2/4/8 B200; % of HBM rooflin
 LAYERS, SLOTS, WIDTH, HEADS, READS, WRITES = 7, 256, 128, 1, 16, 4
 BATCH, PREFIX, QUANTUM_STEPS = 64, 2048, 4
 L2_FLUSH_BYTES = 256 << 20
+# DRAM traffic per launch of the dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum); the capture commands and
+# figures are in profiles/.
+TRAFFIC_SCREEN = {"bytes_per_launch": 5_376_683,
+                  "source": "ncu, cow_decode_kernel, this bench's default run, cold L2 (mean of 3 launches)"}
+TRAFFIC_SCALEOUT = {"bytes_per_launch_per_bank": 14_256,
+                    "source": "ncu at 224 requests (12,544 banks, prefix 256): cow_count_kernel 8.56 MB + "
+                              "cow_decode_kernel 170.27 MB per step, scaled by banks"}
 
 
 def algorithmic_bytes(banks: int, first_touches: int, *, idx_bytes=8, val_bytes=4, act_bytes=4) -> int:
@@ -1021,9 +1029,10 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "frac": achieved / peak, "traffic": TRAFFIC_SCREEN["bytes_per_launch"],
+                     "traffic_source": TRAFFIC_SCREEN["source"], "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": per_launch, "mean_launch_us": mean_launch_s * 1e6,
-                     "kernel": "cow_decode_kernel<f32,1,8>"},
+                     "kernel": "cow_decode_kernel<f32,1,4,1>"},
         "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
                 "d2h_bytes_per_step": res["d2h"], "path": "DecodeSession.step_host: one pinned H2D copy, capacity proof + one fused launch, one D2H copy per step"},
         "gpu_launches": K,
@@ -1076,7 +1085,9 @@ def main_scaleout(args, rank, world, device) -> int:
                    "prefix_state": "written-address union of the Zipf prefix packed in nonzero() order, rows from M0",
                    "l2": "pool state (>100 GB at 1 GPU) far exceeds L2; steps timed back to back"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_source": peak_src, "algorithmic_bytes_per_launch": per_launch,
+                     "traffic": TRAFFIC_SCALEOUT["bytes_per_launch_per_bank"] * res["banks"] * LAYERS,
+                     "traffic_source": TRAFFIC_SCALEOUT["source"], "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": per_launch,
                      "mean_launch_us": mean_s * 1e6, "kernel": "cow_decode_kernel<f32,1,4,1>"},
         "e2e": None, "gpu_launches": K, "clocks": res["clocks"],
         "cpu_baseline": cpu_scaleout_rate(args.cpu_seconds, res["requests"] * world, args.prefix),
