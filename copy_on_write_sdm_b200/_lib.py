@@ -82,6 +82,11 @@ _SIGNATURES = {
                                   c_int32, c_int32, P, c_int64, P]),
     "cow_decode_step_noalloc": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                           c_int32, c_int32, P]),
+    "cow_decode_step_host": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32, c_int32,
+                                       c_int32, P, c_int64, P, P, c_int64, P, P, c_int64, P]),
+    "cow_decode_step_host_overlapped": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
+                                                  c_int32, c_int32, P, c_int64, P, P, c_int64, P, P, c_int64,
+                                                  P, P, P, P, P, P]),
     "cow_dense_step": (c_int32, [POINTER(c_void_p), POINTER(c_int64), POINTER(CowStep), c_int32,
                                  c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, P]),
     "cow_init_pool": (c_int32, [POINTER(CowPool), P]),

@@ -83,6 +83,10 @@ def _scan_scratch(device: torch.device, n: int) -> torch.Tensor:
 # --------------------------------------------------------------------------
 
 
+_TENSOR_FIELDS = frozenset({"shared_initial_memory", "template_indices", "values", "logical_to_physical",
+                            "free_rows", "free_count", "overflow_flag", "_m0_f32"})
+
+
 @dataclass
 class PackedSDMCopyOnWriteState:
     """One shared slab backing several independent logical SDM tables.
@@ -108,6 +112,13 @@ class PackedSDMCopyOnWriteState:
     growth_rows_added: int = 0
     growth_rows_copied: int = 0
     _m0_f32: torch.Tensor | None = field(default=None, repr=False, compare=False)
+
+    def __setattr__(self, name: str, value) -> None:
+        # Descriptor caches (DecodeSession, GraphedDecode) compare this counter
+        # to learn that a tensor of the pool was replaced.
+        object.__setattr__(self, name, value)
+        if name in _TENSOR_FIELDS:
+            object.__setattr__(self, "_tensor_version", self.__dict__.get("_tensor_version", 0) + 1)
 
     # ---------------- construction ----------------
 

@@ -511,6 +511,76 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   return launch_status();
 }
 
+int cow_decode_step_host(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
+                         int32_t index_dtype, int32_t act_dtype, void* scan_scratch, int64_t scratch_bytes,
+                         void* device_inputs, const void* host_inputs, int64_t input_bytes, void* host_outputs,
+                         const void* device_outputs, int64_t output_bytes, void* stream) {
+  if (input_bytes < 0 || output_bytes < 0 || (input_bytes > 0 && (!device_inputs || !host_inputs)) ||
+      (output_bytes > 0 && (!host_outputs || !device_outputs)))
+    return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  if (input_bytes > 0) {
+    const cudaError_t e = cudaMemcpyAsync(device_inputs, host_inputs, static_cast<size_t>(input_bytes),
+                                          cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+  }
+  const int rc = cow_decode_step(pools, steps, layers, writes, reads, index_dtype, act_dtype, scan_scratch,
+                                 scratch_bytes, stream);
+  if (rc != COW_OK) return rc;
+  if (output_bytes > 0) {
+    const cudaError_t e = cudaMemcpyAsync(host_outputs, device_outputs, static_cast<size_t>(output_bytes),
+                                          cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) {
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+  }
+  return COW_OK;
+}
+
+int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
+                                    int32_t reads, int32_t index_dtype, int32_t act_dtype, void* scan_scratch,
+                                    int64_t scratch_bytes, void* device_inputs, const void* host_inputs,
+                                    int64_t input_bytes, void* host_outputs, const void* device_outputs,
+                                    int64_t output_bytes, void* compute_stream, void* h2d_stream, void* d2h_stream,
+                                    void* h2d_done, void* computed, void* d2h_done) {
+  if (input_bytes <= 0 || output_bytes <= 0 || !device_inputs || !host_inputs || !host_outputs || !device_outputs ||
+      !h2d_done || !computed || !d2h_done)
+    return COW_ERR_INVALID;
+  cudaStream_t cs = as_stream(compute_stream), hs = as_stream(h2d_stream), ds = as_stream(d2h_stream);
+  cudaEvent_t e_h2d = static_cast<cudaEvent_t>(h2d_done), e_comp = static_cast<cudaEvent_t>(computed),
+              e_d2h = static_cast<cudaEvent_t>(d2h_done);
+  // The buffers of this step were last used two steps ago: its decode read the
+  // inputs (e_comp) and its readout copy read the outputs (e_d2h).  Waiting
+  // on an event that was never recorded returns at once.
+  cudaError_t e = cudaStreamWaitEvent(hs, e_comp, 0);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(device_inputs, host_inputs, static_cast<size_t>(input_bytes),
+                                            cudaMemcpyHostToDevice, hs);
+  if (e == cudaSuccess) e = cudaEventRecord(e_h2d, hs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, e_h2d, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, e_d2h, 0);
+  if (e != cudaSuccess) {
+    cowrt::last_cuda_error = static_cast<int>(e);
+    return COW_ERR_CUDA;
+  }
+  const int rc = cow_decode_step(pools, steps, layers, writes, reads, index_dtype, act_dtype, scan_scratch,
+                                 scratch_bytes, compute_stream);
+  if (rc != COW_OK) return rc;
+  e = cudaEventRecord(e_comp, cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ds, e_comp, 0);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(host_outputs, device_outputs, static_cast<size_t>(output_bytes),
+                                            cudaMemcpyDeviceToHost, ds);
+  if (e == cudaSuccess) e = cudaEventRecord(e_d2h, ds);
+  if (e != cudaSuccess) {
+    cowrt::last_cuda_error = static_cast<int>(e);
+    return COW_ERR_CUDA;
+  }
+  return COW_OK;
+}
+
 int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
                             int32_t reads, int32_t index_dtype, int32_t act_dtype, void* stream) {
   if (!pools || !steps || layers < 1 || layers > COW_MAX_LAYERS) return COW_ERR_INVALID;

@@ -13,7 +13,11 @@ launch itself at serving batch sizes.  ``DecodeSession`` does that work once:
   admission);
 * ``step()`` runs the reference's per-step capacity proof
   (``prepare_step_capacity``, allocator.py:746-774) for every pool, then one
-  fused ``cow_decode_step`` launch for all pools.
+  fused ``cow_decode_step`` launch for all pools;
+* ``step_host_pipelined()`` streams host steps through two input and two
+  output buffers on three streams, so step k+1's inputs cross PCIe while step
+  k decodes and step k-1's readouts come back (the decode steps themselves
+  stay in order on the compute stream).
 
 Semantics per pool are exactly ``packed_sdm_cow_step`` with
 ``validate_routes=False, collect_diagnostics=False`` (the decode path of
@@ -30,6 +34,14 @@ import torch
 
 from . import _lib
 from .allocator import PackedSDMCopyOnWriteState, decode_scratch
+
+
+def _current_raw_stream(device_index: int) -> int:
+    """Handle of torch's current stream on the device (the cheap accessor when present)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
 
 
 class DecodeSession:
@@ -85,6 +97,8 @@ class DecodeSession:
         self.host_inputs = torch.empty(off, dtype=torch.uint8, pin_memory=pinned_host)
         self.outputs = torch.empty(len(pools), B, D, dtype=act_dtype, device=self.device)
         self.host_outputs = torch.empty(len(pools), B, D, dtype=act_dtype, pin_memory=pinned_host)
+        self._offsets = offsets
+        self._pipe = None
         self.views = [self._views(self.inputs, per) for per in offsets]
         self.host_views = [self._views(self.host_inputs, per) for per in offsets]
         self._steps = (_lib.CowStep * len(pools))(*[
@@ -97,6 +111,9 @@ class DecodeSession:
         self._pool_key = None
         self._pool_array = None
         self._scratch = decode_scratch(self.device, B * len(pools), len(pools))
+        self._need = B * writes  # first touches one step can make in a pool
+        self._out_bytes = self.host_outputs.numel() * self.host_outputs.element_size()
+        self._device_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._lib = _lib.load()
 
     @staticmethod
@@ -107,26 +124,90 @@ class DecodeSession:
         return out
 
     def _pools(self):
-        key = tuple((p.values.data_ptr(), p.logical_to_physical.data_ptr(), p.free_rows.data_ptr(),
-                     p.template_indices.data_ptr(), p.capacity_rows, p.banks) for p in self.pools)
+        key = tuple(p.__dict__.get("_tensor_version", 0) for p in self.pools)
         if key != self._pool_key:
             self._pool_array = (_lib.CowPool * len(self.pools))(*[p._pool() for p in self.pools])
             self._pool_key = key
         return self._pool_array
 
+    def _prove(self) -> None:
+        """The reference's per-step capacity proof (allocator.py:746-774) for every pool;
+        the common case (enough proven rows left) is a host counter decrement."""
+        need = self._need
+        for p in self.pools:
+            d = p.__dict__
+            if d["growth_quantum_rows"]:
+                left = d["proven_maximum_additional_allocations"]
+                if left >= need and d["capacity_is_proven"]:
+                    d["proven_maximum_additional_allocations"] = left - need
+                else:
+                    p.prepare_step_capacity(need)
+            elif not d["capacity_is_proven"]:
+                raise ValueError("SDM COW capacity has no decode proof")
+
+    def _stream_handle(self) -> int:
+        return _current_raw_stream(self._device_index)
+
     @torch.no_grad()
     def step(self, *, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """One decode token for every bank of every pool; returns ``outputs`` ``[L, B, D]`` (device)."""
-        for p in self.pools:
-            if p.growth_quantum_rows:
-                p.prepare_step_capacity(p.banks * self.writes)
-            elif not p.capacity_is_proven:
-                raise ValueError("SDM COW capacity has no decode proof")
-        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        self._prove()
+        handle = stream.cuda_stream if stream is not None else self._stream_handle()
         _lib.check(self._lib.cow_decode_step(self._pools(), self._steps, len(self.pools), self.writes, self.reads,
                                              _lib.I64, self._act_code, self._scratch.data_ptr(),
-                                             self._scratch.numel(), s.cuda_stream), "cow_decode_step")
+                                             self._scratch.numel(), handle), "cow_decode_step")
         return self.outputs
+
+    def _pipeline(self):
+        if self._pipe is None:
+            alt = torch.empty_like(self.inputs)
+            views = [self._views(alt, per) for per in self._offsets]
+            out_alt = torch.empty_like(self.outputs)
+            steps_alt = (_lib.CowStep * len(self.pools))(*[
+                _lib.CowStep(v["write_indices"].data_ptr(), v["write_weights"].data_ptr(), v["values"].data_ptr(),
+                             v["input_gate"].data_ptr(), v["input_gate"].data_ptr(), v["forget_log_gate"].data_ptr(),
+                             v["read_indices"].data_ptr(), v["read_weights"].data_ptr(), out_alt[l].data_ptr(), None)
+                for l, v in enumerate(views)])
+            pinned = self.host_outputs.is_pinned()
+            h2d, d2h = torch.cuda.Stream(self.device), torch.cuda.Stream(self.device)
+            events = [[torch.cuda.Event() for _ in range(3)] for _ in range(2)]
+            for pair in events:  # materialise the handles; a recorded-then-idle event never blocks
+                for ev in pair:
+                    ev.record(h2d)
+            torch.cuda.synchronize(self.device)
+            self._pipe = {
+                "inputs": (self.inputs, alt), "outputs": (self.outputs, out_alt), "steps": (self._steps, steps_alt),
+                "host_outputs": (self.host_outputs, torch.empty_like(self.host_outputs, pin_memory=pinned)),
+                "h2d": h2d, "d2h": d2h, "events": events, "k": 0,
+            }
+        return self._pipe
+
+    @torch.no_grad()
+    def step_host_pipelined(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
+        """Host-to-host step overlapped with its neighbours (``cow_decode_step_host_overlapped``).
+
+        ``host_step`` holds the step's pinned input bytes (``inputs`` layout).
+        Returns the pinned host buffer that will hold this step's readouts
+        ``[L, B, D]`` and the event that marks their arrival; the buffer is
+        reused two steps later.  Steps decode strictly in call order on the
+        current stream; the copies run on two side streams.
+        """
+        if host_step.numel() != self.step_bytes or host_step.dtype != torch.uint8 \
+                or host_step.device.type != "cpu" or not host_step.is_contiguous():
+            raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
+        pipe = self._pipeline()
+        b = pipe["k"] & 1
+        pipe["k"] += 1
+        self._prove()
+        h2d_done, computed, d2h_done = pipe["events"][b]
+        out, dev_out = pipe["host_outputs"][b], pipe["outputs"][b]
+        _lib.check(self._lib.cow_decode_step_host_overlapped(
+            self._pools(), pipe["steps"][b], len(self.pools), self.writes, self.reads, _lib.I64, self._act_code,
+            self._scratch.data_ptr(), self._scratch.numel(), pipe["inputs"][b].data_ptr(), host_step.data_ptr(),
+            self.step_bytes, out.data_ptr(), dev_out.data_ptr(), self._out_bytes,
+            self._stream_handle(), pipe["h2d"].cuda_stream, pipe["d2h"].cuda_stream,
+            h2d_done.cuda_event, computed.cuda_event, d2h_done.cuda_event), "cow_decode_step_host_overlapped")
+        return out, d2h_done
 
     @torch.no_grad()
     def step_host(self, host_step: torch.Tensor | None = None) -> torch.Tensor:
@@ -134,7 +215,14 @@ class DecodeSession:
         default ``host_inputs``) to the device, decode, copy the readouts back into
         ``host_outputs`` (asynchronously on the current stream) and return it."""
         src = self.host_inputs if host_step is None else host_step
-        self.inputs.copy_(src, non_blocking=True)
-        self.step()
-        self.host_outputs.copy_(self.outputs, non_blocking=True)
-        return self.host_outputs
+        if src.numel() != self.step_bytes or src.dtype != torch.uint8 or src.device.type != "cpu" \
+                or not src.is_contiguous():
+            raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
+        self._prove()
+        out = self.host_outputs
+        _lib.check(self._lib.cow_decode_step_host(
+            self._pools(), self._steps, len(self.pools), self.writes, self.reads, _lib.I64, self._act_code,
+            self._scratch.data_ptr(), self._scratch.numel(), self.inputs.data_ptr(), src.data_ptr(), self.step_bytes,
+            out.data_ptr(), self.outputs.data_ptr(), self._out_bytes, self._stream_handle()),
+            "cow_decode_step_host")
+        return out

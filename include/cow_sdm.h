@@ -138,6 +138,33 @@ int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_
                             int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
                             void* stream);
 
+/* Host-to-host decode step on `stream`: one cudaMemcpyAsync of `input_bytes`
+ * from pinned `host_inputs` to `device_inputs` (the buffer the step
+ * descriptors point into), the fused decode step, one cudaMemcpyAsync of
+ * `output_bytes` from `device_outputs` back to pinned `host_outputs`.  The
+ * serving runtime's per-token call (DecodeSession.step_host), one C call per
+ * token instead of three runtime calls from the host language. */
+int cow_decode_step_host(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
+                         int32_t index_dtype, int32_t act_dtype, void* scan_scratch, int64_t scratch_bytes,
+                         void* device_inputs, const void* host_inputs, int64_t input_bytes, void* host_outputs,
+                         const void* device_outputs, int64_t output_bytes, void* stream);
+
+/* cow_decode_step_host with the copies on their own streams, for a runtime
+ * that alternates two input / output buffer pairs: the input copy runs on
+ * `h2d_stream` once the decode that last read `device_inputs` is done
+ * (`computed`, recorded by that step), the decode on `compute_stream` after
+ * the copy (`h2d_done`) and after the readout copy that last read
+ * `device_outputs` (`d2h_done`), the readout copy on `d2h_stream`.  All three
+ * events (cudaEvent_t) belong to this buffer pair and are recorded again
+ * here.  Decode steps stay in call order on `compute_stream`; the copies of
+ * neighbouring steps overlap them. */
+int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
+                                    int32_t reads, int32_t index_dtype, int32_t act_dtype, void* scan_scratch,
+                                    int64_t scratch_bytes, void* device_inputs, const void* host_inputs,
+                                    int64_t input_bytes, void* host_outputs, const void* device_outputs,
+                                    int64_t output_bytes, void* compute_stream, void* h2d_stream, void* d2h_stream,
+                                    void* h2d_done, void* computed, void* d2h_done);
+
 /* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
  * allocator.py:368-460): the same math on dense [banks,slots,width] tables.
  * memories[l] has dtype mem_dtype; same limits as cow_decode_step. */

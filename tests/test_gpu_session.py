@@ -54,3 +54,49 @@ def test_session_matches_per_call_api_through_growth(dev):
         assert torch.equal(p.logical_to_physical, q.logical_to_physical)
         assert p.capacity_rows == q.capacity_rows and p.growth_events == q.growth_events > 0
         q.validate_invariants()
+
+
+def test_pipelined_host_steps_match_sequential(dev):
+    """step_host_pipelined overlaps copies of neighbouring steps on side streams;
+    readouts, maps, stacks and growth must equal the sequential step_host run."""
+    from copy_on_write_sdm_b200 import DecodeSession
+
+    layers, banks, slots, width, W, R = 2, 48, 256, 128, 4, 16
+    quantum = O.growth_quantum_rows(banks, W, 3)
+    seq = DecodeSession(_pools(dev, layers, banks, slots, width, quantum, 7), writes=W, reads=R)
+    pipe = DecodeSession(_pools(dev, layers, banks, slots, width, quantum, 7), writes=W, reads=R)
+    rng = np.random.default_rng(8)
+    steps = 10
+    host = torch.empty(steps, seq.step_bytes, dtype=torch.uint8, pin_memory=True)
+    for i in range(steps):
+        xs = [O.synthetic_step_inputs(rng, banks, slots, width, W, R) for _ in range(layers)]
+        for l, x in enumerate(xs):
+            for k, v in x.items():
+                seq.host_views[l][k].copy_(torch.from_numpy(v))
+        host[i].copy_(seq.host_inputs)
+    want = []
+    for i in range(steps):
+        seq.step_host(host[i])
+        torch.cuda.synchronize(dev)
+        want.append(seq.host_outputs.clone())
+    got = []
+    pending = []
+    for i in range(steps):
+        out, ev = pipe.step_host_pipelined(host[i])
+        pending.append((out, ev))
+        if len(pending) == 2:  # the buffer of step i-1 is reused by step i+1
+            o, e = pending.pop(0)
+            e.synchronize()
+            got.append(o.clone())
+    for o, e in pending:
+        e.synchronize()
+        got.append(o.clone())
+    torch.cuda.synchronize(dev)
+    for a, b in zip(want, got):
+        assert torch.equal(a, b)
+    for p, q in zip(seq.pools, pipe.pools):
+        assert torch.equal(p.logical_to_physical, q.logical_to_physical)
+        fp = int(p.free_count)
+        assert fp == int(q.free_count) and torch.equal(p.free_rows[:fp], q.free_rows[:fp])
+        assert p.growth_events == q.growth_events > 0
+        q.validate_invariants()
