@@ -45,3 +45,33 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.cow_decode_step(ctypes.byref(pool), ctypes.byref(step), 1, 4, 16, 1, 0,
                                ctypes.addressof(scratch), 64, None) == _lib.ERR_UNSUPPORTED
     assert lib.cow_grow(None, None, 0, None, None, 0, 4, 0, None, None, None) == _lib.ERR_INVALID
+
+
+def test_multi_pool_and_host_step_entry_points_reject_bad_arguments():
+    lib = _lib.load()
+    pools = (_lib.CowPool * 2)()
+    for p in pools:
+        p.banks, p.slots, p.width, p.capacity = 4, 8, 128, 16
+    counts = (ctypes.c_int64 * 2)(2, 0)
+    # workspace sizes: masks rounded to 16 bytes + scan header per pool
+    assert lib.cow_release_workspace_bytes(pools, counts, 2) > 0
+    assert lib.cow_release_workspace_bytes(pools, counts, 0) == -1
+    assert lib.cow_release_workspace_bytes(pools, counts, _lib.MAX_LAYERS + 1) == -1
+    assert lib.cow_retain_workspace_bytes(pools, 2) == 2 * 16
+    assert lib.cow_append_workspace_bytes(pools, 2) > 0
+    assert lib.cow_pack_workspace_bytes(-1, 1) == -1
+    assert lib.cow_validate_workspace_bytes(pools, 2) == 2 * 4 * 20
+    # a workspace that is too small (or missing) is rejected before anything launches
+    ws = ctypes.create_string_buffer(16)
+    ptrs = (ctypes.c_void_p * 2)(None, None)
+    out = ctypes.create_string_buffer(8)
+    assert lib.cow_release_layers(pools, ptrs, counts, 2, None, 0, out, None) == _lib.ERR_INVALID
+    assert lib.cow_retain_layers(pools, ptrs, counts, 2, ptrs, ptrs, ws, 0, out, None) == _lib.ERR_INVALID
+    assert lib.cow_validate_layers(pools, 2, ws, 16, out, None) == _lib.ERR_INVALID
+    assert lib.cow_pack_apply_layers(pools, 0, ws, 16, None) == _lib.ERR_INVALID
+    assert lib.cow_prefill_recurrence_layers(pools, None, 2, 4, 4, 16, 1, 0, None) == _lib.ERR_INVALID
+    # host-to-host steps: negative sizes, missing buffers or events
+    assert lib.cow_decode_step_host(pools, None, 1, 4, 16, 1, 0, None, 0, None, None, -1, None, None, 0,
+                                    None) == _lib.ERR_INVALID
+    assert lib.cow_decode_step_host_overlapped(pools, None, 1, 4, 16, 1, 0, None, 0, ws, ws, 16, ws, ws, 16,
+                                               None, None, None, None, None, None) == _lib.ERR_INVALID
