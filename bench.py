@@ -1011,10 +1011,14 @@ def main() -> int:
         print(json.dumps(line))
         return 0
 
-    if world > 1:
-        torch.distributed.init_process_group("nccl")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1:
+        # rank 0's stdout carries exactly one JSON line: keep NCCL's version
+        # banner (NCCL_DEBUG=VERSION) off it
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        torch.distributed.init_process_group("nccl", device_id=device)
     torch.backends.cuda.matmul.allow_tf32 = False
     if args.workload == "scaleout":
         return main_scaleout(args, rank, world, device)
