@@ -74,12 +74,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   uint32_t epoch = 0;
   int old_free = 0, excl_given = 0;
   if (lane == 0) {
-    if (P.two_pass) {
-      // cow_count_kernel already produced this bank's prefix and the pool's
-      // starting free count: plain inputs, no waiting.
-      excl_given = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(L.tile_begin) * kBanksPerCta + bank];
-      old_free = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(P.total_tiles) * kBanksPerCta + l];
-    } else {
+    if (!P.two_pass) {
       epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
       old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
     }
@@ -162,7 +157,18 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   // group's total need it.
   int excl;
   if (P.two_pass) {
+    // cow_count_kernel produced this bank's prefix and the pool's starting free
+    // count.  This grid may start while that kernel still runs (programmatic
+    // dependent launch): everything above touches nothing it writes, and the
+    // wait below returns once its memory operations are visible.  The map
+    // stores of the placement come after it, through the shuffled values.
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      excl_given = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(L.tile_begin) * kBanksPerCta + bank];
+      old_free = reinterpret_cast<const int32_t*>(P.flags)[static_cast<int64_t>(P.total_tiles) * kBanksPerCta + l];
+    }
     excl = __shfl_sync(kFull, excl_given, 0);
+    old_free = __shfl_sync(kFull, old_free, 0);
   } else if (count == 0 && bank != L.banks - 1 && bank % kScanGroup != kScanGroup - 1) {
     // Nothing to place, not the bank that closes the pool and not the bank
     // that publishes its scan group's total: the prefix is not needed.
@@ -271,50 +277,90 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 // flag region, read as int32), and the pool's new free count.
 
 constexpr int kCountThreads = kScanGroup;  // one count block per 128-bank scan group (reuses its flag)
+constexpr int kCountUnroll = 8;  // route elements a thread loads per round
 
 __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_constant__ DecodeLaunch P) {
   __shared__ int s_warp[kCountThreads / 32];
   __shared__ int s_blk, s_base;
   __shared__ uint32_t s_epoch;
   __shared__ int s_old;
+  __shared__ int s_wi[kCountThreads * COW_MAX_WRITES];  // the block's write slots, bank-major
+  __shared__ int s_bad[kCountThreads];
   const int tid = threadIdx.x, lane = tid & 31;
   int l = 0;
   while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l].count_block_begin + P.layer[l].count_blocks) ++l;
   const DecodeLayer& L = P.layer[l];
   uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
+  // The decode pass may start now: it waits for this grid only where it reads
+  // the prefixes.
+  asm volatile("griddepcontrol.launch_dependents;");
   if (tid == 0) {
     s_blk = P.dynamic_tiles ? static_cast<int>(atomicAdd(&hdr[0], 1u))
                             : static_cast<int>(blockIdx.x) - L.count_block_begin;
     s_epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
     s_old = *reinterpret_cast<volatile int32_t*>(L.free_count);
   }
+  s_bad[tid] = 0;
   __syncthreads();
   const int blk = s_blk;
   const uint32_t epoch = s_epoch;
-  const int64_t bank = static_cast<int64_t>(blk) * kCountThreads + tid;
+  const int64_t bank0 = static_cast<int64_t>(blk) * kCountThreads;
+  const int64_t bank = bank0 + tid;
   const int64_t N = L.slots;
   const int W = P.writes, R = P.reads;
-  int count = 0;
-  if (bank < L.banks) {
-    const cow_step& st = L.step;
-    int wi[COW_MAX_WRITES];
-    bool bad = false;
-    for (int w = 0; w < W; ++w) {
-      const int64_t raw = ld_index(st.write_indices, bank * W + w, P.idx64);
-      const bool ok = raw >= 0 && raw < N;
-      wi[w] = ok ? static_cast<int>(raw) : -1 - w;
-      bad |= !ok;
+  const int nb = static_cast<int>(L.banks - bank0 < kCountThreads ? L.banks - bank0 : kCountThreads);
+  const cow_step& st = L.step;
+  // Route indices of the block's banks are contiguous: the whole block reads
+  // them with consecutive threads on consecutive elements.
+  // Loads of kCountUnroll elements go out before any of them is checked.
+  for (int e0 = 0; e0 < nb * W; e0 += kCountThreads * kCountUnroll) {
+    int64_t raw[kCountUnroll];
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      raw[u] = e < nb * W ? ld_index(st.write_indices, bank0 * W + e, P.idx64) : 0;
     }
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      if (e < nb * W) {
+        const bool ok = raw[u] >= 0 && raw[u] < N;
+        s_wi[e] = ok ? static_cast<int>(raw[u]) : -1 - (e % W);  // distinct sentinels never count as repeats
+        if (!ok) s_bad[e / W] = 1;
+      }
+    }
+  }
+  for (int e0 = 0; e0 < nb * R; e0 += kCountThreads * kCountUnroll) {
+    int64_t raw[kCountUnroll];
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      raw[u] = e < nb * R ? ld_index(st.read_indices, bank0 * R + e, P.idx64) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      if (e < nb * R && (raw[u] < 0 || raw[u] >= N)) s_bad[e / R] = 1;
+    }
+  }
+  int64_t tmpl = 0;
+  if (tid < nb) tmpl = L.templates[bank];
+  __syncthreads();
+  int count = 0;
+  if (tid < nb) {
+    const int* wi = s_wi + tid * W;
+    bool bad = s_bad[tid] != 0 || tmpl < 0 || tmpl >= L.template_count;
     for (int a = 1; a < W; ++a)
       for (int b = 0; b < a; ++b) bad |= wi[a] == wi[b];
-    for (int r = 0; r < R; ++r) {
-      const int64_t raw = ld_index(st.read_indices, bank * R + r, P.idx64);
-      bad |= raw < 0 || raw >= N;
+    if (!bad) {
+      for (int w0 = 0; w0 < W; w0 += 8) {
+        int32_t m[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) m[u] = w0 + u < W ? L.map[bank * N + wi[w0 + u]] : 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) count += m[u] < 0 ? 1 : 0;
+      }
     }
-    const int64_t tmpl = L.templates[bank];
-    bad |= tmpl < 0 || tmpl >= L.template_count;
-    if (!bad)
-      for (int w = 0; w < W; ++w) count += L.map[bank * N + wi[w]] < 0 ? 1 : 0;
   }
   int total;
   const int local = block_exclusive_scan_n<kCountThreads>(count, s_warp, total);
@@ -504,6 +550,23 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
     P.two_pass = 1;
     P.dynamic_tiles = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles));
+    cfg.blockDim = dim3(kBanksPerCta * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, P);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+    return launch_status();
   } else {
     P.dynamic_tiles = tiles > resident ? 1 : 0;
   }
