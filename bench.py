@@ -9,10 +9,12 @@ request through all 7 pools = one fused ``cow_decode_step`` launch.
 
 Reported numbers (one JSON line from rank 0):
 
-* ``value``: device throughput, inputs resident in HBM.  Each timed step is a
-  CUDA graph of the one fused launch; L2 is flushed (a 256 MiB write) before
-  every timed step and the step is timed alone with CUDA events on the
-  launching stream, so the pool state starts cold in HBM.
+* ``value``: device throughput, inputs resident in HBM.  The K timed steps
+  are ONE CUDA graph of K x (256 MiB L2 flush, event, the fused launch,
+  event): every step starts with a cold L2 and is timed on the device by its
+  own event pair, with no host submission gap inside any interval.
+  ``single_launch`` is the same step launched and timed alone (each interval
+  then also holds the host's submission latency).
 * ``e2e``: the same metric through the public runtime API with host buffers:
   every step copies its packed routes from pinned host memory (one copy), runs
   the capacity proof and one fused launch, and reads the readouts back to the
@@ -224,18 +226,31 @@ def run_gpu(args, rank, world, device):
     scratch = allocator.decode_scratch(device, banks * LAYERS, LAYERS)
     pools = (_lib.CowPool * LAYERS)(*[st._pool() for st in states])
     stream = torch.cuda.Stream(device)
-    graphs = []
-    with torch.cuda.stream(stream):
-        for s in range(Wm, Wm + K):
-            steps = (_lib.CowStep * LAYERS)(*[_c_step(inputs, s, l, outputs) for l in range(LAYERS)])
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                _lib.check(lib.cow_decode_step(pools, steps, LAYERS, WRITES, READS, _lib.I64, _lib.F32,
-                                               scratch.data_ptr(), scratch.numel(), stream.cuda_stream),
-                           "cow_decode_step")
-            graphs.append(g)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    step_structs = {s: (_lib.CowStep * LAYERS)(*[_c_step(inputs, s, l, outputs) for l in range(LAYERS)])
+                    for s in range(Wm, Wm + K)}
+
+    def packed_launch(s):
+        _lib.check(lib.cow_decode_step(pools, step_structs[s], LAYERS, WRITES, READS, _lib.I64, _lib.F32,
+                                       scratch.data_ptr(), scratch.numel(), stream.cuda_stream), "cow_decode_step")
+
+    def flushed_trace(launch):
+        """ONE graph of K x (L2 flush, event, step, event): every step starts with a
+        cold L2 and is timed on the device by its own event pair, with no host
+        submission gap inside any interval."""
+        evs = [(torch.cuda.Event(enable_timing=True, external=True),
+                torch.cuda.Event(enable_timing=True, external=True)) for _ in range(K)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i, s in enumerate(range(Wm, Wm + K)):
+                    flush.fill_(float(i))
+                    evs[i][0].record(stream)
+                    launch(s)
+                    evs[i][1].record(stream)
+        return g, evs
+
+    graph, ev = flushed_trace(packed_launch)
 
     def barrier():
         if world > 1:
@@ -245,11 +260,7 @@ def run_gpu(args, rank, world, device):
         barrier()
         torch.cuda.synchronize(device)
         with torch.cuda.stream(stream):
-            for s in range(K):
-                flush.fill_(float(s))
-                ev[s][0].record(stream)
-                graphs[s].replay()
-                ev[s][1].record(stream)
+            graph.replay()
         torch.cuda.synchronize(device)
         barrier()
     step_ms = [a.elapsed_time(b) for a, b in ev]
@@ -259,11 +270,28 @@ def run_gpu(args, rank, world, device):
     for st in states:
         st.validate_invariants()
 
+    # Each step as its own graph launch, timed alone (adds the host submission
+    # latency of every launch to its interval): the single-token latency.
+    single = []
+    with torch.cuda.stream(stream):
+        for s in range(Wm, Wm + min(K, 16)):
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=stream):
+                packed_launch(s)
+            flush.fill_(float(s))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g1.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            single.append(e0.elapsed_time(e1))
+    single_ms = statistics.median(single)
+
     # Warm-L2 trace: all K steps captured in ONE graph and replayed back to
     # back (no host in the loop; the pool state stays L2-resident).  The
     # routes are re-applied to the evolved state; with every slot of every
     # bank already private nothing is allocated.
-    warm = dense_warm = dense_ms = None
+    warm = dense_warm = dense_ms = incremental = None
     if rank == 0:
         def trace_graph(launch):
             g = torch.cuda.CUDAGraph()
@@ -284,13 +312,6 @@ def run_gpu(args, rank, world, device):
             torch.cuda.synchronize(device)
             return e0.elapsed_time(e1)
 
-        step_structs = {s: (_lib.CowStep * LAYERS)(*[_c_step(inputs, s, l, outputs) for l in range(LAYERS)])
-                        for s in range(Wm, Wm + K)}
-
-        def packed_launch(s):
-            _lib.check(lib.cow_decode_step(pools, step_structs[s], LAYERS, WRITES, READS, _lib.I64, _lib.F32,
-                                           scratch.data_ptr(), scratch.numel(), stream.cuda_stream), "cow_decode_step")
-
         warm = time_graph(trace_graph(packed_launch))
 
         # Dense-table control, same routes, same timing disciplines.
@@ -303,15 +324,29 @@ def run_gpu(args, rank, world, device):
                                           READS, _lib.I64, _lib.F32, stream.cuda_stream), "cow_dense_step")
 
         dense_warm = time_graph(trace_graph(dense_launch))
-        dev_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        dgraph, dev_ev = flushed_trace(dense_launch)
         with torch.cuda.stream(stream):
-            for i, s in enumerate(range(Wm, Wm + K)):
-                flush.fill_(float(i))
-                dev_ev[i][0].record(stream)
-                dense_launch(s)
-                dev_ev[i][1].record(stream)
+            dgraph.replay()
         torch.cuda.synchronize(device)
         dense_ms = sum(a.elapsed_time(b) for a, b in dev_ev)
+
+        # Incremental device time of a cold step inside a graph: a graph of
+        # K x (flush, step) against a graph of K x flush.  Event nodes around a
+        # microsecond-scale kernel add their own scheduling to its interval;
+        # the difference of two whole-graph times does not.
+        def flushed_only(launch):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    for i, s in enumerate(range(Wm, Wm + K)):
+                        flush.fill_(float(i))
+                        if launch is not None:
+                            launch(s)
+            return g
+
+        base = time_graph(flushed_only(None))
+        incremental = {"packed_us": 1e3 * (time_graph(flushed_only(packed_launch)) - base) / K,
+                       "dense_us": 1e3 * (time_graph(flushed_only(dense_launch)) - base) / K}
         del mems
 
     # End to end through the public runtime API with host buffers: every step
@@ -365,7 +400,8 @@ def run_gpu(args, rank, world, device):
         for k, v in st.storage_bytes().items():
             state_bytes[k] = state_bytes.get(k, 0) + v
     used = [st.used_bytes() for st in states]
-    return dict(total_ms=total_ms, step_ms=step_ms, e2e_ms=e2e_ms, e2e_serial_ms=e2e_serial_ms, warm_ms=warm,
+    return dict(total_ms=total_ms, step_ms=step_ms, single_ms=single_ms, e2e_ms=e2e_ms, e2e_serial_ms=e2e_serial_ms,
+                warm_ms=warm, incremental=incremental,
                 dense_ms=dense_ms,
                 dense_warm_ms=dense_warm,
                 first_touches=first_touches, h2d=h2d, d2h=d2h, clocks=clocks.summary(), setup_s=setup_s,
@@ -970,7 +1006,8 @@ def config_block(world: int) -> dict:
             "layers": LAYERS, "slots": SLOTS, "width": WIDTH, "heads": HEADS, "reads": READS, "writes": WRITES,
             "growth_quantum_rows": max(16, BATCH * HEADS * WRITES * QUANTUM_STEPS),
             "parallelism": f"requests sharded, {BATCH} per GPU x {world} GPU(s), no collective",
-            "l2": "flushed (256 MiB write) before every timed step; each step timed alone"}
+            "l2": "flushed (256 MiB write) before every timed step, inside one CUDA graph; each step timed "
+                  "by its own device event pair"}
 
 
 def main() -> int:
@@ -1065,6 +1102,13 @@ def main() -> int:
                 "serial": {"value": tokens / (res["e2e_serial_ms"] / 1e3), "unit": "tokens/s",
                            "path": "DecodeSession.step_host: copy, decode and read back one step at a time"}},
         "gpu_launches": K,
+        "graph_incremental": None if res["incremental"] is None else {
+            **res["incremental"],
+            "packed_latency_overhead_pct": 100.0 * (res["incremental"]["packed_us"] / res["incremental"]["dense_us"] - 1.0),
+            "note": "cold step's added device time in a graph of K x (L2 flush, step) minus K x flush"},
+        "single_launch": {"value": BATCH / (res["single_ms"] / 1e3), "unit": "tokens/s",
+                          "ms_per_step": res["single_ms"],
+                          "note": "one step per graph launch, timed alone (median); includes host submission"},
         "clocks": res["clocks"],
         "cpu_baseline": cpu,
         "dense_control": None if res["dense_ms"] is None else {
