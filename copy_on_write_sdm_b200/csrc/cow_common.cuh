@@ -168,7 +168,7 @@ struct DecodeLaunch {
   uint64_t* flags;        // one per bank slot, pool-major (tile_begin * 4 + bank)
   uint64_t* group_flags;  // one per group of kScanGroup banks, pool-major (group_begin + group)
   int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, read_stage_bytes;
-  int32_t two_pass, _pad;
+  int32_t two_pass, counter_close;  // counter_close: pools close by arrival count (cow_decode_kernel)
 };
 
 constexpr uint32_t kFlagAggregate = 1u;

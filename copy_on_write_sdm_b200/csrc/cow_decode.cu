@@ -13,8 +13,10 @@
 // ordered by a dynamic ticket so a tile only ever waits on tiles that already
 // started.  First touches depend only on the pre-step map, so every row load
 // is in flight before the scan resolves, and banks without first touches
-// (other than the banks that publish totals) never wait on it; only the
-// placement of first-touch rows needs it.  Every wait is bounded and reports
+// (other than the banks that publish group totals) never wait on it; only the
+// placement of first-touch rows needs it.  The pool's free count and scan
+// epoch are advanced by the bank that arrives last (an atomic arrival count),
+// so closing a pool waits on nobody either.  Every wait is bounded and reports
 // COW_ST_WAIT_TIMEOUT instead of hanging.
 
 
@@ -27,6 +29,11 @@ namespace {
 // --------------------------------------------------------------------------
 // fused packed decode step
 // --------------------------------------------------------------------------
+
+// Single-pass launches close each pool by arrival count: header word 0 of the
+// pool counts arrived banks above bit kCloseShift and their first touches
+// below it (the host enables this when both fields fit).
+constexpr int kCloseShift = 18;
 
 template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
@@ -68,9 +75,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   uint64_t* const flags = P.flags + static_cast<int64_t>(L.tile_begin) * kBanksPerCta;
 
   // Round 1: everything that does not depend on the routes.  The epoch and
-  // the free count are read before this warp publishes anything; the pool's
-  // last bank rewrites them only after every bank has published, so all
-  // banks see the launch's starting values.
+  // the free count are read before this warp publishes or arrives; the bank
+  // that closes the pool rewrites them only after every bank has done so, so
+  // all banks see the launch's starting values.
   uint32_t epoch = 0;
   int old_free = 0, excl_given = 0;
   if (lane == 0) {
@@ -102,9 +109,13 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   epoch = __shfl_sync(kFull, epoch, 0);
   old_free = __shfl_sync(kFull, old_free, 0);
   const int count = __popc(first_mask);
+  uint32_t arrived = 0;
   if (lane == 0 && !P.two_pass) {
     *reinterpret_cast<volatile uint64_t*>(flags + bank) =
         pack_flag(epoch, kFlagAggregate, static_cast<uint32_t>(count));
+    // Arrival: this bank has read the pool's starting epoch and free count (the
+    // values were consumed by the shuffles above, so the reads are complete).
+    if (P.counter_close) arrived = atomicAdd(&hdr[0], (1u << kCloseShift) + static_cast<uint32_t>(count));
   }
 
   // Row traffic: every read row (shared memory) or the first read group
@@ -151,10 +162,25 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     if constexpr (!kStageReads) load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
   }
 
+  // The bank that arrived last closes the pool: every other bank has read the
+  // starting epoch and free count, and the arrivals carried their first
+  // touches.  Its stores depend on the atomic's result, so they cannot be
+  // performed before the other banks' reads; no fence (which would also wait
+  // for this warp's row loads) is needed.
+  if (lane == 0 && P.counter_close && static_cast<int64_t>(arrived >> kCloseShift) == L.banks - 1) {
+    const int total = static_cast<int>(arrived & ((1u << kCloseShift) - 1u)) + count;
+    if (total > 0) {
+      const int remaining = old_free - total;
+      *L.free_count = remaining > 0 ? remaining : 0;
+    }
+    hdr[0] = 0u;
+    *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+  }
+
   // Exclusive prefix of first touches over the preceding banks of this pool
   // (two-level scan, about one round trip), overlapped with the row loads
-  // above.  Only banks that place rows, close the pool or publish a scan
-  // group's total need it.
+  // above.  Only banks that place rows, close the pool by look-back or
+  // publish a scan group's total need it.
   int excl;
   if (P.two_pass) {
     // cow_count_kernel produced this bank's prefix and the pool's starting free
@@ -169,7 +195,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     }
     excl = __shfl_sync(kFull, excl_given, 0);
     old_free = __shfl_sync(kFull, old_free, 0);
-  } else if (count == 0 && bank != L.banks - 1 && bank % kScanGroup != kScanGroup - 1) {
+  } else if (count == 0 && (P.counter_close || bank != L.banks - 1) && bank % kScanGroup != kScanGroup - 1) {
     // Nothing to place, not the bank that closes the pool and not the bank
     // that publishes its scan group's total: the prefix is not needed.
     excl = 0;
@@ -177,7 +203,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     bool timed_out = false;
     excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
     if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
-    if (lane == 0) {
+    if (lane == 0 && !P.counter_close) {
       const int inclusive = excl + count;
       if (bank == L.banks - 1) {
         // Every bank of this pool has published, hence has read the starting
@@ -569,6 +595,14 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     return launch_status();
   } else {
     P.dynamic_tiles = tiles > resident ? 1 : 0;
+    // The arrival count shares header word 0 with the tile ticket; it serves
+    // launches without dynamic tiles whose banks and first touches per pool
+    // fit its two fields.  Otherwise the pool's last bank closes it by look-back.
+    bool fits = !P.dynamic_tiles;
+    for (int l = 0; l < layers; ++l)
+      fits = fits && pools[l].banks < (int64_t(1) << (32 - kCloseShift)) &&
+             pools[l].banks * writes < (int64_t(1) << kCloseShift);
+    P.counter_close = fits ? 1 : 0;
   }
   fn<<<tiles, kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
