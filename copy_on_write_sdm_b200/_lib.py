@@ -108,6 +108,8 @@ _SIGNATURES = {
     "cow_retain": (c_int32, [POINTER(CowPool), P, c_int64, P, P, P, P, P]),
     "cow_validate": (c_int32, [POINTER(CowPool), P, P, P]),
     "cow_materialize": (c_int32, [POINTER(CowPool), P, c_int32, P]),
+    "cow_route_controller": (c_int32, [P, P, P, P, P, P, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
+                                       P, P, P, P, P, P, P]),
     "cow_release_workspace_bytes": (c_int64, [POINTER(CowPool), P, c_int32]),
     "cow_release_layers": (c_int32, [POINTER(CowPool), P, P, c_int32, P, c_int64, P, P]),
     "cow_retain_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32]),

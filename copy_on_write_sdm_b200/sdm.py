@@ -21,6 +21,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import _lib
 from .allocator import PackedSDMCopyOnWriteState
 
 
@@ -154,6 +155,8 @@ class SparseDeltaMemory(nn.Module):
             raise ValueError(f"SDM tokens must be [B,T,{self.width}]")
         batch, time, _ = tokens.shape
         normalized = self.input_norm(tokens)
+        if self._fused_routes_ok(tokens):
+            return self._controller_fused(normalized, batch, time)
         read_w, read_i = product_key_routes(self._per_bank(self.read_projection(normalized), batch, time).reshape(
             batch * self.memory_heads, time, -1), slots=self.slots, selected=self.reads)
         write_w, write_i = product_key_routes(self._per_bank(self.write_projection(normalized), batch, time),
@@ -168,6 +171,40 @@ class SparseDeltaMemory(nn.Module):
             forget_log_gate=forget.permute(0, 2, 1).reshape(batch * self.memory_heads, time),
             read_indices=read_i, read_weights=read_w,
         )
+
+    def _fused_routes_ok(self, tokens: torch.Tensor) -> bool:
+        root = math.isqrt(self.slots)
+        return (tokens.is_cuda and tokens.dtype == torch.float32 and root <= 256 and self.reads <= 32
+                and self.writes <= 32 and min(self.reads, root) <= 32 and min(self.writes, root) <= 32
+                and all(p.dtype == torch.float32 for p in (self.A_log, self.dt_bias)))
+
+    def _controller_fused(self, normalized: torch.Tensor, batch: int, time: int) -> SDMStepInputs:
+        """The same outputs as the PyTorch controller; the route selection and gates
+        run as one ``cow_route_controller`` launch (FP32 activations)."""
+        H = self.memory_heads
+        device = normalized.device
+        rp = self.read_projection(normalized).contiguous()
+        wp = self.write_projection(normalized).contiguous()
+        fp = self.forget_projection(normalized).contiguous()
+        ip = self.input_projection(normalized).contiguous()
+        a_log = self.A_log.detach().contiguous()
+        dt_bias = self.dt_bias.detach().contiguous()
+        banks = batch * H
+        read_i = torch.empty(banks, time, self.reads, dtype=torch.int64, device=device)
+        read_w = torch.empty(banks, time, self.reads, dtype=torch.float32, device=device)
+        write_i = torch.empty(banks, time, self.writes, dtype=torch.int64, device=device)
+        write_w = torch.empty(banks, time, self.writes, dtype=torch.float32, device=device)
+        gate_in = torch.empty(banks, time, dtype=torch.float32, device=device)
+        forget = torch.empty(banks, time, dtype=torch.float32, device=device)
+        _lib.check(_lib.load().cow_route_controller(
+            rp.data_ptr(), wp.data_ptr(), fp.data_ptr(), ip.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
+            batch, time, H, math.isqrt(self.slots), self.reads, self.writes, read_i.data_ptr(), read_w.data_ptr(),
+            write_i.data_ptr(), write_w.data_ptr(), gate_in.data_ptr(), forget.data_ptr(),
+            _lib.stream_of(device)), "cow_route_controller")
+        values = self._per_bank(self.value_projection(normalized), batch, time)
+        return SDMStepInputs(
+            normalized=normalized, write_indices=write_i, write_weights=write_w, values=values.contiguous(),
+            input_gate=gate_in, forget_log_gate=forget, read_indices=read_i, read_weights=read_w)
 
     def finish(self, normalized: torch.Tensor, readings: torch.Tensor) -> torch.Tensor:
         """Readings norm, channel gate and output projection (reference inference.py:522-535)."""

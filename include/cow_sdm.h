@@ -322,6 +322,18 @@ int64_t cow_validate_workspace_bytes(const cow_pool* pools, int32_t layers);
 int cow_validate_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* out,
                         void* stream);
 
+/* Controller route selection (sdm.py:96-159, inference.py:459-519), FP32: from
+ * the read / write codebook projections [B,T,H*2*root] and the forget / input
+ * gate projections [B,T,H], one warp per (bank = b*H+h, position t) writes the
+ * product-key addresses (sorted ascending) and softmax weights [B*H,T,R|W],
+ * forget_log_gate = -exp(A_log[h]) * softplus(f + dt_bias[h]) and
+ * input_gate = sigmoid(i) [B*H,T].  root = sqrt(N) <= 256, R, W <= 32. */
+int cow_route_controller(const float* read_proj, const float* write_proj, const float* forget_proj,
+                         const float* input_proj, const float* a_log, const float* dt_bias, int64_t batch,
+                         int64_t time, int32_t heads, int32_t root, int32_t reads, int32_t writes,
+                         int64_t* read_indices, float* read_weights, int64_t* write_indices, float* write_weights,
+                         float* input_gate, float* forget_log_gate, void* stream);
+
 /* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
 
