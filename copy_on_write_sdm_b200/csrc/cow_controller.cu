@@ -77,49 +77,117 @@ __device__ __forceinline__ void warp_topk(float (&x)[SLOTS], int n, int count, f
   }
 }
 
+// Candidate pairs (i+1)(j+1) <= k for k <= 32: sum over i of floor(32 / (i+1)) = 119.
+constexpr int kRouteMaxCand = 128;
+
 struct RouteSmem {
   float av[kRouteMaxShort], bv[kRouteMaxShort];
   int ai[kRouteMaxShort], bi[kRouteMaxShort];
   float pv[kRouteMaxShort];
   int pi[kRouteMaxShort];
+  int cp[kRouteMaxCand];  // candidate pairs, i * kRouteMaxShort + j
 };
 
-// Product-key selection of `k` addresses for one row of scores (2*root values).
-__device__ __forceinline__ void select_routes(const float* scores, int root, int k, RouteSmem& sm, int lane,
-                                              int64_t* out_idx, float* out_w) {
-  constexpr int kSlots = 2 * kRouteMaxRoot / 32;  // 16 values per lane at most
-  const int short_len = k < root ? k : root;
-  float half[kSlots / 2];
-  // first codebook half
+// Shortlist of one codebook half: its best `short_len` entries, best first.
+// Halves of at most 32 entries take one rank per lane (every lane counts the
+// entries ahead of its own: larger, or equal at a smaller index); longer
+// halves take `short_len` arg-max rounds.
+template <int HALF_SLOTS>
+__device__ __forceinline__ void shortlist(const float* scores, int root, int short_len, float* out_v, int* out_i,
+                                          int lane) {
+  if (root <= 32) {
+    const float x = lane < root ? scores[lane] : kNegInf;
+    int rank = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+      const float v = __shfl_sync(kFull, x, j);
+      rank += (j < root && (v > x || (v == x && j < lane))) ? 1 : 0;
+    }
+    if (lane < root && rank < short_len) {
+      out_v[rank] = x;
+      out_i[rank] = lane;
+    }
+    __syncwarp();
+    return;
+  }
+  float half[HALF_SLOTS];
 #pragma unroll
-  for (int j = 0; j < kSlots / 2; ++j) {
+  for (int j = 0; j < HALF_SLOTS; ++j) {
     const int e = j * 32 + lane;
     half[j] = e < root ? scores[e] : kNegInf;
   }
-  warp_topk<kSlots / 2>(half, root, short_len, sm.av, sm.ai, lane);
+  warp_topk<HALF_SLOTS>(half, root, short_len, out_v, out_i, lane);
+}
+
+// Product-key selection of `k` addresses for one row of scores (2*root values).
+// With both shortlists sorted best first, pair (i, j) has at least
+// (i+1)(j+1) - 1 pairs at least as good ahead of it, so only pairs with
+// (i+1)(j+1) <= k can be among the best k: at most ~4k candidates instead of
+// short^2 (ties between equal sums aside, the same selection).
+__device__ __forceinline__ void select_routes(const float* scores, int root, int k, RouteSmem& sm, int lane,
+                                              int64_t* out_idx, float* out_w) {
+  constexpr int kHalfSlots = kRouteMaxRoot / 32;  // 8 values per lane at most
+  const int short_len = k < root ? k : root;
+  shortlist<kHalfSlots>(scores, root, short_len, sm.av, sm.ai, lane);
+  shortlist<kHalfSlots>(scores + root, root, short_len, sm.bv, sm.bi, lane);
+  // candidates: lane i < short_len owns pairs (i, j), j < min(short, k / (i+1)),
+  // written to sm.cp at that lane's exclusive prefix
+  const int lim = lane < short_len ? min(short_len, k / (lane + 1)) : 0;
+  int incl = lim;
 #pragma unroll
-  for (int j = 0; j < kSlots / 2; ++j) {
-    const int e = j * 32 + lane;
-    half[j] = e < root ? scores[root + e] : kNegInf;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += y;
   }
-  warp_topk<kSlots / 2>(half, root, short_len, sm.bv, sm.bi, lane);
-  // pair (i, j) at flat position i * short + j, score a_i + b_j
-  const int pairs = short_len * short_len;
-  constexpr int kPairSlots = kRouteMaxShort * kRouteMaxShort / 32;
-  float ps[kPairSlots];
+  const int total = __shfl_sync(kFull, incl, 31);
+  for (int j = 0; j < lim; ++j) sm.cp[incl - lim + j] = lane * kRouteMaxShort + j;
+  __syncwarp();
+  constexpr int kCandSlots = kRouteMaxCand / 32;
+  float ps[kCandSlots];
+  int pp[kCandSlots];
 #pragma unroll
-  for (int j = 0; j < kPairSlots; ++j) {
-    const int p = j * 32 + lane;
-    ps[j] = p < pairs ? sm.av[p / short_len] + sm.bv[p % short_len] : kNegInf;
+  for (int j = 0; j < kCandSlots; ++j) {
+    const int c = j * 32 + lane;
+    pp[j] = c < total ? sm.cp[c] : 0;
+    ps[j] = c < total ? sm.av[pp[j] / kRouteMaxShort] + sm.bv[pp[j] % kRouteMaxShort] : kNegInf;
   }
-  const int take = k < pairs ? k : pairs;
-  warp_topk<kPairSlots>(ps, pairs, take, sm.pv, sm.pi, lane);
+  const int take = k < total ? k : total;
+  // `take` arg-max rounds over the candidates; a tie goes to the smaller (i, j)
+  for (int s = 0; s < take; ++s) {
+    float v = kNegInf;
+    int key = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kCandSlots; ++j) {
+      const int c = j * 32 + lane;
+      if (c < total && (ps[j] > v || (ps[j] == v && pp[j] < key))) {
+        v = ps[j];
+        key = pp[j];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, v, o);
+      const int ok = __shfl_xor_sync(kFull, key, o);
+      if (ov > v || (ov == v && ok < key)) {
+        v = ov;
+        key = ok;
+      }
+    }
+    if (lane == 0) {
+      sm.pv[s] = v;
+      sm.pi[s] = key;
+    }
+#pragma unroll
+    for (int j = 0; j < kCandSlots; ++j)
+      if (j * 32 + lane < total && pp[j] == key) ps[j] = kNegInf;
+  }
+  __syncwarp();
   // lane s < take holds selected pair s; addresses ascending, softmax weights
   int addr = 0x7fffffff;
   float v = kNegInf;
   if (lane < take) {
     const int p = sm.pi[lane];
-    addr = sm.ai[p / short_len] * root + sm.bi[p % short_len];
+    addr = sm.ai[p / kRouteMaxShort] * root + sm.bi[p % kRouteMaxShort];
     v = sm.pv[lane];
   }
   float m = v;
@@ -154,11 +222,13 @@ __global__ void __launch_bounds__(128) cow_route_kernel(const __grid_constant__ 
   const int64_t tok = b * P.time + t;  // row of the [B, T, ...] projections
   const int key_w = 2 * P.root;
   auto& sm = s_sm[warp];
-  select_routes(P.read_proj + (tok * H + h) * key_w, P.root, P.reads, sm, lane, P.read_indices + row * P.reads,
-                P.read_weights + row * P.reads);
-  __syncwarp();
-  select_routes(P.write_proj + (tok * H + h) * key_w, P.root, P.writes, sm, lane,
-                P.write_indices + row * P.writes, P.write_weights + row * P.writes);
+  auto select = [&](const float* scores, int k, int64_t* idx, float* w) {
+    select_routes(scores, P.root, k, sm, lane, idx, w);
+    __syncwarp();
+  };
+  select(P.read_proj + (tok * H + h) * key_w, P.reads, P.read_indices + row * P.reads, P.read_weights + row * P.reads);
+  select(P.write_proj + (tok * H + h) * key_w, P.writes, P.write_indices + row * P.writes,
+         P.write_weights + row * P.writes);
   if (lane == 0) {
     const float x = P.forget_proj[tok * H + h] + P.dt_bias[h];
     const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, threshold 20
