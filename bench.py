@@ -949,7 +949,7 @@ def main_model(args, rank, world, device) -> int:
         "cpu_baseline_note": "the CPU port covers the SDM step and allocator, not the whole model",
         "retained_state": res["state_bytes"], "setup_s": res["setup_s"],
     }
-    print(json.dumps(line))
+    emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -1010,6 +1010,25 @@ def config_block(world: int) -> dict:
                   "by its own device event pair"}
 
 
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the one result line to the process's original stdout."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _reserve_stdout() -> None:
+    """Keep the original stdout for the result line and send everything else that
+    writes to file descriptor 1 (library banners, NCCL) to stderr."""
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1027,6 +1046,7 @@ def main() -> int:
     ap.add_argument("--churn-warm-prefix", type=int, default=CH_WARM_PREFIX,
                     help="churn: prefix tokens of the initial batch")
     args = ap.parse_args()
+    _reserve_stdout()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
@@ -1045,7 +1065,7 @@ def main() -> int:
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": config_block(args.gpus), "cpu_baseline": cpu,
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
+        emit(line)
         return 0
 
     device = torch.device("cuda", local)
@@ -1126,7 +1146,7 @@ def main() -> int:
         "first_touches_in_timed_steps": res["first_touches"],
         "setup_s": res["setup_s"],
     }
-    print(json.dumps(line))
+    emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -1168,7 +1188,7 @@ def main_scaleout(args, rank, world, device) -> int:
         "first_touches_in_timed_steps": res["first_touches"], "retained_state": res["state_bytes"],
         "setup_s": res["setup_s"],
     }
-    print(json.dumps(line))
+    emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -1208,7 +1228,7 @@ def main_churn(args, rank, world, device) -> int:
         "cpu_baseline": cpu_churn_rate(args.cpu_seconds, args.quantum_steps),
         "setup_s": res["setup_s"],
     }
-    print(json.dumps(line))
+    emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
