@@ -114,11 +114,13 @@ class PackedSDMCopyOnWriteState:
     _m0_f32: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
     def __setattr__(self, name: str, value) -> None:
-        # Descriptor caches (DecodeSession, GraphedDecode) compare this counter
-        # to learn that a tensor of the pool was replaced.
+        # Caches in DecodeSession and GraphedDecode compare these counters: one
+        # counts replaced tensors (descriptors), one every assignment (proofs).
         object.__setattr__(self, name, value)
+        d = self.__dict__
+        d["_mutations"] = d.get("_mutations", 0) + 1
         if name in _TENSOR_FIELDS:
-            object.__setattr__(self, "_tensor_version", self.__dict__.get("_tensor_version", 0) + 1)
+            d["_tensor_version"] = d.get("_tensor_version", 0) + 1
 
     # ---------------- construction ----------------
 

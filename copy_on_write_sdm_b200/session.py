@@ -112,6 +112,7 @@ class DecodeSession:
         self._pool_array = None
         self._scratch = decode_scratch(self.device, B * len(pools), len(pools))
         self._need = B * writes  # first touches one step can make in a pool
+        self._proof_steps, self._proof_key = 0, None
         self._out_bytes = self.host_outputs.numel() * self.host_outputs.element_size()
         self._device_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._lib = _lib.load()
@@ -131,10 +132,22 @@ class DecodeSession:
         return self._pool_array
 
     def _prove(self) -> None:
-        """The reference's per-step capacity proof (allocator.py:746-774) for every pool;
-        the common case (enough proven rows left) is a host counter decrement."""
+        """The reference's per-step capacity proof (allocator.py:746-774) for every pool.
+
+        The common case (every pool proven with rows left for this step) is one
+        decrement per pool: after a full check the session knows how many steps
+        every pool's proof still covers, and keeps that count while no pool was
+        assigned to since (its ``_mutations`` counter is unchanged)."""
         need = self._need
-        for p in self.pools:
+        pools = self.pools
+        if self._proof_steps > 0 and self._proof_key == tuple(p.__dict__["_mutations"] for p in pools):
+            self._proof_steps -= 1
+            for p in pools:
+                d = p.__dict__
+                d["proven_maximum_additional_allocations"] -= need
+            return
+        steps = None
+        for p in pools:
             d = p.__dict__
             if d["growth_quantum_rows"]:
                 left = d["proven_maximum_additional_allocations"]
@@ -142,8 +155,14 @@ class DecodeSession:
                     d["proven_maximum_additional_allocations"] = left - need
                 else:
                     p.prepare_step_capacity(need)
+                left = d["proven_maximum_additional_allocations"] // need if need else 1 << 30
+                steps = left if steps is None else min(steps, left)
             elif not d["capacity_is_proven"]:
                 raise ValueError("SDM COW capacity has no decode proof")
+            else:
+                steps = 0  # fixed pools keep the full check (no counter to decrement)
+        self._proof_steps = steps or 0
+        self._proof_key = tuple(p.__dict__["_mutations"] for p in pools)
 
     def _stream_handle(self) -> int:
         return _current_raw_stream(self._device_index)
