@@ -39,9 +39,11 @@ template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_decode_kernel(const __grid_constant__ DecodeLaunch P) {
   // Common shapes (f32 rows, R <= 32, width <= 128) copy their read rows into
-  // shared memory (cp.async) rather than holding them in registers.
+  // shared memory with bulk copies (one per row, on a per-warp mbarrier)
+  // rather than holding them in registers.
   constexpr bool kStageReads = RC == 1 && CH == 1 && SDT == COW_F32;
   __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta];
+  __shared__ uint64_t s_bar[kBanksPerCta];  // per warp: the read-row copies' barrier
   __shared__ int s_tile;
   // dynamic: [read rows, per warp R x D floats (kStageReads)] [map rows, per warp N ints (P.stage_map)]
   extern __shared__ __align__(16) unsigned char dyn_smem[];
@@ -146,17 +148,21 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       }
     }
     if constexpr (kStageReads) {
-      if (lane * 4 < D) {
-#pragma unroll 4
-        for (int r = 0; r < R; ++r) {
-          const int src = sm.rsrc[r];
-          if (src >= 0) {
-            cp_async16(s_reads + r * D + lane * 4,
-                       static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D + lane * 4);
-          } else if (src == -1) {
-            cp_async16(s_reads + r * D + lane * 4, L.m0 + (m0_base + sm.ridx[r]) * D + lane * 4);
-          }
-        }
+      // Lane r requests read row r as one bulk copy (R <= 32); the warp's
+      // barrier completes when all the bytes have landed.
+      uint64_t* bar = &s_bar[warp];
+      const int src = lane < R ? sm.rsrc[lane] : -2;
+      const bool copy = src >= -1;
+      const unsigned n_rows = __popc(__ballot_sync(kFull, copy));
+      if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_arrive_expect_tx(bar, n_rows * static_cast<unsigned>(D) * 4u);
+      }
+      __syncwarp();
+      if (copy) {
+        const float* row = src >= 0 ? static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D
+                                    : L.m0 + (m0_base + sm.ridx[lane]) * D;
+        bulk_row_copy(s_reads + lane * D, row, static_cast<unsigned>(D) * 4u, bar);
       }
     }
     if constexpr (!kStageReads) load_read_group<SDT, CH>(v0, wt0, sm, 0, R, L.slab, 0, L.m0, m0_base, lane, D);
@@ -238,8 +244,11 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       }
     }
     if constexpr (kStageReads) {
-      // Each lane reads back only the 16-byte chunks it copied itself.
-      cp_async_wait_all();
+      if (!mbar_wait(&s_bar[warp], 0, kSpinLimit)) {
+        // Report, then wait (bounded again) so no copy lands after the warp exits.
+        if (lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+        mbar_wait(&s_bar[warp], 0, kSpinLimit);
+      }
       if (lane * 4 < D) {
         for (int r = 0; r < R; ++r) {
           if (sm.rsrc[r] >= -1) acc[0] = f4_axpy(sm.rw[r], *reinterpret_cast<const float4*>(s_reads + r * D + lane * 4), acc[0]);
