@@ -108,6 +108,8 @@ _SIGNATURES = {
     "cow_retain": (c_int32, [POINTER(CowPool), P, c_int64, P, P, P, P, P]),
     "cow_validate": (c_int32, [POINTER(CowPool), P, P, P]),
     "cow_materialize": (c_int32, [POINTER(CowPool), P, c_int32, P]),
+    "cow_controller_step": (c_int32, [P, P, P, ctypes.c_float, P, P, P, P, c_int64, c_int64, c_int32, c_int32,
+                                      c_int32, c_int32, c_int32, P, P, P, P, P, P, P, P, P]),
     "cow_route_controller": (c_int32, [P, P, P, P, P, P, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
                                        P, P, P, P, P, P, P]),
     "cow_release_workspace_bytes": (c_int64, [POINTER(CowPool), P, c_int32]),

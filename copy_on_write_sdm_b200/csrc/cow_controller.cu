@@ -237,6 +237,110 @@ __global__ void __launch_bounds__(128) cow_route_kernel(const __grid_constant__ 
   }
 }
 
+// Whole controller for one token row (b, t): layer norm, the read / write /
+// value / forget / input projections (weights concatenated and transposed to
+// [width, Ntot] so that consecutive threads read consecutive outputs), then
+// per bank h the route selection, the gates and the value slice.
+struct ControllerLaunch {
+  const float* tokens;      // [B*T, width]
+  const float* ln_w;        // [width]
+  const float* ln_b;
+  const float* wt;          // [width, Ntot]: read H*2root | write H*2root | value width | forget H | input H
+  const float* bias;        // [Ntot]
+  const float* a_log;       // [H]
+  const float* dt_bias;     // [H]
+  float* normalized;        // [B*T, width]
+  int64_t* read_indices;    // [B*H, T, R]
+  float* read_weights;
+  int64_t* write_indices;   // [B*H, T, W]
+  float* write_weights;
+  float* values;            // [B*H, T, width / H]
+  float* input_gate;        // [B*H, T]
+  float* forget_log_gate;
+  int64_t batch, time;
+  float eps;
+  int32_t width, heads, root, reads, writes, ntot;
+};
+
+constexpr int kCtrlThreads = 128;
+constexpr int kCtrlMaxWidth = 512;
+constexpr int kCtrlMaxOut = 4096;
+
+__global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __grid_constant__ ControllerLaunch P) {
+  __shared__ float s_x[kCtrlMaxWidth];
+  __shared__ float s_out[kCtrlMaxOut];
+  __shared__ float s_red[2][kCtrlThreads / 32];
+  __shared__ RouteSmem s_sm[kCtrlThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t tok = blockIdx.x;  // b * T + t
+  const int width = P.width, H = P.heads, key_w = 2 * P.root;
+  // layer norm: mean, then variance of the centred values (two passes over shared memory)
+  float sum = 0.f;
+  for (int k = tid; k < width; k += kCtrlThreads) {
+    const float v = P.tokens[tok * width + k];
+    s_x[k] = v;
+    sum += v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
+  if (lane == 0) s_red[0][warp] = sum;
+  __syncthreads();
+  float mean = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCtrlThreads / 32; ++w) mean += s_red[0][w];
+  mean /= static_cast<float>(width);
+  float sq = 0.f;
+  for (int k = tid; k < width; k += kCtrlThreads) {
+    const float d = s_x[k] - mean;
+    sq += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+  if (lane == 0) s_red[1][warp] = sq;
+  __syncthreads();
+  float var = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCtrlThreads / 32; ++w) var += s_red[1][w];
+  const float rstd = rsqrtf(var / static_cast<float>(width) + P.eps);
+  for (int k = tid; k < width; k += kCtrlThreads) {
+    const float nv = (s_x[k] - mean) * rstd * P.ln_w[k] + P.ln_b[k];
+    P.normalized[tok * width + k] = nv;
+    s_x[k] = nv;
+  }
+  __syncthreads();
+  // projections
+  for (int o = tid; o < P.ntot; o += kCtrlThreads) {
+    float acc = P.bias[o];
+    for (int k = 0; k < width; ++k) acc = fmaf(s_x[k], P.wt[static_cast<int64_t>(k) * P.ntot + o], acc);
+    s_out[o] = acc;
+  }
+  __syncthreads();
+  const int64_t b = tok / P.time, t = tok % P.time;
+  const int hw = width / H;
+  const float* rproj = s_out;
+  const float* wproj = s_out + H * key_w;
+  const float* vproj = wproj + H * key_w;
+  const float* fproj = vproj + width;
+  const float* iproj = fproj + H;
+  for (int h = warp; h < H; h += kCtrlThreads / 32) {
+    const int64_t row = (b * H + h) * P.time + t;
+    auto& sm = s_sm[warp];
+    select_routes(rproj + h * key_w, P.root, P.reads, sm, lane, P.read_indices + row * P.reads,
+                  P.read_weights + row * P.reads);
+    __syncwarp();
+    select_routes(wproj + h * key_w, P.root, P.writes, sm, lane, P.write_indices + row * P.writes,
+                  P.write_weights + row * P.writes);
+    __syncwarp();
+    for (int k = lane; k < hw; k += 32) P.values[row * hw + k] = vproj[h * hw + k];
+    if (lane == 0) {
+      const float x = fproj[h] + P.dt_bias[h];
+      const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, threshold 20
+      P.forget_log_gate[row] = -expf(P.a_log[h]) * sp;
+      P.input_gate[row] = 1.f / (1.f + expf(-iproj[h]));
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -259,6 +363,29 @@ int cow_route_controller(const float* read_proj, const float* write_proj, const 
   RouteLaunch P{read_proj, write_proj, forget_proj, input_proj, a_log, dt_bias, read_indices, read_weights,
                 write_indices, write_weights, input_gate, forget_log_gate, batch, time, heads, root, reads, writes};
   cow_route_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, as_stream(stream)>>>(P);
+  return launch_status();
+}
+
+int cow_controller_step(const float* tokens, const float* ln_weight, const float* ln_bias, float eps,
+                        const float* weights_t, const float* bias, const float* a_log, const float* dt_bias,
+                        int64_t batch, int64_t time, int32_t width, int32_t heads, int32_t root, int32_t reads,
+                        int32_t writes, float* normalized, int64_t* read_indices, float* read_weights,
+                        int64_t* write_indices, float* write_weights, float* values, float* input_gate,
+                        float* forget_log_gate, void* stream) {
+  if (!tokens || !ln_weight || !ln_bias || !weights_t || !bias || !a_log || !dt_bias || !normalized ||
+      !read_indices || !read_weights || !write_indices || !write_weights || !values || !input_gate ||
+      !forget_log_gate || batch < 0 || time < 0 || heads < 1 || width < 1 || width % heads)
+    return COW_ERR_INVALID;
+  const int64_t ntot = 4LL * heads * root + width + 2LL * heads;
+  if (width > kCtrlMaxWidth || ntot > kCtrlMaxOut || root < 1 || root > kRouteMaxRoot || reads < 1 || writes < 1 ||
+      reads > root * root || writes > root * root || reads > 32 || writes > 32)
+    return COW_ERR_UNSUPPORTED;
+  const int64_t rows = batch * time;
+  if (rows == 0) return COW_OK;
+  ControllerLaunch P{tokens, ln_weight, ln_bias, weights_t, bias, a_log, dt_bias, normalized, read_indices,
+                     read_weights, write_indices, write_weights, values, input_gate, forget_log_gate, batch, time,
+                     eps, width, heads, root, reads, writes, static_cast<int32_t>(ntot)};
+  cow_controller_kernel<<<static_cast<unsigned>(rows), kCtrlThreads, 0, as_stream(stream)>>>(P);
   return launch_status();
 }
 

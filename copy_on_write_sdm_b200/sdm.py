@@ -154,6 +154,8 @@ class SparseDeltaMemory(nn.Module):
         if tokens.ndim != 3 or tokens.shape[-1] != self.width:
             raise ValueError(f"SDM tokens must be [B,T,{self.width}]")
         batch, time, _ = tokens.shape
+        if self._fused_routes_ok(tokens) and self._fused_controller_ok():
+            return self._controller_step(tokens, batch, time)
         normalized = self.input_norm(tokens)
         if self._fused_routes_ok(tokens):
             return self._controller_fused(normalized, batch, time)
@@ -177,6 +179,58 @@ class SparseDeltaMemory(nn.Module):
         return (tokens.is_cuda and tokens.dtype == torch.float32 and root <= 256 and self.reads <= 32
                 and self.writes <= 32 and min(self.reads, root) <= 32 and min(self.writes, root) <= 32
                 and all(p.dtype == torch.float32 for p in (self.A_log, self.dt_bias)))
+
+    def _fused_controller_ok(self) -> bool:
+        root = math.isqrt(self.slots)
+        ntot = 4 * self.memory_heads * root + self.width + 2 * self.memory_heads
+        norm = self.input_norm
+        return (self.width <= 512 and ntot <= 4096 and norm.elementwise_affine and norm.weight is not None
+                and norm.bias is not None and all(p.weight.dtype == torch.float32 for p in self._routing_linears()))
+
+    def _routing_linears(self):
+        return (self.read_projection, self.write_projection, self.value_projection, self.forget_projection,
+                self.input_projection)
+
+    def _stacked_weights(self):
+        """[width, Ntot] transposed concatenation of the routing projections and their
+        bias; rebuilt only when a parameter was replaced or changed in place."""
+        params = [t for lin in self._routing_linears() for t in (lin.weight, lin.bias)]
+        key = tuple((t.data_ptr(), t._version) for t in params)
+        cached = self.__dict__.get("_stacked_cache")
+        if cached is None or cached[0] != key:
+            with torch.no_grad():
+                wt = torch.cat([lin.weight for lin in self._routing_linears()], 0).t().contiguous()
+                bias = torch.cat([lin.bias for lin in self._routing_linears()], 0).contiguous()
+            cached = (key, wt, bias)
+            self.__dict__["_stacked_cache"] = cached
+        return cached[1], cached[2]
+
+    def _controller_step(self, tokens: torch.Tensor, batch: int, time: int) -> SDMStepInputs:
+        """The whole controller in one ``cow_controller_step`` launch (FP32): layer norm,
+        the five routing projections, route selection, gates and value slices."""
+        H = self.memory_heads
+        device = tokens.device
+        x = tokens.contiguous()
+        wt, bias = self._stacked_weights()
+        banks = batch * H
+        normalized = torch.empty_like(x)
+        read_i = torch.empty(banks, time, self.reads, dtype=torch.int64, device=device)
+        read_w = torch.empty(banks, time, self.reads, dtype=torch.float32, device=device)
+        write_i = torch.empty(banks, time, self.writes, dtype=torch.int64, device=device)
+        write_w = torch.empty(banks, time, self.writes, dtype=torch.float32, device=device)
+        values = torch.empty(banks, time, self.head_width, dtype=torch.float32, device=device)
+        gate_in = torch.empty(banks, time, dtype=torch.float32, device=device)
+        forget = torch.empty(banks, time, dtype=torch.float32, device=device)
+        norm = self.input_norm
+        _lib.check(_lib.load().cow_controller_step(
+            x.data_ptr(), norm.weight.data_ptr(), norm.bias.data_ptr(), float(norm.eps), wt.data_ptr(),
+            bias.data_ptr(), self.A_log.data_ptr(), self.dt_bias.data_ptr(), batch, time, self.width, H,
+            math.isqrt(self.slots), self.reads, self.writes, normalized.data_ptr(), read_i.data_ptr(),
+            read_w.data_ptr(), write_i.data_ptr(), write_w.data_ptr(), values.data_ptr(), gate_in.data_ptr(),
+            forget.data_ptr(), _lib.stream_of(device)), "cow_controller_step")
+        return SDMStepInputs(
+            normalized=normalized, write_indices=write_i, write_weights=write_w, values=values,
+            input_gate=gate_in, forget_log_gate=forget, read_indices=read_i, read_weights=read_w)
 
     def _controller_fused(self, normalized: torch.Tensor, batch: int, time: int) -> SDMStepInputs:
         """The same outputs as the PyTorch controller; the route selection and gates

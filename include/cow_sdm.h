@@ -334,6 +334,20 @@ int cow_route_controller(const float* read_proj, const float* write_proj, const 
                          int64_t* read_indices, float* read_weights, int64_t* write_indices, float* write_weights,
                          float* input_gate, float* forget_log_gate, void* stream);
 
+/* The whole SDM controller for a [B,T,width] token block, FP32: layer norm
+ * (ln_weight, ln_bias, eps), the read / write / value / forget / input
+ * projections as one matrix weights_t [width, Ntot] (columns: read H*2*root,
+ * write H*2*root, value width, forget H, input H; bias [Ntot]), then per bank
+ * the route selection and gates of cow_route_controller and the value slice
+ * [B*H,T,width/H].  normalized [B,T,width] is written for the readout.
+ * width <= 512, Ntot <= 4096, root <= 256, R, W <= 32. */
+int cow_controller_step(const float* tokens, const float* ln_weight, const float* ln_bias, float eps,
+                        const float* weights_t, const float* bias, const float* a_log, const float* dt_bias,
+                        int64_t batch, int64_t time, int32_t width, int32_t heads, int32_t root, int32_t reads,
+                        int32_t writes, float* normalized, int64_t* read_indices, float* read_weights,
+                        int64_t* write_indices, float* write_weights, float* values, float* input_gate,
+                        float* forget_log_gate, void* stream);
+
 /* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
 
