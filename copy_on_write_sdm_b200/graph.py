@@ -99,8 +99,7 @@ class GraphedDecode:
             step = module.controller(tokens)
             reading, _ = packed_sdm_cow_step(state.sdm_states[b_i], **_step_kwargs(step), validate_routes=False,
                                              collect_diagnostics=False)
-            tokens = tokens + module.finish(step.normalized, reading[:, None])
-            tokens = tokens + stack.sdm_mlps[str(i)](tokens)
+            tokens = module.finish_residual(tokens, step.normalized, reading[:, None], stack.sdm_mlps[str(i)])
             b_i += 1
         return model.output(model.final_norm(tokens))
 

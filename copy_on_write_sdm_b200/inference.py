@@ -20,6 +20,7 @@ from dataclasses import dataclass
 from typing import TYPE_CHECKING, Sequence
 
 import torch
+from torch import nn
 
 from .allocator import (PackedSDMCopyOnWriteState, append_layers, dense_sdm_sparse_step, packed_sdm_cow_step,
                         release_layers, retain_layers)
@@ -305,8 +306,11 @@ def _step_kwargs(step) -> dict:
 
 @torch.no_grad()
 def _decode_faithful_sdm_layer(module: SparseDeltaMemory, tokens: torch.Tensor,
-                               state: PackedSDMCopyOnWriteState, *, backend: str = "auto") -> torch.Tensor:
-    """One token through one SDM layer and its pool (inference.py:538-566)."""
+                               state: PackedSDMCopyOnWriteState, *, backend: str = "auto",
+                               mlp: nn.Module | None = None) -> torch.Tensor:
+    """One token through one SDM layer and its pool (inference.py:538-566).  Returns the
+    layer's mixed output; with ``mlp`` given, the residual stream after the layer and
+    that MLP block (inference.py:655-661) instead."""
     step = _one_token(module, tokens)
     if state.banks != tokens.shape[0] * module.memory_heads:
         raise ValueError("packed SDM banks do not match batch and memory heads")
@@ -314,6 +318,8 @@ def _decode_faithful_sdm_layer(module: SparseDeltaMemory, tokens: torch.Tensor,
         state.prepare_step_capacity(state.banks * module.writes)
     reading, _ = packed_sdm_cow_step(state, **_step_kwargs(step), backend=backend, validate_routes=False,
                                      collect_diagnostics=False)
+    if mlp is not None:
+        return module.finish_residual(tokens, step.normalized, reading[:, None], mlp)
     return module.finish(step.normalized, reading[:, None])
 
 
@@ -366,8 +372,8 @@ def decode_faithful_sdm_stack(stack: "SDMDecoderStack", tokens: torch.Tensor,
             continue
         if state.sdm_layer_positions[b_i] != i:
             raise ValueError("SDM decode layer ordering is inconsistent")
-        tokens = tokens + _decode_faithful_sdm_layer(stack.sdm_layers[str(i)], tokens, state.sdm_states[b_i])
-        tokens = tokens + stack.sdm_mlps[str(i)](tokens)
+        tokens = _decode_faithful_sdm_layer(stack.sdm_layers[str(i)], tokens, state.sdm_states[b_i],
+                                            mlp=stack.sdm_mlps[str(i)])
         b_i += 1
     if state.positions is None:
         state.position += 1

@@ -267,6 +267,71 @@ class SparseDeltaMemory(nn.Module):
         r = r.permute(0, 2, 1, 3).reshape(batch, time, self.width)
         return self.output_projection(torch.sigmoid(self.output_gate(normalized)) * r)
 
+    def finish_residual(self, tokens: torch.Tensor, normalized: torch.Tensor, readings: torch.Tensor,
+                        mlp: nn.Module) -> torch.Tensor:
+        """``t = tokens + finish(normalized, readings)`` followed by ``t + mlp(t)``: the
+        SDM layer's residual and the MLP block after it (reference inference.py:655-661).
+        FP32 CUDA activations in eval mode run as one ``cow_readout_mlp_step`` launch."""
+        if self._fused_readout_ok(tokens, normalized, readings, mlp):
+            return self._readout_step(tokens, normalized, readings, mlp)
+        tokens = tokens + self.finish(normalized, readings)
+        return tokens + mlp(tokens)
+
+    def _fused_readout_ok(self, tokens, normalized, readings, mlp) -> bool:
+        rn, mn = self.readings_norm, getattr(mlp, "norm", None)
+        if not (tokens.is_cuda and tokens.dtype == normalized.dtype == readings.dtype == torch.float32):
+            return False
+        if self.training or mlp.training or not isinstance(mn, nn.LayerNorm):
+            return False
+        act = getattr(mlp, "activation", None)
+        if not (isinstance(act, nn.GELU) and act.approximate == "none"):
+            return False
+        if not (rn.elementwise_affine and rn.bias is not None and mn.elementwise_affine and mn.bias is not None):
+            return False
+        if self.output_gate.bias is None or self.output_projection.bias is None:
+            return False
+        if mlp.input.bias is not None or mlp.output.bias is not None:
+            return False
+        params = self._readout_params(mlp)
+        return (self.width <= 512 and mlp.input.out_features <= 2048 and self.memory_heads <= 64
+                and all(p.dtype == torch.float32 and p.is_cuda for p in params))
+
+    def _readout_params(self, mlp):
+        return (self.readings_norm.weight, self.readings_norm.bias, self.output_gate.weight, self.output_gate.bias,
+                self.output_projection.weight, self.output_projection.bias, mlp.norm.weight, mlp.norm.bias,
+                mlp.input.weight, mlp.output.weight)
+
+    def _readout_weights(self, mlp):
+        """Transposed ([in, out]) copies of the gate, output and MLP matrices; rebuilt
+        only when a parameter was replaced or changed in place."""
+        params = self._readout_params(mlp)
+        key = (id(mlp),) + tuple((t.data_ptr(), t._version) for t in params)
+        cached = self.__dict__.get("_readout_cache")
+        if cached is None or cached[0] != key:
+            with torch.no_grad():
+                mats = tuple(w.t().contiguous() for w in (self.output_gate.weight, self.output_projection.weight,
+                                                        mlp.input.weight, mlp.output.weight))
+            cached = (key, mats)
+            self.__dict__["_readout_cache"] = cached
+        return cached[1]
+
+    def _readout_step(self, tokens, normalized, readings, mlp) -> torch.Tensor:
+        batch, time, _ = tokens.shape
+        x, n = tokens.contiguous(), normalized.contiguous()
+        r = readings.contiguous()
+        if r.shape != (batch * self.memory_heads, time, self.head_width):
+            raise ValueError("SDM readings must be [B*H,T,head_width]")
+        wg, wo, w1, w2 = self._readout_weights(mlp)
+        rn, mn = self.readings_norm, mlp.norm
+        out = torch.empty_like(x)
+        _lib.check(_lib.load().cow_readout_mlp_step(
+            x.data_ptr(), n.data_ptr(), r.data_ptr(), rn.weight.data_ptr(), rn.bias.data_ptr(), float(rn.eps),
+            wg.data_ptr(), self.output_gate.bias.data_ptr(), wo.data_ptr(), self.output_projection.bias.data_ptr(),
+            mn.weight.data_ptr(), mn.bias.data_ptr(), float(mn.eps), w1.data_ptr(), w2.data_ptr(), batch, time,
+            self.width, self.memory_heads, mlp.input.out_features, out.data_ptr(), _lib.stream_of(tokens.device)),
+            "cow_readout_mlp_step")
+        return out
+
     def template_indices(self, batch: int, device) -> torch.Tensor:
         return torch.arange(self.memory_heads, device=device, dtype=torch.int64).repeat(batch)
 

@@ -348,6 +348,22 @@ int cow_controller_step(const float* tokens, const float* ln_weight, const float
                         int64_t* write_indices, float* write_weights, float* values, float* input_gate,
                         float* forget_log_gate, void* stream);
 
+/* The SDM layer's readout, its residual add and the MLP block after it, for a
+ * [B,T,width] token block, FP32 (replaces copy_on_write_sdm/inference.py:523-536
+ * _finish_faithful_sdm_step with the adds at inference.py:660-661 and
+ * model.py:25-45 ResidualMLP in eval mode):
+ *   r   = LayerNorm_hw(readings [B*H,T,hw]; rn_weight, rn_bias, rn_eps), heads -> width
+ *   t1  = tokens + out_weight (sigmoid(gate_weight normalized + gate_bias) * r) + out_bias
+ *   out = t1 + mlp_out_weight GELU_erf(mlp_in_weight LayerNorm(t1; mlp_norm_*, mlp_eps))
+ * Matrices are passed transposed ([in, out], row-major).  width <= 512,
+ * hidden <= 2048, heads <= 64; out must not alias tokens. */
+int cow_readout_mlp_step(const float* tokens, const float* normalized, const float* readings, const float* rn_weight,
+                         const float* rn_bias, float rn_eps, const float* gate_weight_t, const float* gate_bias,
+                         const float* out_weight_t, const float* out_bias, const float* mlp_norm_weight,
+                         const float* mlp_norm_bias, float mlp_eps, const float* mlp_in_weight_t,
+                         const float* mlp_out_weight_t, int64_t batch, int64_t time, int32_t width, int32_t heads,
+                         int32_t hidden, float* out, void* stream);
+
 /* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
 

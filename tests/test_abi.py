@@ -75,3 +75,18 @@ def test_multi_pool_and_host_step_entry_points_reject_bad_arguments():
                                     None) == _lib.ERR_INVALID
     assert lib.cow_decode_step_host_overlapped(pools, None, 1, 4, 16, 1, 0, None, 0, ws, ws, 16, ws, ws, 16,
                                                None, None, None, None, None, None) == _lib.ERR_INVALID
+
+
+def test_readout_entry_rejects_bad_arguments():
+    lib = _lib.load()
+    ws = ctypes.create_string_buffer(16)
+    p = [ws] * 5
+    # missing output
+    assert lib.cow_readout_mlp_step(*p, 1e-6, *[ws] * 6, 1e-5, ws, ws, 1, 1, 64, 2, 256, None,
+                                    None) == _lib.ERR_INVALID
+    # width not a multiple of heads
+    assert lib.cow_readout_mlp_step(*p, 1e-6, *[ws] * 6, 1e-5, ws, ws, 1, 1, 65, 2, 256, ws,
+                                    None) == _lib.ERR_INVALID
+    # wider than the compiled kernel
+    assert lib.cow_readout_mlp_step(*p, 1e-6, *[ws] * 6, 1e-5, ws, ws, 1, 1, 1024, 2, 256, ws,
+                                    None) == _lib.ERR_UNSUPPORTED
