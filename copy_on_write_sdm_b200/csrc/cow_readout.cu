@@ -6,15 +6,15 @@
 //   r      = LayerNorm_hw(readings)              per bank, eps 1e-6, then heads -> width
 //   t1     = tokens + W_o (sigmoid(W_g n + b_g) * r) + b_o   (n: the controller's normalised input)
 //   out    = t1 + W_2 GELU(W_1 LayerNorm_width(t1))          (no biases in the MLP)
-// as about a dozen PyTorch kernels.  Here one block per token row does it all;
-// weights are stored transposed ([in, out]) so that consecutive threads read
+// as about a dozen PyTorch kernels.  Here one 1024-thread block per token row does
+// it all; weights are stored transposed ([in, out]) so that consecutive lanes read
 // consecutive outputs of each input element.
 
 #include "cow_common.cuh"
 
 namespace {
 
-constexpr int kReadoutThreads = 256;
+constexpr int kReadoutThreads = 1024;
 constexpr int kReadoutMaxWidth = 512;
 constexpr int kReadoutMaxHidden = 2048;
 
@@ -51,32 +51,36 @@ __device__ __forceinline__ float block_sum(float v, float* red, int tid) {
 }
 
 // y[o] = epi(o, sum_k in[k] * Wt[k*N + o]) for o < N, from the block's shared
-// vector ``in``.  Outputs go in chunks of 128 (four per lane); the eight warps
-// split k and their partial sums meet in shared memory, so every weight row is
-// read coalesced and each thread keeps 4 x 4 independent loads in flight.
-template <typename Epi>
+// vector ``in``.  A pass covers 32*J outputs (J per lane); the 32 warps split k
+// (warp w takes k = w, w+32, ...) and each lane keeps U x J independent weight
+// loads in flight, so a phase costs a handful of dependent L2 round trips rather
+// than one per k step.  The warps' partial sums meet in shared memory, where four
+// threads per output add them up.
+template <int J, int U, typename Epi>
 __device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const float* __restrict__ Wt, int N,
                                      float* part, Epi epi) {
-  constexpr int kWarps = kReadoutThreads / 32;
+  constexpr int kWarps = kReadoutThreads / 32, kPass = 32 * J;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int o0 = 0; o0 < N; o0 += 128) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool full = o0 + 128 <= N;
+  for (int o0 = 0; o0 < N; o0 += kPass) {
+    float acc[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) acc[j] = 0.f;
+    const bool full = o0 + kPass <= N;
     int k = warp;
     if (full) {
-      for (; k + 3 * kWarps < K; k += 4 * kWarps) {
-        float w[4][4];
+      for (; k + (U - 1) * kWarps < K; k += U * kWarps) {
+        float w[U][J];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < U; ++u) {
           const float* row = Wt + static_cast<int64_t>(k + u * kWarps) * N + o0 + lane;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) w[u][j] = __ldg(row + 32 * j);
+          for (int j = 0; j < J; ++j) w[u][j] = __ldg(row + 32 * j);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < U; ++u) {
           const float x = in[k + u * kWarps];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
+          for (int j = 0; j < J; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
         }
       }
     }
@@ -84,17 +88,21 @@ __device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const 
       const float x = in[k];
       const float* row = Wt + static_cast<int64_t>(k) * N + o0 + lane;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < J; ++j)
         if (o0 + lane + 32 * j < N) acc[j] = fmaf(x, __ldg(row + 32 * j), acc[j]);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) part[warp * 128 + lane + 32 * j] = acc[j];
+    for (int j = 0; j < J; ++j) part[warp * kPass + lane + 32 * j] = acc[j];
     __syncthreads();
-    if (tid < 128 && o0 + tid < N) {
+    // four threads per output, each adding a quarter of the warps' partials
+    for (int q = tid; q < 4 * kPass; q += kReadoutThreads) {
+      const int o = q >> 2, r = q & 3;
       float v = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += part[w * 128 + tid];
-      epi(o0 + tid, v);
+      for (int w = r; w < kWarps; w += 4) v += part[w * kPass + o];
+      v += __shfl_xor_sync(kFull, v, 1);
+      v += __shfl_xor_sync(kFull, v, 2);
+      if (r == 0 && o0 + o < N) epi(o0 + o, v);
     }
     __syncthreads();
   }
@@ -105,7 +113,7 @@ __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __gr
   __shared__ float s_r[kReadoutMaxWidth];    // normalised readings (heads -> width), later t1
   __shared__ float s_t[kReadoutMaxWidth];    // gated readings
   __shared__ float s_h[kReadoutMaxHidden];   // MLP hidden activations
-  __shared__ float s_part[kReadoutThreads / 32 * 128];
+  __shared__ float s_part[kReadoutThreads / 32 * 256];  // partials of passes up to 256 outputs
   __shared__ float s_red[kReadoutThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tok = blockIdx.x;  // b * T + t
@@ -132,9 +140,9 @@ __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __gr
   }
   __syncthreads();
   // gated readings: sigmoid(W_g n + b_g) * r
-  gemv(s_n, W, P.wg_t, W, s_part, [&](int o, float g) { s_t[o] = s_r[o] / (1.f + expf(-(g + P.bg[o]))); });
+  gemv<4, 8>(s_n, W, P.wg_t, W, s_part, [&](int o, float g) { s_t[o] = s_r[o] / (1.f + expf(-(g + P.bg[o]))); });
   // t1 = tokens + W_o (gated) + b_o
-  gemv(s_t, W, P.wo_t, W, s_part, [&](int o, float v) { s_r[o] = P.tokens[tok * W + o] + (v + P.bo[o]); });
+  gemv<4, 8>(s_t, W, P.wo_t, W, s_part, [&](int o, float v) { s_r[o] = P.tokens[tok * W + o] + (v + P.bo[o]); });
   // MLP norm over t1 (held in s_r)
   float part = 0.f;
   for (int k = tid; k < W; k += kReadoutThreads) part += s_r[k];
@@ -148,10 +156,10 @@ __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __gr
   for (int k = tid; k < W; k += kReadoutThreads) s_n[k] = (s_r[k] - mean) * rstd * P.mn_w[k] + P.mn_b[k];
   __syncthreads();
   // hidden = GELU(W_1 n), exact (erf) form
-  gemv(s_n, W, P.w1_t, P.hidden, s_part,
+  gemv<8, 4>(s_n, W, P.w1_t, P.hidden, s_part,
        [&](int o, float v) { s_h[o] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); });
   // out = t1 + W_2 hidden
-  gemv(s_h, P.hidden, P.w2_t, W, s_part, [&](int o, float v) { P.out[tok * W + o] = s_r[o] + v; });
+  gemv<4, 8>(s_h, P.hidden, P.w2_t, W, s_part, [&](int o, float v) { P.out[tok * W + o] = s_r[o] + v; });
 }
 
 }  // namespace

@@ -22,7 +22,8 @@ def dev():
 
 
 @pytest.mark.parametrize("width,heads,batch,time", [
-    (128, 2, 16, 1), (64, 4, 3, 5), (256, 8, 2, 1), (512, 4, 4, 2), (96, 3, 1, 1),
+    (128, 2, 16, 1), (64, 4, 3, 5), (256, 8, 2, 1), (512, 4, 4, 2), (96, 3, 1, 1), (128, 1, 37, 1),
+    (256, 8, 9, 3),
 ])
 def test_finish_residual_matches_torch(dev, width, heads, batch, time):
     from copy_on_write_sdm_b200.model import ResidualMLP
@@ -39,8 +40,8 @@ def test_finish_residual_matches_torch(dev, width, heads, batch, time):
     normalized = torch.randn(batch, time, width, device=dev)
     readings = 2.0 * torch.randn(batch * heads, time, width // heads, device=dev) + 0.5
     with torch.no_grad():
-        assert m._fused_readout_ok(tokens, normalized, readings, mlp)
-        got = m.finish_residual(tokens, normalized, readings, mlp)
+        assert m._fused_readout_ok(tokens, normalized, readings, mlp) == (width <= 256)
+        got = m._readout_step(tokens, normalized, readings, mlp)  # the kernel, also beyond the dispatch limit
         t1 = tokens + m.finish(normalized, readings)
         want = t1 + mlp(t1)
     assert got.shape == want.shape and got.dtype == want.dtype
