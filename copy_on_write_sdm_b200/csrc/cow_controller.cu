@@ -262,15 +262,18 @@ struct ControllerLaunch {
   int32_t width, heads, root, reads, writes, ntot;
 };
 
-constexpr int kCtrlThreads = 128;
+constexpr int kCtrlThreads = 512;
 constexpr int kCtrlMaxWidth = 512;
 constexpr int kCtrlMaxOut = 4096;
+constexpr int kCtrlWarps = kCtrlThreads / 32;
+constexpr int kCtrlJ = 4, kCtrlU = 8, kCtrlPass = 32 * kCtrlJ;  // projection pass: 128 outputs
 
 __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __grid_constant__ ControllerLaunch P) {
   __shared__ float s_x[kCtrlMaxWidth];
   __shared__ float s_out[kCtrlMaxOut];
-  __shared__ float s_red[2][kCtrlThreads / 32];
-  __shared__ RouteSmem s_sm[kCtrlThreads / 32];
+  __shared__ float s_red[2][kCtrlWarps];
+  __shared__ float s_part[kCtrlWarps * kCtrlPass];
+  __shared__ RouteSmem s_sm[kCtrlWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tok = blockIdx.x;  // b * T + t
   const int width = P.width, H = P.heads, key_w = 2 * P.root;
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
   __syncthreads();
   float mean = 0.f;
 #pragma unroll
-  for (int w = 0; w < kCtrlThreads / 32; ++w) mean += s_red[0][w];
+  for (int w = 0; w < kCtrlWarps; ++w) mean += s_red[0][w];
   mean /= static_cast<float>(width);
   float sq = 0.f;
   for (int k = tid; k < width; k += kCtrlThreads) {
@@ -300,7 +303,7 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
   __syncthreads();
   float var = 0.f;
 #pragma unroll
-  for (int w = 0; w < kCtrlThreads / 32; ++w) var += s_red[1][w];
+  for (int w = 0; w < kCtrlWarps; ++w) var += s_red[1][w];
   const float rstd = rsqrtf(var / static_cast<float>(width) + P.eps);
   for (int k = tid; k < width; k += kCtrlThreads) {
     const float nv = (s_x[k] - mean) * rstd * P.ln_w[k] + P.ln_b[k];
@@ -308,13 +311,51 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
     s_x[k] = nv;
   }
   __syncthreads();
-  // projections
-  for (int o = tid; o < P.ntot; o += kCtrlThreads) {
-    float acc = P.bias[o];
-    for (int k = 0; k < width; ++k) acc = fmaf(s_x[k], P.wt[static_cast<int64_t>(k) * P.ntot + o], acc);
-    s_out[o] = acc;
+  // projections: passes of 128 outputs (4 per lane); the warps split k (warp w
+  // takes k = w, w + 16, ...) with up to 32 weight loads in flight per lane, and
+  // their partial sums meet in shared memory
+  const int N = P.ntot;
+  for (int o0 = 0; o0 < N; o0 += kCtrlPass) {
+    float acc[kCtrlJ] = {0.f, 0.f, 0.f, 0.f};
+    int k = warp;
+    if (o0 + kCtrlPass <= N) {
+      for (; k + (kCtrlU - 1) * kCtrlWarps < width; k += kCtrlU * kCtrlWarps) {
+        float w[kCtrlU][kCtrlJ];
+#pragma unroll
+        for (int u = 0; u < kCtrlU; ++u) {
+          const float* row = P.wt + static_cast<int64_t>(k + u * kCtrlWarps) * N + o0 + lane;
+#pragma unroll
+          for (int j = 0; j < kCtrlJ; ++j) w[u][j] = __ldg(row + 32 * j);
+        }
+#pragma unroll
+        for (int u = 0; u < kCtrlU; ++u) {
+          const float x = s_x[k + u * kCtrlWarps];
+#pragma unroll
+          for (int j = 0; j < kCtrlJ; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
+        }
+      }
+    }
+    for (; k < width; k += kCtrlWarps) {
+      const float x = s_x[k];
+      const float* row = P.wt + static_cast<int64_t>(k) * N + o0 + lane;
+#pragma unroll
+      for (int j = 0; j < kCtrlJ; ++j)
+        if (o0 + lane + 32 * j < N) acc[j] = fmaf(x, __ldg(row + 32 * j), acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kCtrlJ; ++j) s_part[warp * kCtrlPass + lane + 32 * j] = acc[j];
+    __syncthreads();
+    {  // four threads per output, each adding a quarter of the warps' partials
+      const int o = tid >> 2, r = tid & 3;
+      float v = 0.f;
+#pragma unroll
+      for (int w = r; w < kCtrlWarps; w += 4) v += s_part[w * kCtrlPass + o];
+      v += __shfl_xor_sync(kFull, v, 1);
+      v += __shfl_xor_sync(kFull, v, 2);
+      if (r == 0 && o0 + o < N) s_out[o0 + o] = v + P.bias[o0 + o];
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const int64_t b = tok / P.time, t = tok % P.time;
   const int hw = width / H;
   const float* rproj = s_out;
@@ -322,15 +363,20 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
   const float* vproj = wproj + H * key_w;
   const float* fproj = vproj + width;
   const float* iproj = fproj + H;
-  for (int h = warp; h < H; h += kCtrlThreads / 32) {
+  // one warp per (bank, read or write) route selection; the read warp also
+  // writes the bank's value slice and gates
+  for (int item = warp; item < 2 * H; item += kCtrlWarps) {
+    const int h = item >> 1;
     const int64_t row = (b * H + h) * P.time + t;
     auto& sm = s_sm[warp];
+    __syncwarp();  // the warp's previous selection is done with sm
+    if (item & 1) {
+      select_routes(wproj + h * key_w, P.root, P.writes, sm, lane, P.write_indices + row * P.writes,
+                    P.write_weights + row * P.writes);
+      continue;
+    }
     select_routes(rproj + h * key_w, P.root, P.reads, sm, lane, P.read_indices + row * P.reads,
                   P.read_weights + row * P.reads);
-    __syncwarp();
-    select_routes(wproj + h * key_w, P.root, P.writes, sm, lane, P.write_indices + row * P.writes,
-                  P.write_weights + row * P.writes);
-    __syncwarp();
     for (int k = lane; k < hw; k += 32) P.values[row * hw + k] = vproj[h * hw + k];
     if (lane == 0) {
       const float x = fproj[h] + P.dt_bias[h];

@@ -33,7 +33,11 @@ def test_fused_routes_match_torch(dev, slots, heads, reads, writes, time, whole)
     m = SparseDeltaMemory(width, slots=slots, reads=reads, writes=writes, memory_heads=heads).to(dev).eval()
     tokens = torch.randn(6, time, width, device=dev)
     with torch.no_grad():
-        assert m._fused_routes_ok(tokens) and m._fused_controller_ok()
+        assert m._fused_routes_ok(tokens)
+        ntot = 4 * heads * int(slots ** 0.5) + width + 2 * heads
+        assert m._fused_controller_ok() == (ntot <= 4096)
+        if whole and ntot > 4096:
+            pytest.skip("projection wider than the whole-controller kernel; the route kernel covers it")
         if not whole:
             m._fused_controller_ok = lambda: False  # routes fused, projections in PyTorch
         got = m.controller(tokens)
