@@ -941,10 +941,11 @@ def main_model(args, rank, world, device) -> int:
         "eager": {"value": tokens / (eager_ms / 1e3), "unit": "tokens/s", "ms_per_step": eager_ms / K,
                   "path": "LanguageModel.decode (the reference's eager call sequence)"},
         "graph_captures": res["captures"],
-        "gpu_launches": 3 * 7 * K,
-        "gpu_launches_note": "per SDM layer per step (7 layers): cow_controller_kernel, the fused decode "
-                             "step, cow_readout_kernel (readout + residual + MLP); the embedding, the "
-                             "attention block and the vocabulary head run as PyTorch kernels",
+        "gpu_launches": (3 * 7 + 1) * K,
+        "gpu_launches_note": "per step: for each of the 7 SDM layers cow_controller_kernel, the fused decode "
+                             "step and cow_readout_kernel (readout + residual + MLP), and one "
+                             "cow_attention_kernel for the dense block; the embedding, final norm and "
+                             "vocabulary head run as PyTorch kernels",
         "clocks": res["clocks"],
         "cpu_baseline": None,
         "cpu_baseline_note": "the CPU port covers the SDM step and allocator, not the whole model",

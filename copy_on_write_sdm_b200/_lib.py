@@ -112,6 +112,8 @@ _SIGNATURES = {
                                       c_int32, c_int32, c_int32, P, P, P, P, P, P, P, P, P]),
     "cow_readout_mlp_step": (c_int32, [P, P, P, P, P, ctypes.c_float, P, P, P, P, P, P, ctypes.c_float, P, P,
                                        c_int64, c_int64, c_int32, c_int32, c_int32, P, P]),
+    "cow_attention_mlp_decode": (c_int32, [P, P, P, P, ctypes.c_float, P, P, P, P, c_int64, P, P, ctypes.c_float,
+                                           P, P, c_int64, c_int32, c_int32, c_int32, P, P]),
     "cow_route_controller": (c_int32, [P, P, P, P, P, P, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
                                        P, P, P, P, P, P, P]),
     "cow_release_workspace_bytes": (c_int64, [POINTER(CowPool), P, c_int32]),

@@ -11,10 +11,11 @@
 // consecutive outputs of each input element.
 
 #include "cow_common.cuh"
+#include "cow_gemv.cuh"
 
 namespace {
 
-constexpr int kReadoutThreads = 1024;
+constexpr int kReadoutThreads = kGemvThreads;
 constexpr int kReadoutMaxWidth = 512;
 constexpr int kReadoutMaxHidden = 2048;
 
@@ -37,76 +38,6 @@ struct ReadoutLaunch {
   float rn_eps, mn_eps;
   int32_t width, heads, hidden;
 };
-
-__device__ __forceinline__ float block_sum(float v, float* red, int tid) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-  __syncthreads();  // red may still be read from the previous call
-  if ((tid & 31) == 0) red[tid >> 5] = v;
-  __syncthreads();
-  float s = 0.f;
-#pragma unroll
-  for (int w = 0; w < kReadoutThreads / 32; ++w) s += red[w];
-  return s;
-}
-
-// y[o] = epi(o, sum_k in[k] * Wt[k*N + o]) for o < N, from the block's shared
-// vector ``in``.  A pass covers 32*J outputs (J per lane); the 32 warps split k
-// (warp w takes k = w, w+32, ...) and each lane keeps U x J independent weight
-// loads in flight, so a phase costs a handful of dependent L2 round trips rather
-// than one per k step.  The warps' partial sums meet in shared memory, where four
-// threads per output add them up.
-template <int J, int U, typename Epi>
-__device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const float* __restrict__ Wt, int N,
-                                     float* part, Epi epi) {
-  constexpr int kWarps = kReadoutThreads / 32, kPass = 32 * J;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int o0 = 0; o0 < N; o0 += kPass) {
-    float acc[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) acc[j] = 0.f;
-    const bool full = o0 + kPass <= N;
-    int k = warp;
-    if (full) {
-      for (; k + (U - 1) * kWarps < K; k += U * kWarps) {
-        float w[U][J];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float* row = Wt + static_cast<int64_t>(k + u * kWarps) * N + o0 + lane;
-#pragma unroll
-          for (int j = 0; j < J; ++j) w[u][j] = __ldg(row + 32 * j);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float x = in[k + u * kWarps];
-#pragma unroll
-          for (int j = 0; j < J; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
-        }
-      }
-    }
-    for (; k < K; k += kWarps) {
-      const float x = in[k];
-      const float* row = Wt + static_cast<int64_t>(k) * N + o0 + lane;
-#pragma unroll
-      for (int j = 0; j < J; ++j)
-        if (o0 + lane + 32 * j < N) acc[j] = fmaf(x, __ldg(row + 32 * j), acc[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) part[warp * kPass + lane + 32 * j] = acc[j];
-    __syncthreads();
-    // four threads per output, each adding a quarter of the warps' partials
-    for (int q = tid; q < 4 * kPass; q += kReadoutThreads) {
-      const int o = q >> 2, r = q & 3;
-      float v = 0.f;
-#pragma unroll
-      for (int w = r; w < kWarps; w += 4) v += part[w * kPass + o];
-      v += __shfl_xor_sync(kFull, v, 1);
-      v += __shfl_xor_sync(kFull, v, 2);
-      if (r == 0 && o0 + o < N) epi(o0 + o, v);
-    }
-    __syncthreads();
-  }
-}
 
 __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __grid_constant__ ReadoutLaunch P) {
   __shared__ float s_n[kReadoutMaxWidth];    // normalised controller input, later the MLP's normalised t1
@@ -143,23 +74,9 @@ __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __gr
   gemv<4, 8>(s_n, W, P.wg_t, W, s_part, [&](int o, float g) { s_t[o] = s_r[o] / (1.f + expf(-(g + P.bg[o]))); });
   // t1 = tokens + W_o (gated) + b_o
   gemv<4, 8>(s_t, W, P.wo_t, W, s_part, [&](int o, float v) { s_r[o] = P.tokens[tok * W + o] + (v + P.bo[o]); });
-  // MLP norm over t1 (held in s_r)
-  float part = 0.f;
-  for (int k = tid; k < W; k += kReadoutThreads) part += s_r[k];
-  const float mean = block_sum(part, s_red, tid) / static_cast<float>(W);
-  part = 0.f;
-  for (int k = tid; k < W; k += kReadoutThreads) {
-    const float d = s_r[k] - mean;
-    part += d * d;
-  }
-  const float rstd = rsqrtf(block_sum(part, s_red, tid) / static_cast<float>(W) + P.mn_eps);
-  for (int k = tid; k < W; k += kReadoutThreads) s_n[k] = (s_r[k] - mean) * rstd * P.mn_w[k] + P.mn_b[k];
-  __syncthreads();
-  // hidden = GELU(W_1 n), exact (erf) form
-  gemv<8, 4>(s_n, W, P.w1_t, P.hidden, s_part,
-       [&](int o, float v) { s_h[o] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); });
-  // out = t1 + W_2 hidden
-  gemv<4, 8>(s_h, P.hidden, P.w2_t, W, s_part, [&](int o, float v) { P.out[tok * W + o] = s_r[o] + v; });
+  // the MLP block over t1 (held in s_r)
+  mlp_residual(s_r, s_n, s_h, s_part, s_red, W, P.hidden, P.mn_w, P.mn_b, P.mn_eps, P.w1_t, P.w2_t,
+               P.out + tok * W);
 }
 
 }  // namespace

@@ -90,9 +90,12 @@ class GraphedDecode:
         for i, kind in enumerate(stack.layout):
             if kind == "A":
                 block = stack.attention_layers[str(i)]
-                tokens = tokens + _attend_full(block.attention, tokens, state.dense_keys[a_i],
-                                               state.dense_values[a_i], self.pos)
-                tokens = tokens + block.mlp(tokens)
+                kc, vc = state.dense_keys[a_i], state.dense_values[a_i]
+                if block._fused_decode_ok(tokens, kc, vc):
+                    tokens = block.decode_residual(tokens, kc, vc, self.pos)
+                else:
+                    tokens = tokens + _attend_full(block.attention, tokens, kc, vc, self.pos)
+                    tokens = tokens + block.mlp(tokens)
                 a_i += 1
                 continue
             module = stack.sdm_layers[str(i)]

@@ -365,9 +365,7 @@ def decode_faithful_sdm_stack(stack: "SDMDecoderStack", tokens: torch.Tensor,
     for i, kind in enumerate(stack.layout):
         if kind == "A":
             block = stack.attention_layers[str(i)]
-            tokens = tokens + block.attention.decode_with_cache(tokens, state.dense_keys[a_i],
-                                                                state.dense_values[a_i], position=where)
-            tokens = tokens + block.mlp(tokens)
+            tokens = block.decode_residual(tokens, state.dense_keys[a_i], state.dense_values[a_i], where)
             a_i += 1
             continue
         if state.sdm_layer_positions[b_i] != i:

@@ -111,6 +111,81 @@ class DenseAttentionBlock(nn.Module):
         tokens = tokens + self.attention(tokens)
         return tokens + self.mlp(tokens)
 
+    def decode_residual(self, tokens: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                        position) -> torch.Tensor:
+        """One decode token through the block: ``t = tokens + attention.decode_with_cache(...)``
+        then ``t + mlp(t)`` (reference inference.py:640-651).  ``position`` is an int or a
+        ``[B]`` tensor.  FP32 CUDA activations in eval mode run as one
+        ``cow_attention_mlp_decode`` launch, which also stores this token's K/V."""
+        if self._fused_decode_ok(tokens, key_cache, value_cache):
+            return self._decode_fused(tokens, key_cache, value_cache, position)
+        tokens = tokens + self.attention.decode_with_cache(tokens, key_cache, value_cache, position=position)
+        return tokens + self.mlp(tokens)
+
+    def _fused_decode_ok(self, tokens, key_cache, value_cache) -> bool:
+        att, mlp = self.attention, self.mlp
+        if not (tokens.is_cuda and tokens.dtype == key_cache.dtype == value_cache.dtype == torch.float32):
+            return False
+        if self.training or tokens.ndim != 3 or tokens.shape[1] != 1:
+            return False
+        if not (key_cache.is_contiguous() and value_cache.is_contiguous() and key_cache.shape == value_cache.shape
+                and key_cache.shape[:2] == (tokens.shape[0], att.heads) and key_cache.shape[3] == att.head_width):
+            return False
+        if att.qkv.bias is not None or att.output.bias is not None or mlp.input.bias is not None \
+                or mlp.output.bias is not None:
+            return False
+        if not (att.norm.elementwise_affine and att.norm.bias is not None and mlp.norm.elementwise_affine
+                and mlp.norm.bias is not None and isinstance(mlp.activation, nn.GELU)
+                and mlp.activation.approximate == "none"):
+            return False
+        # scores for every cache slot stay in shared memory; wider blocks are faster as GEMMs
+        return (att.width <= 256 and mlp.hidden <= 1024 and att.heads * key_cache.shape[2] <= 16384
+                and all(p.dtype == torch.float32 for p in self._decode_params()))
+
+    def _decode_params(self):
+        att, mlp = self.attention, self.mlp
+        return (att.norm.weight, att.norm.bias, att.qkv.weight, att.output.weight, mlp.norm.weight, mlp.norm.bias,
+                mlp.input.weight, mlp.output.weight)
+
+    def _decode_weights(self):
+        """Transposed ([in, out]) QKV, output and MLP matrices; rebuilt only when a
+        parameter was replaced or changed in place."""
+        params = self._decode_params()
+        key = tuple((t.data_ptr(), t._version) for t in params)
+        cached = self.__dict__.get("_decode_cache")
+        if cached is None or cached[0] != key:
+            with torch.no_grad():
+                mats = tuple(w.detach().t().contiguous() for w in (self.attention.qkv.weight,
+                                                                   self.attention.output.weight,
+                                                                   self.mlp.input.weight, self.mlp.output.weight))
+            cached = (key, mats)
+            self.__dict__["_decode_cache"] = cached
+        return cached[1]
+
+    def _decode_fused(self, tokens, key_cache, value_cache, position) -> torch.Tensor:
+        from . import _lib
+
+        att, mlp = self.attention, self.mlp
+        batch = tokens.shape[0]
+        if isinstance(position, int):
+            if not 0 <= position < key_cache.shape[2]:
+                raise ValueError("dense decode position is outside the cache")
+            pos = torch.full((batch,), position, dtype=torch.int64, device=tokens.device)
+        else:
+            pos = torch.as_tensor(position, device=tokens.device, dtype=torch.int64).contiguous()
+            if pos.shape != (batch,):
+                raise ValueError("dense decode positions are invalid")
+        x = tokens.contiguous()
+        qkv_t, out_t, w1, w2 = self._decode_weights()
+        out = torch.empty_like(x)
+        _lib.check(_lib.load().cow_attention_mlp_decode(
+            x.data_ptr(), pos.data_ptr(), att.norm.weight.data_ptr(), att.norm.bias.data_ptr(), float(att.norm.eps),
+            qkv_t.data_ptr(), out_t.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), key_cache.shape[2],
+            mlp.norm.weight.data_ptr(), mlp.norm.bias.data_ptr(), float(mlp.norm.eps), w1.data_ptr(), w2.data_ptr(),
+            batch, att.width, att.heads, mlp.hidden, out.data_ptr(), _lib.stream_of(tokens.device)),
+            "cow_attention_mlp_decode")
+        return out
+
 
 class SDMDecoderStack(nn.Module):
     """Layout string of "A" (dense attention) and "B" (SDM) physical layers (reference model.py:214-325)."""

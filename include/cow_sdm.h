@@ -364,6 +364,24 @@ int cow_readout_mlp_step(const float* tokens, const float* normalized, const flo
                          const float* mlp_out_weight_t, int64_t batch, int64_t time, int32_t width, int32_t heads,
                          int32_t hidden, float* out, void* stream);
 
+/* One decode token per request through a dense attention block and the MLP after
+ * it, FP32 (replaces copy_on_write_sdm/inference.py:640-651: model.py
+ * CausalSelfAttention.decode_with_cache, the residual adds and ResidualMLP, eval
+ * mode): LayerNorm(ln_*), q|k|v = qkv_weight n (no bias), k and v stored at
+ * positions[b] of key_cache / value_cache [batch, heads, capacity, width/heads],
+ * softmax(q.K/sqrt(hw)) V over slots 0..positions[b] per head, t1 = tokens +
+ * out_weight o, out = t1 + mlp_out GELU_erf(mlp_in LayerNorm(t1; mlp_norm_*)).
+ * positions is a device int64 [batch]; a position outside [0, capacity) gives a
+ * NaN row and writes nothing.  Matrices are transposed ([in, out], row-major).
+ * width <= 512, hidden <= 2048, heads * capacity bounded by shared memory
+ * (COW_ERR_UNSUPPORTED beyond); out must not alias tokens. */
+int cow_attention_mlp_decode(const float* tokens, const int64_t* positions, const float* ln_weight,
+                             const float* ln_bias, float ln_eps, const float* qkv_weight_t,
+                             const float* out_weight_t, float* key_cache, float* value_cache, int64_t capacity,
+                             const float* mlp_norm_weight, const float* mlp_norm_bias, float mlp_eps,
+                             const float* mlp_in_weight_t, const float* mlp_out_weight_t, int64_t batch,
+                             int32_t width, int32_t heads, int32_t hidden, float* out, void* stream);
+
 /* materialize_dense (allocator.py:1004-1017): dense [banks,slots,width] in out_dtype. */
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream);
 

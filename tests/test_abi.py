@@ -90,3 +90,19 @@ def test_readout_entry_rejects_bad_arguments():
     # wider than the compiled kernel
     assert lib.cow_readout_mlp_step(*p, 1e-6, *[ws] * 6, 1e-5, ws, ws, 1, 1, 1024, 2, 256, ws,
                                     None) == _lib.ERR_UNSUPPORTED
+
+
+def test_attention_entry_rejects_bad_arguments():
+    lib = _lib.load()
+    ws = ctypes.create_string_buffer(64)
+    out = ctypes.create_string_buffer(64)
+
+    def call(width, heads, hidden, cap, dst):
+        return lib.cow_attention_mlp_decode(ws, ws, ws, ws, 1e-5, ws, ws, ws, ws, cap, ws, ws, 1e-5, ws, ws, 1,
+                                            width, heads, hidden, dst, None)
+    assert call(64, 2, 256, 8, None) == _lib.ERR_INVALID  # missing output
+    assert call(64, 3, 256, 8, out) == _lib.ERR_INVALID  # width not a multiple of heads
+    assert call(64, 2, 256, 0, out) == _lib.ERR_INVALID  # empty cache
+    assert call(64, 2, 256, 8, ws) == _lib.ERR_INVALID  # output aliasing the residual input
+    assert call(1024, 2, 256, 8, out) == _lib.ERR_UNSUPPORTED  # wider than the compiled kernel
+    assert call(128, 4, 512, 1 << 20, out) == _lib.ERR_UNSUPPORTED  # scores beyond shared memory
