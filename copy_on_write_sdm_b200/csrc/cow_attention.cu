@@ -41,7 +41,7 @@ struct AttentionLaunch {
 };
 
 size_t attention_smem_floats(int width, int heads, int hidden, int64_t capacity) {
-  return static_cast<size_t>(7) * width + hidden + static_cast<size_t>(heads) * capacity + kGemvWarps * kGemvMaxPass +
+  return static_cast<size_t>(11) * width + hidden + static_cast<size_t>(heads) * capacity + kGemvWarps * kGemvMaxPass +
          kGemvWarps + heads;
 }
 
@@ -58,7 +58,11 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
   float* s_part = s_h + HD;                          // [kGemvWarps * kGemvMaxPass]
   float* s_red = s_part + kGemvWarps * kGemvMaxPass;  // [kGemvWarps]
   float* s_inv = s_red + kGemvWarps;                 // [H] 1 / softmax denominator
-  float* s_sc = s_inv + H;                           // [H][L] scores, then probabilities
+  float* s_lnw = s_inv + H;                          // [W] attention norm
+  float* s_lnb = s_lnw + W;
+  float* s_mnw = s_lnb + W;                          // [W] MLP norm
+  float* s_mnb = s_mnw + W;
+  float* s_sc = s_mnb + W;                           // [H][L] scores, then probabilities
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t b = blockIdx.x;
   const int64_t pos = P.pos[b];
@@ -69,8 +73,12 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
   const int L = static_cast<int>(pos) + 1;
   // attention norm
   float acc = 0.f;
-  for (int k = tid; k < W; k += kGemvThreads) {
+  for (int k = tid; k < W; k += kGemvThreads) {  // the token and the norms' weights in one batch of loads
     const float v = P.tokens[b * W + k];
+    s_lnw[k] = P.ln_w[k];
+    s_lnb[k] = P.ln_b[k];
+    s_mnw[k] = P.mn_w[k];
+    s_mnb[k] = P.mn_b[k];
     s_x[k] = v;
     acc += v;
   }
@@ -81,7 +89,7 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
     acc += d * d;
   }
   const float rstd = rsqrtf(block_sum(acc, s_red, tid) / static_cast<float>(W) + P.ln_eps);
-  for (int k = tid; k < W; k += kGemvThreads) s_n[k] = (s_x[k] - mean) * rstd * P.ln_w[k] + P.ln_b[k];
+  for (int k = tid; k < W; k += kGemvThreads) s_n[k] = (s_x[k] - mean) * rstd * s_lnw[k] + s_lnb[k];
   __syncthreads();
   gemv<8, 4>(s_n, W, P.qkv_t, 3 * W, s_part, [&](int o, float v) { s_qkv[o] = v; });
   // this token's key and value into the cache
@@ -141,8 +149,8 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
     }
     __syncthreads();
   }
-  gemv<4, 8>(s_o, W, P.out_t, W, s_part, [&](int o, float v) { s_t1[o] = s_x[o] + v; });
-  mlp_residual(s_t1, s_n, s_h, s_part, s_red, W, HD, P.mn_w, P.mn_b, P.mn_eps, P.w1_t, P.w2_t, P.out + b * W);
+  gemv<4, 4>(s_o, W, P.out_t, W, s_part, [&](int o, float v) { s_t1[o] = s_x[o] + v; });
+  mlp_residual(s_t1, s_n, s_h, s_part, s_red, W, HD, s_mnw, s_mnb, P.mn_eps, P.w1_t, P.w2_t, P.out + b * W);
 }
 
 }  // namespace

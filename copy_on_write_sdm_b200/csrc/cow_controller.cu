@@ -267,6 +267,8 @@ constexpr int kCtrlMaxWidth = 512;
 constexpr int kCtrlMaxOut = 4096;
 constexpr int kCtrlWarps = kCtrlThreads / 32;
 constexpr int kCtrlJ = 4, kCtrlU = 8, kCtrlPass = 32 * kCtrlJ;  // projection pass: 128 outputs
+static_assert(kCtrlMaxWidth <= kCtrlThreads, "the prologue loads one element per thread");
+constexpr int kCtrlGateHeads = 64;  // gate parameters of the first 64 banks staged in shared memory
 
 __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __grid_constant__ ControllerLaunch P) {
   __shared__ float s_x[kCtrlMaxWidth];
@@ -274,16 +276,27 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
   __shared__ float s_red[2][kCtrlWarps];
   __shared__ float s_part[kCtrlWarps * kCtrlPass];
   __shared__ RouteSmem s_sm[kCtrlWarps];
+  __shared__ float s_al[kCtrlGateHeads], s_dt[kCtrlGateHeads];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tok = blockIdx.x;  // b * T + t
   const int width = P.width, H = P.heads, key_w = 2 * P.root;
-  // layer norm: mean, then variance of the centred values (two passes over shared memory)
-  float sum = 0.f;
-  for (int k = tid; k < width; k += kCtrlThreads) {
-    const float v = P.tokens[tok * width + k];
-    s_x[k] = v;
-    sum += v;
+  // every small operand in one batch of independent loads: the token, the norm's
+  // weights (width <= kCtrlThreads, so one element per thread), the projection
+  // bias (into s_out, where the projection adds to it) and the gate parameters
+  float sum = 0.f, lw = 0.f, lb = 0.f;
+  if (tid < width) {
+    const float v = P.tokens[tok * width + tid];
+    lw = P.ln_w[tid];
+    lb = P.ln_b[tid];
+    s_x[tid] = v;
+    sum = v;
   }
+  for (int o = tid; o < P.ntot; o += kCtrlThreads) s_out[o] = P.bias[o];
+  if (tid < H && tid < kCtrlGateHeads) {
+    s_al[tid] = P.a_log[tid];
+    s_dt[tid] = P.dt_bias[tid];
+  }
+  // layer norm: mean, then variance of the centred values (two passes over shared memory)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
   if (lane == 0) s_red[0][warp] = sum;
@@ -305,10 +318,10 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
 #pragma unroll
   for (int w = 0; w < kCtrlWarps; ++w) var += s_red[1][w];
   const float rstd = rsqrtf(var / static_cast<float>(width) + P.eps);
-  for (int k = tid; k < width; k += kCtrlThreads) {
-    const float nv = (s_x[k] - mean) * rstd * P.ln_w[k] + P.ln_b[k];
-    P.normalized[tok * width + k] = nv;
-    s_x[k] = nv;
+  if (tid < width) {
+    const float nv = (s_x[tid] - mean) * rstd * lw + lb;
+    P.normalized[tok * width + tid] = nv;
+    s_x[tid] = nv;
   }
   __syncthreads();
   // projections: passes of 128 outputs (4 per lane); the warps split k (warp w
@@ -352,7 +365,7 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
       for (int w = r; w < kCtrlWarps; w += 4) v += s_part[w * kCtrlPass + o];
       v += __shfl_xor_sync(kFull, v, 1);
       v += __shfl_xor_sync(kFull, v, 2);
-      if (r == 0 && o0 + o < N) s_out[o0 + o] = v + P.bias[o0 + o];
+      if (r == 0 && o0 + o < N) s_out[o0 + o] += v;
     }
     __syncthreads();
   }
@@ -379,9 +392,9 @@ __global__ void __launch_bounds__(kCtrlThreads) cow_controller_kernel(const __gr
                   P.read_weights + row * P.reads);
     for (int k = lane; k < hw; k += 32) P.values[row * hw + k] = vproj[h * hw + k];
     if (lane == 0) {
-      const float x = fproj[h] + P.dt_bias[h];
+      const float x = fproj[h] + (h < kCtrlGateHeads ? s_dt[h] : P.dt_bias[h]);
       const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, threshold 20
-      P.forget_log_gate[row] = -expf(P.a_log[h]) * sp;
+      P.forget_log_gate[row] = -expf(h < kCtrlGateHeads ? s_al[h] : P.a_log[h]) * sp;
       P.input_gate[row] = 1.f / (1.f + expf(-iproj[h]));
     }
   }

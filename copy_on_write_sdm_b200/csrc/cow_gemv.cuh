@@ -25,46 +25,42 @@ __device__ __forceinline__ float block_sum(float v, float* red, int tid) {
   return s;
 }
 
-// y[o] = epi(o, sum_k in[k] * Wt[k*N + o]) for o < N, from the block's shared
-// vector ``in``.  A pass covers 32*J outputs (J per lane); the 32 warps split k
-// (warp w takes k = w, w+32, ...) and each lane keeps U x J independent weight
-// loads in flight, so a phase costs a handful of dependent L2 round trips rather
-// than one per k step.  The warps' partial sums meet in shared memory, where four
-// threads per output add them up.
+// y[j] = epi(j, sum_k in[k] * Wt[k*ld + j]) for j < N (a window of N columns of a
+// row-major [K, ld] matrix), from the block's shared vector ``in``.  A pass covers
+// 32*J outputs (J per lane); the 32 warps split k (warp w takes k = w, w+32, ...),
+// and each lane issues a group of U x J predicated weight loads before the FMAs
+// that consume them, so a phase costs ceil(K / (32 U)) dependent L2 round trips.
+// The warps' partial sums meet in shared memory, where four threads per output
+// add them up.
 template <int J, int U, typename Epi>
-__device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const float* __restrict__ Wt, int N,
-                                     float* part, Epi epi) {
+__device__ __forceinline__ void gemv_cols(const float* __restrict__ in, int K, const float* __restrict__ Wt, int ld,
+                                          int N, float* part, Epi epi) {
   constexpr int kWarps = kGemvThreads / 32, kPass = 32 * J;
+  static_assert(kPass <= kGemvMaxPass, "pass wider than the partial-sum scratch");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int o0 = 0; o0 < N; o0 += kPass) {
     float acc[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) acc[j] = 0.f;
-    const bool full = o0 + kPass <= N;
-    int k = warp;
-    if (full) {
-      for (; k + (U - 1) * kWarps < K; k += U * kWarps) {
-        float w[U][J];
+    bool on[J];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float* row = Wt + static_cast<int64_t>(k + u * kWarps) * N + o0 + lane;
+    for (int j = 0; j < J; ++j) on[j] = o0 + lane + 32 * j < N;
+    for (int k0 = warp; k0 < K; k0 += U * kWarps) {
+      float w[U][J];
 #pragma unroll
-          for (int j = 0; j < J; ++j) w[u][j] = __ldg(row + 32 * j);
-        }
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u * kWarps;
+        const float* row = Wt + static_cast<int64_t>(k) * ld + o0 + lane;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float x = in[k + u * kWarps];
-#pragma unroll
-          for (int j = 0; j < J; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
-        }
+        for (int j = 0; j < J; ++j) w[u][j] = (k < K && on[j]) ? __ldg(row + 32 * j) : 0.f;
       }
-    }
-    for (; k < K; k += kWarps) {
-      const float x = in[k];
-      const float* row = Wt + static_cast<int64_t>(k) * N + o0 + lane;
 #pragma unroll
-      for (int j = 0; j < J; ++j)
-        if (o0 + lane + 32 * j < N) acc[j] = fmaf(x, __ldg(row + 32 * j), acc[j]);
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u * kWarps;
+        const float x = k < K ? in[k] : 0.f;
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = fmaf(x, w[u][j], acc[j]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < J; ++j) part[warp * kPass + lane + 32 * j] = acc[j];
@@ -83,6 +79,12 @@ __device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const 
   }
 }
 
+// The whole [K, N] matrix: y[o] = epi(o, sum_k in[k] * Wt[k*N + o]).
+template <int J, int U, typename Epi>
+__device__ __forceinline__ void gemv(const float* __restrict__ in, int K, const float* __restrict__ Wt, int N,
+                                     float* part, Epi epi) {
+  gemv_cols<J, U>(in, K, Wt, N, N, part, epi);
+}
 
 // out_row[o] = t1[o] + (W_2 GELU_erf(W_1 LayerNorm(t1)))[o]: the pre-norm MLP block
 // (no biases in W_1, W_2) and its residual add for the block's token.  t1 [W] is in

@@ -39,26 +39,54 @@ struct ReadoutLaunch {
   int32_t width, heads, hidden;
 };
 
+size_t readout_smem_floats(int width, int hidden, int heads) {
+  return static_cast<size_t>(8) * width + hidden + 2 * (width / heads) + kGemvWarps * kGemvMaxPass + kGemvWarps;
+}
+
 __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __grid_constant__ ReadoutLaunch P) {
-  __shared__ float s_n[kReadoutMaxWidth];    // normalised controller input, later the MLP's normalised t1
-  __shared__ float s_r[kReadoutMaxWidth];    // normalised readings (heads -> width), later t1
-  __shared__ float s_t[kReadoutMaxWidth];    // gated readings
-  __shared__ float s_h[kReadoutMaxHidden];   // MLP hidden activations
-  __shared__ float s_part[kReadoutThreads / 32 * 256];  // partials of passes up to 256 outputs
-  __shared__ float s_red[kReadoutThreads / 32];
+  extern __shared__ float4 smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tok = blockIdx.x;  // b * T + t
   const int64_t b = tok / P.time, t = tok % P.time;
-  const int W = P.width, H = P.heads, hw = W / H;
-  for (int k = tid; k < W; k += kReadoutThreads) s_n[k] = P.normalized[tok * W + k];
-  // readings norm, one warp per head
+  const int W = P.width, H = P.heads, hw = W / H, HD = P.hidden;
+  float* s_n = reinterpret_cast<float*>(smem_raw);  // [W] controller input, later the MLP's normalised t1
+  float* s_r = s_n + W;                              // [W] readings (heads side by side), normalised; later t1
+  float* s_t = s_r + W;                              // [W] gated readings
+  float* s_tok = s_t + W;                            // [W] residual input
+  float* s_bg = s_tok + W;                           // [W] gate bias
+  float* s_bo = s_bg + W;                            // [W] output bias
+  float* s_mnw = s_bo + W;                           // [W] MLP norm
+  float* s_mnb = s_mnw + W;
+  float* s_rnw = s_mnb + W;                          // [hw] readings norm
+  float* s_rnb = s_rnw + hw;
+  float* s_h = s_rnb + hw;                           // [HD]
+  float* s_part = s_h + HD;                          // [kGemvWarps * kGemvMaxPass]
+  float* s_red = s_part + kGemvWarps * kGemvMaxPass;  // [kGemvWarps]
+  // every small operand in one batch of independent loads (one L2 round trip),
+  // instead of one dependent round trip per epilogue
+  for (int k = tid; k < W; k += kReadoutThreads) {
+    const int h = k / hw, d = k % hw;
+    s_n[k] = P.normalized[tok * W + k];
+    s_r[k] = P.readings[((b * H + h) * P.time + t) * hw + d];
+    s_tok[k] = P.tokens[tok * W + k];
+    s_bg[k] = P.bg[k];
+    s_bo[k] = P.bo[k];
+    s_mnw[k] = P.mn_w[k];
+    s_mnb[k] = P.mn_b[k];
+  }
+  for (int k = tid; k < hw; k += kReadoutThreads) {
+    s_rnw[k] = P.rn_w[k];
+    s_rnb[k] = P.rn_b[k];
+  }
+  __syncthreads();
+  // readings norm in place, one warp per head
   for (int h = warp; h < H; h += kReadoutThreads / 32) {
-    const float* row = P.readings + ((b * H + h) * P.time + t) * hw;
-    float s = 0.f;
-    for (int k = lane; k < hw; k += 32) s += row[k];
+    float* row = s_r + h * hw;
+    float sum = 0.f;
+    for (int k = lane; k < hw; k += 32) sum += row[k];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
-    const float mean = s / static_cast<float>(hw);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
+    const float mean = sum / static_cast<float>(hw);
     float q = 0.f;
     for (int k = lane; k < hw; k += 32) {
       const float d = row[k] - mean;
@@ -67,16 +95,15 @@ __global__ void __launch_bounds__(kReadoutThreads) cow_readout_kernel(const __gr
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(kFull, q, o);
     const float rstd = rsqrtf(q / static_cast<float>(hw) + P.rn_eps);
-    for (int k = lane; k < hw; k += 32) s_r[h * hw + k] = (row[k] - mean) * rstd * P.rn_w[k] + P.rn_b[k];
+    for (int k = lane; k < hw; k += 32) row[k] = (row[k] - mean) * rstd * s_rnw[k] + s_rnb[k];
   }
   __syncthreads();
   // gated readings: sigmoid(W_g n + b_g) * r
-  gemv<4, 8>(s_n, W, P.wg_t, W, s_part, [&](int o, float g) { s_t[o] = s_r[o] / (1.f + expf(-(g + P.bg[o]))); });
+  gemv<4, 4>(s_n, W, P.wg_t, W, s_part, [&](int o, float g) { s_t[o] = s_r[o] / (1.f + expf(-(g + s_bg[o]))); });
   // t1 = tokens + W_o (gated) + b_o
-  gemv<4, 8>(s_t, W, P.wo_t, W, s_part, [&](int o, float v) { s_r[o] = P.tokens[tok * W + o] + (v + P.bo[o]); });
+  gemv<4, 4>(s_t, W, P.wo_t, W, s_part, [&](int o, float v) { s_r[o] = s_tok[o] + (v + s_bo[o]); });
   // the MLP block over t1 (held in s_r)
-  mlp_residual(s_r, s_n, s_h, s_part, s_red, W, P.hidden, P.mn_w, P.mn_b, P.mn_eps, P.w1_t, P.w2_t,
-               P.out + tok * W);
+  mlp_residual(s_r, s_n, s_h, s_part, s_red, W, HD, s_mnw, s_mnb, P.mn_eps, P.w1_t, P.w2_t, P.out + tok * W);
 }
 
 }  // namespace
@@ -99,7 +126,18 @@ int cow_readout_mlp_step(const float* tokens, const float* normalized, const flo
   ReadoutLaunch P{tokens, normalized, readings, rn_weight, rn_bias, gate_weight_t, gate_bias, out_weight_t,
                   out_bias, mlp_norm_weight, mlp_norm_bias, mlp_in_weight_t, mlp_out_weight_t, out, time,
                   rn_eps, mlp_eps, width, heads, hidden};
-  cow_readout_kernel<<<static_cast<unsigned>(rows), kReadoutThreads, 0, as_stream(stream)>>>(P);
+  const size_t smem = sizeof(float) * readout_smem_floats(width, hidden, heads);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return COW_ERR_CUDA;
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return COW_ERR_UNSUPPORTED;
+  if (!configured[dev]) {
+    const int most = static_cast<int>(sizeof(float) * readout_smem_floats(kReadoutMaxWidth, kReadoutMaxHidden, 1));
+    if (cudaFuncSetAttribute(cow_readout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, most) != cudaSuccess)
+      return COW_ERR_CUDA;
+    configured[dev] = true;
+  }
+  cow_readout_kernel<<<static_cast<unsigned>(rows), kReadoutThreads, smem, as_stream(stream)>>>(P);
   return launch_status();
 }
 
