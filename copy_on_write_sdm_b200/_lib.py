@@ -102,6 +102,7 @@ _SIGNATURES = {
     "cow_prefill_recurrence_layers": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int64, c_int32,
                                                 c_int32, c_int32, c_int32, P]),
     "cow_grow": (c_int32, [P, P, c_int64, P, P, c_int64, c_int64, c_int32, P, P, P]),
+    "cow_grow_in_place": (c_int32, [P, c_int64, c_int64, P, P, P]),
     "cow_release": (c_int32, [POINTER(CowPool), P, c_int64, P, P, P, P]),
     "cow_repack": (c_int32, [POINTER(CowPool), P, P, P, c_int64, P, P, P]),
     "cow_append": (c_int32, [POINTER(CowPool), POINTER(CowPool), P, P, P, P, P]),

@@ -111,6 +111,7 @@ class PackedSDMCopyOnWriteState:
     growth_events: int = 0
     growth_rows_added: int = 0
     growth_rows_copied: int = 0
+    slab_rows_moved: int = 0
     _m0_f32: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
     def __setattr__(self, name: str, value) -> None:
@@ -121,6 +122,11 @@ class PackedSDMCopyOnWriteState:
         d["_mutations"] = d.get("_mutations", 0) + 1
         if name in _TENSOR_FIELDS:
             d["_tensor_version"] = d.get("_tensor_version", 0) + 1
+            # a slab or stack replaced other than by growth releases the growth reserve
+            store = d.get("_slab_store")
+            if store is not None and name in ("values", "free_rows") \
+                    and value.data_ptr() != store[0 if name == "values" else 1].data_ptr():
+                del d["_slab_store"]
 
     # ---------------- construction ----------------
 
@@ -411,7 +417,12 @@ class PackedSDMCopyOnWriteState:
 
     @torch.no_grad()
     def grow_capacity(self, minimum_capacity_rows: int) -> int:
-        """Grow the slab by whole quanta; row IDs stay stable (allocator.py:692-744)."""
+        """Grow the slab by whole quanta; row IDs stay stable (allocator.py:692-744).
+
+        The slab is stored with a reserve behind ``capacity_rows``, so most growths
+        only extend the views and push the new row ids (``cow_grow_in_place``); the
+        allocator state after each growth is the reference's.  ``growth_rows_copied``
+        counts what the reference copies; ``slab_rows_moved`` what this one did."""
 
         if minimum_capacity_rows <= self.capacity_rows:
             return 0
@@ -421,14 +432,33 @@ class PackedSDMCopyOnWriteState:
         selected = ((minimum_capacity_rows + quantum - 1) // quantum) * quantum
         old_capacity = self.capacity_rows
         added = selected - old_capacity
-        values = torch.empty(selected, self.width, device=self.values.device, dtype=self.values.dtype)
-        free_rows = torch.empty(selected, device=self.free_rows.device, dtype=self.free_rows.dtype)
-        self._call("cow_grow", self.values.data_ptr(), self.free_rows.data_ptr(), old_capacity,
-                   values.data_ptr(), free_rows.data_ptr(), selected, self.width,
-                   _lib.dtype_code(self.values.dtype), self.free_count.data_ptr(),
-                   self.overflow_flag.data_ptr(), self._stream())
-        self.values = values
-        self.free_rows = free_rows
+        store = self.__dict__.get("_slab_store")
+        if (store is not None and store[0].data_ptr() == self.values.data_ptr()
+                and store[1].data_ptr() == self.free_rows.data_ptr() and store[0].shape[0] >= selected):
+            # Inside the reserve: the rows exist already; only their ids join the
+            # free stack, in the order the copying growth gives them.
+            self._call("cow_grow_in_place", self.free_rows.data_ptr(), old_capacity, selected,
+                       self.free_count.data_ptr(), self.overflow_flag.data_ptr(), self._stream())
+            self.values = store[0][:selected]
+            self.free_rows = store[1][:selected]
+        else:
+            # A new slab with a reserve behind it (a quarter of the capacity, at most
+            # 1 GiB of rows, at least one quantum), so that the following growths
+            # copy nothing; old rows are copied once here.
+            row_bytes = self.width * self.values.element_size()
+            extra = max(quantum, min(selected // 4, (1 << 30) // max(row_bytes, 1)))
+            reserve = selected + ((extra + quantum - 1) // quantum) * quantum
+            device = self.values.device
+            values = torch.empty(reserve, self.width, device=device, dtype=self.values.dtype)
+            free_rows = torch.empty(reserve, device=device, dtype=self.free_rows.dtype)
+            self._call("cow_grow", self.values.data_ptr(), self.free_rows.data_ptr(), old_capacity,
+                       values.data_ptr(), free_rows.data_ptr(), selected, self.width,
+                       _lib.dtype_code(self.values.dtype), self.free_count.data_ptr(),
+                       self.overflow_flag.data_ptr(), self._stream())
+            self.__dict__["_slab_store"] = (values, free_rows)
+            self.values = values[:selected]
+            self.free_rows = free_rows[:selected]
+            self.slab_rows_moved += old_capacity
         self.proven_maximum_additional_allocations += added
         self.growth_events += 1
         self.growth_rows_added += added

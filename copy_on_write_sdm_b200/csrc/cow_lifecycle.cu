@@ -366,6 +366,14 @@ __global__ void grow_kernel(const void* old_slab, const int32_t* old_free_rows, 
   }
 }
 
+// Growth inside reserved storage: the slab rows old_cap..new_cap-1 already exist,
+// so only their ids are pushed above the current free entries, in the order the
+// copying growth gives them.
+__global__ void grow_append_kernel(int32_t* free_rows, int64_t old_cap, int64_t new_cap, const int32_t* free_count) {
+  const int64_t old_free = *free_count;
+  COW_GRID_STRIDE(i, new_cap - old_cap) { free_rows[old_free + i] = static_cast<int32_t>(old_cap + i); }
+}
+
 __global__ void grow_finish_kernel(int32_t* free_count, int64_t added, int32_t* status) {
   *free_count += static_cast<int32_t>(added);
   *status = 0;
@@ -626,6 +634,20 @@ int cow_grow(const void* old_slab, const int32_t* old_free_rows, int64_t old_cap
   const int64_t work = (row_bytes * old_capacity) / 16 > new_capacity ? (row_bytes * old_capacity) / 16 : new_capacity;
   grow_kernel<<<grid_for(work, 256), 256, 0, st>>>(old_slab, old_free_rows, old_capacity, new_slab, new_free_rows,
                                                  new_capacity, row_bytes, free_count, status);
+  if (launch_status() != COW_OK) return COW_ERR_CUDA;
+  grow_finish_kernel<<<1, 1, 0, st>>>(free_count, new_capacity - old_capacity, status);
+  return launch_status();
+}
+
+int cow_grow_in_place(int32_t* free_rows, int64_t old_capacity, int64_t new_capacity, int32_t* free_count,
+                      int32_t* status, void* stream) {
+  if (!free_rows || !free_count || !status || old_capacity < 0 || new_capacity < old_capacity ||
+      new_capacity > INT32_MAX)
+    return COW_ERR_INVALID;
+  if (new_capacity == old_capacity) return COW_OK;
+  cudaStream_t st = as_stream(stream);
+  grow_append_kernel<<<grid_for(new_capacity - old_capacity, 256), 256, 0, st>>>(free_rows, old_capacity,
+                                                                                  new_capacity, free_count);
   if (launch_status() != COW_OK) return COW_ERR_CUDA;
   grow_finish_kernel<<<1, 1, 0, st>>>(free_count, new_capacity - old_capacity, status);
   return launch_status();

@@ -233,6 +233,13 @@ int cow_grow(const void* old_slab, const int32_t* old_free_rows, int64_t old_cap
              void* new_slab, int32_t* new_free_rows, int64_t new_capacity, int64_t width,
              int32_t slab_dtype, int32_t* free_count, int32_t* status, void* stream);
 
+/* grow_capacity (allocator.py:692-744) when the slab and free stack already have
+ * storage for new_capacity rows (a reserve behind the current capacity): the
+ * same resulting stack and free_count as cow_grow, with no row copy.  free_rows
+ * must hold new_capacity entries. */
+int cow_grow_in_place(int32_t* free_rows, int64_t old_capacity, int64_t new_capacity, int32_t* free_count,
+                      int32_t* status, void* stream);
+
 /* release (allocator.py:1019-1068): push every live row of the selected banks
  * at old_free + rank over the flattened [S,slots] order given; clear their map
  * rows.  `released` receives the count (device int32).  `bank_mask` is int32

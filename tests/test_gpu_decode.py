@@ -166,6 +166,8 @@ def test_growth_through_prepare_step_capacity(dev):
         np.testing.assert_allclose(got.cpu().numpy(), want, atol=ATOL, rtol=RTOL)
     assert st.growth_events == ref.growth_events > 0
     assert st.growth_rows_copied == ref.growth_rows_copied
+    # growths inside the reserve move no rows (only the first copies the initial slab)
+    assert st.growth_events > 2 and st.slab_rows_moved < st.growth_rows_copied
     assert st.proven_maximum_additional_allocations == ref.proven_maximum_additional_allocations
     assert_same_state(st, ref)
     st.validate_invariants()
