@@ -38,6 +38,7 @@ struct AttentionLaunch {
   int64_t capacity;
   float ln_eps, mn_eps;
   int32_t width, heads, hidden;
+  int32_t vec;  // cache rows read as float4 words: head width a multiple of 4, caches 16-byte aligned
 };
 
 size_t attention_smem_floats(int width, int heads, int hidden, int64_t capacity) {
@@ -99,14 +100,35 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
     cache[((b * H + h) * cap + pos) * hw + d] = s_qkv[(1 + which) * W + hd];
   }
   __syncthreads();  // the block's cache stores are visible to its own loads below
-  // scores, one thread per (head, position)
+  // scores, one thread per (head, position); a key row is read as float4 words,
+  // all issued before the dot product so one row costs one round trip
   const float scale = 1.f / sqrtf(static_cast<float>(hw));
+  const bool vec = P.vec != 0;
   for (int i = tid; i < H * L; i += kGemvThreads) {
     const int h = i / L, j = i % L;
     const float* kr = P.key_cache + ((b * H + h) * cap + j) * hw;
     const float* q = s_qkv + h * hw;
     float dot = 0.f;
-    for (int d = 0; d < hw; ++d) dot = fmaf(q[d], kr[d], dot);
+    if (vec) {
+      for (int d0 = 0; d0 < hw; d0 += 32) {
+        float4 kv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          kv[u] = d0 + 4 * u < hw ? __ldg(reinterpret_cast<const float4*>(kr + d0) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (d0 + 4 * u < hw) {
+            const float* qq = q + d0 + 4 * u;
+            dot = fmaf(qq[0], kv[u].x, dot);
+            dot = fmaf(qq[1], kv[u].y, dot);
+            dot = fmaf(qq[2], kv[u].z, dot);
+            dot = fmaf(qq[3], kv[u].w, dot);
+          }
+        }
+      }
+    } else {
+      for (int d = 0; d < hw; ++d) dot = fmaf(q[d], kr[d], dot);
+    }
     s_sc[i] = dot * scale;
   }
   __syncthreads();
@@ -128,24 +150,53 @@ __global__ void __launch_bounds__(kGemvThreads) cow_attention_kernel(const __gri
     if (lane == 0) s_inv[h] = 1.f / sum;
   }
   __syncthreads();
-  // o[h, d] = sum_j p[h, j] V[h, j, d]: strands of threads split j, coalesced over (h, d)
+  // o[h, d] = sum_j p[h, j] V[h, j, d]: strands of threads split j; with hw a
+  // multiple of 4 a thread owns four dimensions (float4 loads, 32 strands at width
+  // 128), each strand issuing its value rows eight at a time
   {
-    const int strands = kGemvThreads / W;
-    const int hd = tid % W, st = tid / W;
-    float v = 0.f;
+    const int cols = vec ? W / 4 : W;  // threads per strand
+    const int strands = kGemvThreads / cols;
+    const int c = tid % cols, st = tid / cols;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (st < strands) {
-      const int h = hd / hw, d = hd % hw;
+      const int hd = vec ? 4 * c : c, h = hd / hw, d = hd % hw;
       const float* vr = P.value_cache + (b * H + h) * cap * hw + d;
       const float* p = s_sc + h * L;
-      for (int j = st; j < L; j += strands) v = fmaf(p[j], vr[static_cast<int64_t>(j) * hw], v);
+      for (int j0 = st; j0 < L; j0 += 8 * strands) {
+        float4 x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u * strands;
+          if (j < L)
+            x[u] = vec ? __ldg(reinterpret_cast<const float4*>(vr + static_cast<int64_t>(j) * hw))
+                       : make_float4(__ldg(vr + static_cast<int64_t>(j) * hw), 0.f, 0.f, 0.f);
+          else
+            x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u * strands;
+          const float pj = j < L ? p[j] : 0.f;
+          v.x = fmaf(pj, x[u].x, v.x);
+          v.y = fmaf(pj, x[u].y, v.y);
+          v.z = fmaf(pj, x[u].z, v.z);
+          v.w = fmaf(pj, x[u].w, v.w);
+        }
+      }
+      // partials reuse the gemv scratch: strands * W <= kGemvThreads * 4 floats
+      float* pp = s_part + st * W + hd;
+      pp[0] = v.x;
+      if (vec) {
+        pp[1] = v.y;
+        pp[2] = v.z;
+        pp[3] = v.w;
+      }
     }
-    // partials reuse the gemv scratch: strands * W <= kGemvThreads floats
-    if (st < strands) s_part[st * W + hd] = v;
     __syncthreads();
     for (int o = tid; o < W; o += kGemvThreads) {
-      float s = 0.f;
-      for (int k = 0; k < strands; ++k) s += s_part[k * W + o];
-      s_o[o] = s * s_inv[o / hw];
+      float sum = 0.f;
+      for (int k = 0; k < strands; ++k) sum += s_part[k * W + o];
+      s_o[o] = sum * s_inv[o / hw];
     }
     __syncthreads();
   }
@@ -183,7 +234,9 @@ int cow_attention_mlp_decode(const float* tokens, const int64_t* positions, cons
   }
   AttentionLaunch P{tokens, positions, ln_weight, ln_bias, qkv_weight_t, out_weight_t, key_cache, value_cache,
                     mlp_norm_weight, mlp_norm_bias, mlp_in_weight_t, mlp_out_weight_t, out, capacity, ln_eps,
-                    mlp_eps, width, heads, hidden};
+                    mlp_eps, width, heads, hidden,
+                    ((width / heads) % 4 == 0 && (reinterpret_cast<uintptr_t>(key_cache) |
+                                                  reinterpret_cast<uintptr_t>(value_cache)) % 16 == 0) ? 1 : 0};
   cow_attention_kernel<<<static_cast<unsigned>(batch), kGemvThreads, smem, as_stream(stream)>>>(P);
   return launch_status();
 }
