@@ -396,22 +396,60 @@ __global__ void status_or_kernel(const __grid_constant__ Layers<StatusOrCtx> L) 
   if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(c.status, *c.bits);
 }
 
+// One warp per bank row of the map.  Rows of 16-byte multiples (slots % 4 == 0,
+// the map 16-byte aligned) move as int4 words, four in flight per lane.
+__device__ __forceinline__ bool map_row_vec(const int32_t* map, int64_t slots) {
+  return (slots & 3) == 0 && (reinterpret_cast<uintptr_t>(map) & 15) == 0;
+}
+
+// A bank that is not retained must hold no live rows (release cleared them);
+// retained banks are not read at all.
 __global__ void retain_check_kernel(const __grid_constant__ Layers<RetainCtx> L) {
   const RetainCtx& c = L.c[blockIdx.y];
-  COW_GRID_STRIDE(i, c.banks * c.slots) {
-    if (c.map[i] >= 0 && c.mask[i / c.slots] == 0) atomicOr(c.status, COW_ST_DISCARD_LIVE);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const bool vec = map_row_vec(c.map, c.slots);
+  for (int64_t b = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); b < c.banks;
+       b += warps) {
+    if (c.mask[b]) continue;
+    const int32_t* row = c.map + b * c.slots;
+    bool live = false;
+    if (vec) {
+      const int4* r4 = reinterpret_cast<const int4*>(row);
+#pragma unroll 4
+      for (int64_t j = lane; j < c.slots / 4; j += 32) {
+        const int4 v = r4[j];
+        live |= (v.x >= 0) | (v.y >= 0) | (v.z >= 0) | (v.w >= 0);
+      }
+    } else {
+      for (int64_t j = lane; j < c.slots; j += 32) live |= row[j] >= 0;
+    }
+    if (__any_sync(kFull, live) && lane == 0) atomicOr(c.status, COW_ST_DISCARD_LIVE);
   }
 }
 
+// Survivor s takes bank idx[s]'s map row and template, in list order.
 __global__ void retain_gather_kernel(const __grid_constant__ Layers<RetainCtx> L) {
   const RetainCtx& c = L.c[blockIdx.y];
   if (c.banks == 0) return;
-  COW_GRID_STRIDE(i, c.count * c.slots) {
-    const int64_t s = i / c.slots;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const bool vec = map_row_vec(c.map, c.slots) && map_row_vec(c.new_map, c.slots);
+  for (int64_t s = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); s < c.count;
+       s += warps) {
     int64_t b = c.idx[s];
     b = b < 0 ? 0 : (b >= c.banks ? c.banks - 1 : b);
-    c.new_map[i] = c.map[b * c.slots + i % c.slots];
-    if (i % c.slots == 0) c.new_templates[s] = c.templates[b];
+    const int32_t* src = c.map + b * c.slots;
+    int32_t* dst = c.new_map + s * c.slots;
+    if (vec) {
+      const int4* s4 = reinterpret_cast<const int4*>(src);
+      int4* d4 = reinterpret_cast<int4*>(dst);
+#pragma unroll 4
+      for (int64_t j = lane; j < c.slots / 4; j += 32) d4[j] = s4[j];
+    } else {
+      for (int64_t j = lane; j < c.slots; j += 32) dst[j] = src[j];
+    }
+    if (lane == 0) c.new_templates[s] = c.templates[b];
   }
 }
 
@@ -897,11 +935,11 @@ int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count,
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   if (pool->banks * pool->slots > 0) {
-    retain_check_kernel<<<layer_grid(pool->banks * pool->slots, 256, 1), 256, 0, st>>>(R);
+    retain_check_kernel<<<layer_grid(pool->banks * 32, 256, 1), 256, 0, st>>>(R);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   if (count > 0 && pool->banks > 0) {
-    retain_gather_kernel<<<layer_grid(count * pool->slots, 256, 1), 256, 0, st>>>(R);
+    retain_gather_kernel<<<layer_grid(count * 32, 256, 1), 256, 0, st>>>(R);
     return launch_status();
   }
   return COW_OK;
@@ -939,19 +977,19 @@ int cow_retain_layers(const cow_pool* pools, const int64_t* const* bank_indices,
                        new_templates[l], status + l};
     w += words16(p.banks > 0 ? p.banks : 1);
     max_count = std::max(max_count, cnt);
-    max_map = std::max(max_map, p.banks * p.slots);
-    if (p.banks > 0) max_gather = std::max(max_gather, cnt * p.slots);
+    if (p.slots > 0) max_map = std::max(max_map, p.banks);  // one warp per bank row
+    if (p.banks > 0 && p.slots > 0) max_gather = std::max(max_gather, cnt);
   }
   if (max_count > 0) {
     bank_list_kernel<<<layer_grid(max_count, 256, layers), 256, 0, st>>>(B);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   if (max_map > 0) {
-    retain_check_kernel<<<layer_grid(max_map, 256, layers), 256, 0, st>>>(R);
+    retain_check_kernel<<<layer_grid(max_map * 32, 256, layers), 256, 0, st>>>(R);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   if (max_gather > 0) {
-    retain_gather_kernel<<<layer_grid(max_gather, 256, layers), 256, 0, st>>>(R);
+    retain_gather_kernel<<<layer_grid(max_gather * 32, 256, layers), 256, 0, st>>>(R);
     return launch_status();
   }
   return COW_OK;
