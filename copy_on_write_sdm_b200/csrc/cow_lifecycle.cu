@@ -310,35 +310,57 @@ __global__ void prefill_mark_kernel(const __grid_constant__ Layers<MarkCtx> L, i
 // One warp per row; 16-byte vectors when both dtypes allow it.  mode 0: row
 // src_rows[k] of src; mode 1: src_rows[k] is a flat bank*slots+slot index and
 // the row comes from m0[templates[bank], slot].
+constexpr int kCopyRowsPerWarp = 4;  // rows a warp moves per iteration, their loads in flight together
+
 __global__ void copy_rows_kernel(const __grid_constant__ Layers<CopyCtx> L) {
   const CopyCtx& c = L.c[blockIdx.y];
   const int lane = threadIdx.x & 31;
   const int64_t count = c.count_dev != nullptr ? min(c.count, static_cast<int64_t>(*c.count_dev)) : c.count;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t width = c.width;
-  for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); k < count; k += warps) {
-    const int64_t d = c.dst_rows ? c.dst_rows[k] : k;
-    const void* sbase = c.src;
-    int sdt = c.src_dt;
-    int64_t s;
-    if (c.mode == 1) {
-      const int64_t flat = c.src_rows[k];
-      s = c.templates[flat / c.slots] * c.slots + flat % c.slots;
-      sbase = c.m0;
-      sdt = COW_F32;
-    } else {
-      s = c.src_rows ? c.src_rows[k] : k;
+  const void* sbase = c.mode == 1 ? static_cast<const void*>(c.m0) : c.src;
+  const int sdt = c.mode == 1 ? static_cast<int>(COW_F32) : c.src_dt;
+  const bool small = c.slots > 0 && c.slots < (int64_t{1} << 31);
+  for (int64_t k0 = (blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5)) * kCopyRowsPerWarp;
+       k0 < count; k0 += warps * kCopyRowsPerWarp) {
+    int64_t d[kCopyRowsPerWarp], s[kCopyRowsPerWarp];
+#pragma unroll
+    for (int u = 0; u < kCopyRowsPerWarp; ++u) {
+      const int64_t k = k0 + u < count ? k0 + u : count - 1;  // a clamped duplicate rewrites the same row
+      d[u] = c.dst_rows ? c.dst_rows[k] : k;
+      if (c.mode == 1) {
+        const int64_t flat = c.src_rows[k];
+        int64_t bank, slot;
+        if (small && flat >= 0 && flat < (int64_t{1} << 31)) {
+          const uint32_t f = static_cast<uint32_t>(flat), n = static_cast<uint32_t>(c.slots);
+          bank = f / n;
+          slot = f - static_cast<uint32_t>(bank) * n;
+        } else {
+          bank = flat / c.slots;
+          slot = flat % c.slots;
+        }
+        s[u] = c.templates[bank] * c.slots + slot;
+      } else {
+        s[u] = c.src_rows ? c.src_rows[k] : k;
+      }
     }
     if ((width & 3) == 0) {
       for (int64_t e = lane * 4; e < width; e += 128) {
-        st4_rt(c.dst, d * width + e, ld4_rt(sbase, s * width + e, sdt), c.dst_dt);
+        float4 v[kCopyRowsPerWarp];
+#pragma unroll
+        for (int u = 0; u < kCopyRowsPerWarp; ++u) v[u] = ld4_rt(sbase, s[u] * width + e, sdt);
+#pragma unroll
+        for (int u = 0; u < kCopyRowsPerWarp; ++u) st4_rt(c.dst, d[u] * width + e, v[u], c.dst_dt);
       }
     } else {
-      for (int64_t e = lane; e < width; e += 32) {
-        const float v = ld1_rt(sbase, s * width + e, sdt);
-        if (c.dst_dt == COW_F32) static_cast<float*>(c.dst)[d * width + e] = v;
-        else if (c.dst_dt == COW_BF16) static_cast<__nv_bfloat16*>(c.dst)[d * width + e] = __float2bfloat16_rn(v);
-        else static_cast<__half*>(c.dst)[d * width + e] = __float2half_rn(v);
+#pragma unroll
+      for (int u = 0; u < kCopyRowsPerWarp; ++u) {
+        for (int64_t e = lane; e < width; e += 32) {
+          const float v = ld1_rt(sbase, s[u] * width + e, sdt);
+          if (c.dst_dt == COW_F32) static_cast<float*>(c.dst)[d[u] * width + e] = v;
+          else if (c.dst_dt == COW_BF16) static_cast<__nv_bfloat16*>(c.dst)[d[u] * width + e] = __float2bfloat16_rn(v);
+          else static_cast<__half*>(c.dst)[d[u] * width + e] = __float2half_rn(v);
+        }
       }
     }
   }
