@@ -73,6 +73,31 @@ class CowStep(ctypes.Structure):
     ]
 
 
+class CowHostPipeline(ctypes.Structure):
+    _fields_ = [
+        ("pools", POINTER(CowPool)),
+        ("steps", POINTER(CowStep)),
+        ("layers", c_int32),
+        ("writes", c_int32),
+        ("reads", c_int32),
+        ("index_dtype", c_int32),
+        ("act_dtype", c_int32),
+        ("_pad", c_int32),
+        ("scan_scratch", c_void_p),
+        ("scratch_bytes", c_int64),
+        ("device_inputs", c_void_p),
+        ("input_bytes", c_int64),
+        ("host_outputs", c_void_p),
+        ("device_outputs", c_void_p),
+        ("output_bytes", c_int64),
+        ("h2d_stream", c_void_p),
+        ("d2h_stream", c_void_p),
+        ("h2d_done", c_void_p),
+        ("computed", c_void_p),
+        ("d2h_done", c_void_p),
+    ]
+
+
 P = c_void_p
 _SIGNATURES = {
     "cow_abi_version": (c_int32, []),
@@ -84,6 +109,7 @@ _SIGNATURES = {
                                           c_int32, c_int32, P]),
     "cow_decode_step_host": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32, c_int32,
                                        c_int32, P, c_int64, P, P, c_int64, P, P, c_int64, P]),
+    "cow_decode_step_host_piped": (c_int32, [P, P, P]),
     "cow_decode_step_host_overlapped": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                                   c_int32, c_int32, P, c_int64, P, P, c_int64, P, P, c_int64,
                                                   P, P, P, P, P, P]),

@@ -687,6 +687,15 @@ int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps
   return COW_OK;
 }
 
+int cow_decode_step_host_piped(const cow_host_pipeline* p, const void* host_inputs, void* compute_stream) {
+  if (!p) return COW_ERR_INVALID;
+  return cow_decode_step_host_overlapped(p->pools, p->steps, p->layers, p->writes, p->reads, p->index_dtype,
+                                         p->act_dtype, p->scan_scratch, p->scratch_bytes, p->device_inputs,
+                                         host_inputs, p->input_bytes, p->host_outputs, p->device_outputs,
+                                         p->output_bytes, compute_stream, p->h2d_stream, p->d2h_stream, p->h2d_done,
+                                         p->computed, p->d2h_done);
+}
+
 int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
                             int32_t reads, int32_t index_dtype, int32_t act_dtype, void* stream) {
   if (!pools || !steps || layers < 1 || layers > COW_MAX_LAYERS) return COW_ERR_INVALID;

@@ -113,6 +113,14 @@ class DecodeSession:
         self._scratch = decode_scratch(self.device, B * len(pools), len(pools))
         self._need = B * writes  # first touches one step can make in a pool
         self._proof_steps, self._proof_key = 0, None
+        # free-count snapshots copied to the host without a synchronisation
+        # (see _prove): the issued-step counter, the pending snapshot and its
+        # pinned landing buffer
+        self._issued = 0
+        self._snap = None
+        self._snapshots = True  # off for good once a step decodes on another stream than the current one
+        self.snapshot_proofs = 0  # pool proofs renewed from a snapshot instead of a synchronising read
+        self._snap_host = torch.empty(len(pools), dtype=torch.int32, pin_memory=pinned_host)
         self._out_bytes = self.host_outputs.numel() * self.host_outputs.element_size()
         self._device_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._lib = _lib.load()
@@ -131,28 +139,48 @@ class DecodeSession:
             self._pool_key = key
         return self._pool_array
 
-    def _prove(self) -> None:
+    def _prove(self, on_current: bool = True) -> None:
         """The reference's per-step capacity proof (allocator.py:746-774) for every pool.
 
         The common case (every pool proven with rows left for this step) is one
         decrement per pool: after a full check the session knows how many steps
         every pool's proof still covers, and keeps that count while no pool was
-        assigned to since (its ``_mutations`` counter is unchanged)."""
+        assigned to since (its ``_mutations`` counter is unchanged).
+
+        When a proof runs out the reference reads ``free_count`` (a host
+        synchronisation).  Two steps before that, the session copies every
+        pool's free count to pinned host memory in the background; a pool whose
+        proof runs out then takes ``snapshot - need x (steps issued after it)``
+        as its proof when that lower bound covers the step.  Otherwise, or when
+        the snapshot has not landed or a pool changed since, the reference's
+        synchronising check runs, so growth happens at exactly the steps where
+        the reference grows (the bound never exceeds the true free count).
+        Snapshots are taken and used only while every step decodes on the current
+        stream, which orders them with the decodes they must follow."""
         need = self._need
         pools = self.pools
+        self._issued += 1
+        if not on_current:
+            self._snapshots, self._snap = False, None
         if self._proof_steps > 0 and self._proof_key == tuple(p.__dict__["_mutations"] for p in pools):
             self._proof_steps -= 1
             for p in pools:
                 d = p.__dict__
                 d["proven_maximum_additional_allocations"] -= need
+            if self._proof_steps <= 2 and self._snap is None and self._snapshots:
+                self._snapshot()
             return
+        snap = self._snap_bounds()
         steps = None
-        for p in pools:
+        for l, p in enumerate(pools):
             d = p.__dict__
             if d["growth_quantum_rows"]:
                 left = d["proven_maximum_additional_allocations"]
                 if left >= need and d["capacity_is_proven"]:
                     d["proven_maximum_additional_allocations"] = left - need
+                elif snap is not None and d["capacity_is_proven"] and snap[l] >= need:
+                    d["proven_maximum_additional_allocations"] = snap[l] - need
+                    self.snapshot_proofs += 1
                 else:
                     p.prepare_step_capacity(need)
                 left = d["proven_maximum_additional_allocations"] // need if need else 1 << 30
@@ -164,14 +192,40 @@ class DecodeSession:
         self._proof_steps = steps or 0
         self._proof_key = tuple(p.__dict__["_mutations"] for p in pools)
 
+    def _snapshot(self) -> None:
+        """Queue a copy of every pool's free count (after the steps issued so far) to
+        pinned host memory on the current stream (not while it is being captured)."""
+        if torch.cuda.is_current_stream_capturing():
+            return
+        counts = torch.cat([p.free_count.reshape(1) for p in self.pools])
+        self._snap_host.copy_(counts, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._snap = (ev, self._issued - 1, tuple(p.__dict__["_mutations"] for p in self.pools))
+
+    def _snap_bounds(self):
+        """Per-pool lower bounds on the free rows before the step being issued, from a
+        landed snapshot taken since the pools last changed; None otherwise."""
+        snap, self._snap = self._snap, None
+        if snap is None:
+            return None
+        ev, at, key = snap
+        if key != tuple(p.__dict__["_mutations"] for p in self.pools) or torch.cuda.is_current_stream_capturing() \
+                or not ev.query():
+            return None
+        # every step issued after the snapshot pops at most `need` rows per pool
+        charged = self._need * (self._issued - 1 - at)
+        return [int(c) - charged for c in self._snap_host.tolist()]
+
     def _stream_handle(self) -> int:
         return _current_raw_stream(self._device_index)
 
     @torch.no_grad()
     def step(self, *, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """One decode token for every bank of every pool; returns ``outputs`` ``[L, B, D]`` (device)."""
-        self._prove()
-        handle = stream.cuda_stream if stream is not None else self._stream_handle()
+        current = self._stream_handle()
+        handle = stream.cuda_stream if stream is not None else current
+        self._prove(on_current=handle == current)
         _lib.check(self._lib.cow_decode_step(self._pools(), self._steps, len(self.pools), self.writes, self.reads,
                                              _lib.I64, self._act_code, self._scratch.data_ptr(),
                                              self._scratch.numel(), handle), "cow_decode_step")
@@ -194,16 +248,26 @@ class DecodeSession:
                 for ev in pair:
                     ev.record(h2d)
             torch.cuda.synchronize(self.device)
+            host_outputs = (self.host_outputs, torch.empty_like(self.host_outputs, pin_memory=pinned))
+            inputs, outputs, steps = (self.inputs, alt), (self.outputs, out_alt), (self._steps, steps_alt)
+            # one descriptor per buffer pair: every argument of the overlapped step
+            # but the host input bytes and the compute stream
+            descs = tuple(_lib.CowHostPipeline(
+                None, ctypes.cast(steps[b], ctypes.POINTER(_lib.CowStep)), len(self.pools), self.writes, self.reads,
+                _lib.I64, self._act_code, 0, self._scratch.data_ptr(), self._scratch.numel(), inputs[b].data_ptr(),
+                self.step_bytes, host_outputs[b].data_ptr(), outputs[b].data_ptr(), self._out_bytes,
+                h2d.cuda_stream, d2h.cuda_stream, events[b][0].cuda_event, events[b][1].cuda_event,
+                events[b][2].cuda_event) for b in range(2))
             self._pipe = {
-                "inputs": (self.inputs, alt), "outputs": (self.outputs, out_alt), "steps": (self._steps, steps_alt),
-                "host_outputs": (self.host_outputs, torch.empty_like(self.host_outputs, pin_memory=pinned)),
-                "h2d": h2d, "d2h": d2h, "events": events, "k": 0,
+                "inputs": inputs, "outputs": outputs, "steps": steps, "host_outputs": host_outputs,
+                "h2d": h2d, "d2h": d2h, "events": events, "k": 0, "descs": descs,
+                "desc_ptrs": tuple(ctypes.addressof(d) for d in descs), "desc_pools": None,
             }
         return self._pipe
 
     @torch.no_grad()
     def step_host_pipelined(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
-        """Host-to-host step overlapped with its neighbours (``cow_decode_step_host_overlapped``).
+        """Host-to-host step overlapped with its neighbours (``cow_decode_step_host_piped``).
 
         ``host_step`` holds the step's pinned input bytes (``inputs`` layout).
         Returns the pinned host buffer that will hold this step's readouts
@@ -214,19 +278,19 @@ class DecodeSession:
         if host_step.numel() != self.step_bytes or host_step.dtype != torch.uint8 \
                 or host_step.device.type != "cpu" or not host_step.is_contiguous():
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
-        pipe = self._pipeline()
+        pipe = self._pipe if self._pipe is not None else self._pipeline()
         b = pipe["k"] & 1
         pipe["k"] += 1
         self._prove()
-        h2d_done, computed, d2h_done = pipe["events"][b]
-        out, dev_out = pipe["host_outputs"][b], pipe["outputs"][b]
-        _lib.check(self._lib.cow_decode_step_host_overlapped(
-            self._pools(), pipe["steps"][b], len(self.pools), self.writes, self.reads, _lib.I64, self._act_code,
-            self._scratch.data_ptr(), self._scratch.numel(), pipe["inputs"][b].data_ptr(), host_step.data_ptr(),
-            self.step_bytes, out.data_ptr(), dev_out.data_ptr(), self._out_bytes,
-            self._stream_handle(), pipe["h2d"].cuda_stream, pipe["d2h"].cuda_stream,
-            h2d_done.cuda_event, computed.cuda_event, d2h_done.cuda_event), "cow_decode_step_host_overlapped")
-        return out, d2h_done
+        pools = self._pools()
+        if pipe["desc_pools"] is not pools:  # a pool's tensors were replaced: new pool array
+            for d in pipe["descs"]:
+                d.pools = ctypes.cast(pools, ctypes.POINTER(_lib.CowPool))
+            pipe["desc_pools"] = pools
+        rc = self._lib.cow_decode_step_host_piped(pipe["desc_ptrs"][b], host_step.data_ptr(), self._stream_handle())
+        if rc:
+            _lib.check(rc, "cow_decode_step_host_piped")
+        return pipe["host_outputs"][b], pipe["events"][b][2]
 
     @torch.no_grad()
     def step_host(self, host_step: torch.Tensor | None = None) -> torch.Tensor:

@@ -165,6 +165,33 @@ int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps
                                     int64_t output_bytes, void* compute_stream, void* h2d_stream, void* d2h_stream,
                                     void* h2d_done, void* computed, void* d2h_done);
 
+/* The constant arguments of cow_decode_step_host_overlapped for one buffer pair,
+ * built once by a runtime that streams many steps through the same pools and
+ * buffers (rebuilt whenever a pool's tensors are replaced). */
+typedef struct cow_host_pipeline {
+  const cow_pool* pools;
+  const cow_step* steps;
+  int32_t layers, writes, reads, index_dtype, act_dtype, _pad;
+  void* scan_scratch;
+  int64_t scratch_bytes;
+  void* device_inputs;
+  int64_t input_bytes;
+  void* host_outputs;
+  const void* device_outputs;
+  int64_t output_bytes;
+  void* h2d_stream;
+  void* d2h_stream;
+  void* h2d_done;
+  void* computed;
+  void* d2h_done;
+} cow_host_pipeline;
+
+/* cow_decode_step_host_overlapped with the arguments of `pipe`, for the step
+ * whose pinned input bytes are `host_inputs`, decoded on `compute_stream`.
+ * Same ordering and error behaviour; three arguments cross the binding per
+ * step instead of twenty-one. */
+int cow_decode_step_host_piped(const cow_host_pipeline* pipe, const void* host_inputs, void* compute_stream);
+
 /* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
  * allocator.py:368-460): the same math on dense [banks,slots,width] tables.
  * memories[l] has dtype mem_dtype; same limits as cow_decode_step. */

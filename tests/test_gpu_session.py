@@ -27,6 +27,40 @@ def _pools(dev, layers, banks, slots, width, quantum, seed):
             for _ in range(layers)]
 
 
+def test_snapshot_proofs_keep_growth_where_the_reference_grows(dev):
+    """Proofs renewed from background free-count snapshots (no synchronisation)
+    leave maps, stacks, capacity and growth events exactly as the reference's
+    per-step proof does."""
+    from copy_on_write_sdm_b200 import DecodeSession, packed_sdm_cow_step_layers
+
+    layers, banks, slots, width, W, R = 2, 32, 512, 128, 4, 16
+    quantum = O.growth_quantum_rows(banks, W, 8)
+    ref = _pools(dev, layers, banks, slots, width, quantum, 1)
+    new = _pools(dev, layers, banks, slots, width, quantum, 1)
+    sess = DecodeSession(new, writes=W, reads=R)
+    rng = np.random.default_rng(9)
+    for step in range(40):
+        xs = [O.synthetic_step_inputs(rng, banks, slots, width, W, R) for _ in range(layers)]
+        for l, x in enumerate(xs):
+            for k, v in x.items():
+                sess.host_views[l][k].copy_(torch.from_numpy(v))
+        sess.step_host()
+        torch.cuda.synchronize(dev)  # snapshots land before they are needed
+        got = sess.host_outputs.clone()
+        for p in ref:
+            p.prepare_step_capacity(banks * W)
+        want = packed_sdm_cow_step_layers(ref, [{k: torch.from_numpy(v).to(dev) for k, v in x.items()} for x in xs])
+        torch.cuda.synchronize(dev)
+        for l in range(layers):
+            np.testing.assert_allclose(got[l].numpy(), want[l].cpu().numpy(), atol=1e-5, rtol=1e-5)
+    assert sess.snapshot_proofs > 0
+    for p, q in zip(ref, new):
+        assert torch.equal(p.logical_to_physical, q.logical_to_physical)
+        assert torch.equal(p.free_rows[:int(p.free_count)], q.free_rows[:int(q.free_count)])
+        assert p.capacity_rows == q.capacity_rows and p.growth_events == q.growth_events > 0
+        q.validate_invariants()
+
+
 def test_session_matches_per_call_api_through_growth(dev):
     from copy_on_write_sdm_b200 import DecodeSession, packed_sdm_cow_step_layers
 
