@@ -893,15 +893,16 @@ def run_gpu_model(args, rank, world, device):
     # e2e: a fresh prefill, then K graphed steps fed from pinned host ids, greedy ids read back
     _, state = model.prefill(ids_dev[:, :M_PREFIX], capacity=M_MAXLEN)
     runner = GraphedDecode(model, state)
-    host_ids = ids[:, M_PREFIX:].contiguous().pin_memory()
+    # one contiguous pinned [B,1] block per step, as a serving loop holds the next ids
+    host_ids = ids[:, M_PREFIX:].t().contiguous().unsqueeze(-1).pin_memory()
     nxt = torch.empty(M_BATCH, 1, dtype=torch.int64).pin_memory()
     for i in range(Wm):
-        runner.step(host_ids[:, i:i + 1].to(device, non_blocking=True))
+        runner.step(host_ids[i].to(device, non_blocking=True))
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(Wm, Wm + K):
-        logits = runner.step(host_ids[:, i:i + 1].to(device, non_blocking=True))
+        logits = runner.step(host_ids[i].to(device, non_blocking=True))
         nxt.copy_(logits.argmax(-1), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize(device)
@@ -910,7 +911,7 @@ def run_gpu_model(args, rank, world, device):
     state_bytes = state.storage_bytes()
     return dict(total_ms=dev_ms, eager_ms=eager_ms, e2e_ms=e0.elapsed_time(e1), clocks=clocks.summary(),
                 setup_s=setup_s, captures=runner.captures,
-                state_bytes=state_bytes, h2d=host_ids[:, :1].numel() * 8, d2h=nxt.numel() * 8)
+                state_bytes=state_bytes, h2d=host_ids[0].numel() * 8, d2h=nxt.numel() * 8)
 
 
 def main_model(args, rank, world, device) -> int:

@@ -65,6 +65,7 @@ class GraphedDecode:
         self._alloc(state.batch)
         self.replays = 0
         self.captures = 0
+        self._active_ok = None  # key of the active-flags tensor last found all true
 
     def _alloc(self, batch: int) -> None:
         self.batch = batch
@@ -73,14 +74,15 @@ class GraphedDecode:
         self.logits = None
 
     def _tensor_key(self):
+        """What the captured graph depends on: the batch, each pool object and its
+        tensor-replacement counter (slab, map, stack, counters; capacity follows the
+        slab view) and the K/V cache tensors.  Objects are keyed by identity and kept
+        referenced with the graph (``_key_refs``), so an id in a held key cannot be
+        reused by another object."""
         s = self.state
-        key = [s.batch]
-        for st in s.sdm_states:
-            key += [st.values.data_ptr(), st.logical_to_physical.data_ptr(), st.free_rows.data_ptr(),
-                    st.template_indices.data_ptr(), st.free_count.data_ptr(), st.overflow_flag.data_ptr(),
-                    st._m0_f32.data_ptr(), st.capacity_rows]
-        key += [t.data_ptr() for t in (*s.dense_keys, *s.dense_values)]
-        return tuple(key)
+        objs = (*s.sdm_states, *s.dense_keys, *s.dense_values)
+        return (s.batch, tuple(id(o) for o in objs),
+                tuple(st.__dict__.get("_tensor_version", 0) for st in s.sdm_states)), objs
 
     def _body(self) -> torch.Tensor:
         """One token through the stack, reading ``self.ids`` / ``self.pos``."""
@@ -114,8 +116,15 @@ class GraphedDecode:
             raise ValueError("sequence exceeds maximum_sequence_length")
         if state.position >= state.capacity:
             raise ValueError("decode state has reached its fixed capacity")
-        if not bool(state.active_sequences.all()):
-            raise ValueError("released requests must be removed before further decode")
+        # The reference reads the active flags every token (a host synchronisation);
+        # they change only through assignments or in-place tensor ops, so one
+        # passing check holds until the tensor object or its version changes.
+        act = state.active_sequences
+        ok = self._active_ok
+        if ok is None or ok[0] is not act or ok[1] != act._version:
+            if not bool(act.all()):
+                raise ValueError("released requests must be removed before further decode")
+            self._active_ok = (act, act._version)  # holds the tensor, so its identity cannot be reused
         for st, module in zip(state.sdm_states, (model.stack.sdm_layers[str(i)] for i in state.sdm_layer_positions)):
             if st.banks != state.batch * module.memory_heads:
                 raise ValueError("packed SDM banks do not match batch and memory heads")
@@ -138,7 +147,7 @@ class GraphedDecode:
             self.pos.fill_(state.position)
         else:
             self.pos.copy_(state.positions)
-        key = self._tensor_key()
+        key, objs = self._tensor_key()
         if key != self._key or self._graph is None:
             # Eager step (it is this token's real step), then capture for the next ones.
             self._graph = None
@@ -150,7 +159,7 @@ class GraphedDecode:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 self.logits = self._body()
-            self._graph, self._key = graph, key
+            self._graph, self._key, self._key_refs = graph, key, objs
             self.captures += 1
             self.logits.copy_(logits)
         else:
