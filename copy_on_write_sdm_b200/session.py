@@ -156,7 +156,9 @@ class DecodeSession:
         synchronising check runs, so growth happens at exactly the steps where
         the reference grows (the bound never exceeds the true free count).
         Snapshots are taken and used only while every step decodes on the current
-        stream, which orders them with the decodes they must follow."""
+        stream, which orders them with the decodes they must follow.  A step run on
+        these pools outside the session goes through ``prepare_step_capacity`` (the
+        reference's contract), whose assignment invalidates a pending snapshot."""
         need = self._need
         pools = self.pools
         self._issued += 1
