@@ -106,3 +106,18 @@ def test_attention_entry_rejects_bad_arguments():
     assert call(64, 2, 256, 8, ws) == _lib.ERR_INVALID  # output aliasing the residual input
     assert call(1024, 2, 256, 8, out) == _lib.ERR_UNSUPPORTED  # wider than the compiled kernel
     assert call(128, 4, 512, 1 << 20, out) == _lib.ERR_UNSUPPORTED  # scores beyond shared memory
+
+
+def test_growth_in_place_and_piped_step_reject_bad_arguments():
+    lib = _lib.load()
+    ws = ctypes.create_string_buffer(64)
+    # a shrinking, negative or missing-buffer growth is rejected before any launch
+    assert lib.cow_grow_in_place(ws, 8, 4, ws, ws, None) == _lib.ERR_INVALID
+    assert lib.cow_grow_in_place(ws, -1, 4, ws, ws, None) == _lib.ERR_INVALID
+    assert lib.cow_grow_in_place(None, 4, 8, ws, ws, None) == _lib.ERR_INVALID
+    assert lib.cow_grow_in_place(ws, 4, 8, None, ws, None) == _lib.ERR_INVALID
+    assert lib.cow_grow_in_place(ws, 4, 1 << 32, ws, ws, None) == _lib.ERR_INVALID
+    # no descriptor, and a descriptor without buffers or events
+    assert lib.cow_decode_step_host_piped(None, ws, None) == _lib.ERR_INVALID
+    desc = _lib.CowHostPipeline()
+    assert lib.cow_decode_step_host_piped(ctypes.addressof(desc), ws, None) == _lib.ERR_INVALID
