@@ -98,13 +98,18 @@ class FaithfulSDMDecodeState:
         """Return the private rows of finished requests to every layer's pool (inference.py:71-114)."""
         if sequence_indices is None:
             chosen = self.active_sequences.nonzero().flatten()
-        else:
-            chosen = torch.as_tensor(sequence_indices, device=self.device, dtype=torch.int64)
+            host = chosen.tolist()
+        elif isinstance(sequence_indices, torch.Tensor):
+            chosen = sequence_indices.to(device=self.device, dtype=torch.int64)
+            host = chosen.tolist() if chosen.ndim == 1 else None
+        else:  # a host sequence: checked on the host, copied to the device once
+            flat = torch.as_tensor(sequence_indices, dtype=torch.int64)
+            host = flat.tolist() if flat.ndim == 1 else None
+            chosen = flat.to(self.device)
         if chosen.ndim != 1:
             raise ValueError("released sequence indices must be a vector")
         if chosen.numel() == 0:
             return 0
-        host = chosen.tolist()
         if (min(host) < 0 or max(host) >= self.batch or len(set(host)) != len(host)
                 or not bool(self.active_sequences[chosen].all())):
             raise ValueError("released sequence is invalid, duplicated, or inactive")
@@ -126,7 +131,7 @@ class FaithfulSDMDecodeState:
             if not before:
                 self.position = 0
             elif self.positions is not None:
-                self.position = int(self.positions.max().item())
+                self.position = self._max_position()
             return keep
         positions = self.current_positions()
         if before:
@@ -138,7 +143,8 @@ class FaithfulSDMDecodeState:
         if self.positions is not None:
             self.positions = kept_positions
         self.active_sequences = torch.ones(keep.numel(), device=self.device, dtype=torch.bool)
-        self.position = int(kept_positions.max().item()) if keep.numel() else 0
+        self.position = (self._max_position() if self.positions is not None else int(kept_positions.max().item())) \
+            if keep.numel() else 0
         return keep
 
     @torch.no_grad()
@@ -161,13 +167,28 @@ class FaithfulSDMDecodeState:
                                   for p in zip(self.dense_values, incoming.dense_values))
         merged = torch.cat((self.current_positions(), incoming.current_positions())).contiguous()
         self.active_sequences = torch.ones(merged.numel(), device=self.device, dtype=torch.bool)
-        if merged.numel() and bool((merged == merged[0]).all()):
-            self.position, self.positions = int(merged[0].item()), None
+        if merged.numel():
+            # all positions equal <=> min == max; one read for both
+            lo, hi = torch.stack((merged.min(), merged.max())).tolist()
+            if lo == hi:
+                self.position, self.positions = lo, None
+            else:
+                self.positions = merged
+                self.position = hi
         else:
             self.positions = merged
-            if merged.numel():
-                self.position = int(merged.max().item())
         return incoming.batch
+
+    def _max_position(self) -> int:
+        """``int(positions.max())``, read again only when the positions tensor was
+        replaced or changed in place since the last read."""
+        pos = self.positions
+        cached = self.__dict__.get("_max_position_of")
+        if cached is not None and cached[0] is pos and cached[1] == pos._version:
+            return cached[2]
+        value = int(pos.max().item())
+        self.__dict__["_max_position_of"] = (pos, pos._version, value)  # holds the tensor: its identity stays unique
+        return value
 
     @torch.no_grad()
     def trim_sdm_pools(self, *, headroom_rows: int = 0) -> int:
