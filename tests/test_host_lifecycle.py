@@ -41,3 +41,22 @@ def test_max_position_is_cached_while_unchanged(monkeypatch):
     monkeypatch.setattr(torch.Tensor, "max", counting_max)
     assert state._max_position() == 7
     assert not calls
+
+
+def test_slab_reserve_is_released_when_the_slab_is_replaced():
+    """Growth keeps the slab and stack as views of a reserved store; a slab or stack
+    replaced any other way (trim, restore) drops that store so its memory is freed."""
+    from copy_on_write_sdm_b200.allocator import PackedSDMCopyOnWriteState
+
+    st = PackedSDMCopyOnWriteState(
+        shared_initial_memory=torch.zeros(1, 4, 8), template_indices=torch.zeros(2, dtype=torch.int64),
+        values=torch.zeros(16, 8), logical_to_physical=torch.full((2, 4), -1, dtype=torch.int32),
+        free_rows=torch.arange(16, dtype=torch.int32), free_count=torch.tensor(16, dtype=torch.int32),
+        overflow_flag=torch.tensor(0, dtype=torch.int32))
+    store = (torch.zeros(32, 8), torch.zeros(32, dtype=torch.int32))
+    st.__dict__["_slab_store"] = store
+    st.values = store[0][:24]  # growth inside the reserve: same storage, the store stays
+    st.free_rows = store[1][:24]
+    assert st.__dict__.get("_slab_store") is store and st.capacity_rows == 24
+    st.values = torch.zeros(20, 8)  # replaced by other means: the reserve goes
+    assert "_slab_store" not in st.__dict__
