@@ -107,14 +107,14 @@ def step_inputs(gen, banks, steps, device):
     )
 
 
-def prefill_pools(gen, banks, device):
+def prefill_pools(gen, banks, device, prefix=PREFIX):
     from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState
 
     q = max(16, banks * WRITES * QUANTUM_STEPS)
     states = []
     for _ in range(LAYERS):
         m0 = 0.02 * torch.randn(HEADS, SLOTS, WIDTH, generator=gen, device=device)
-        shape = (banks, PREFIX)
+        shape = (banks, prefix)
         st, _ = PackedSDMCopyOnWriteState.from_prefix_routes(
             m0,
             uniform_routes(gen, shape, WRITES, device),
@@ -197,15 +197,28 @@ def _c_step(inputs, s, l, outputs):
                         outputs[l].data_ptr(), None)
 
 
-def run_gpu(args, rank, world, device):
+def _sum_state_bytes(states) -> dict:
+    out = {}
+    for st in states:
+        for k, v in st.storage_bytes().items():
+            out[k] = out.get(k, 0) + v
+    return out
+
+
+def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=True):
+    """Configuration 3 on this rank: ``batch`` requests, ``prefix`` prefill tokens.
+
+    ``extras`` adds the warm-L2 trace, the single-launch timing and the
+    end-to-end legs; without it the flushed device trace, the dense control
+    and the incremental graph timing run (the sub-legs of the default run)."""
     from copy_on_write_sdm_b200 import _lib, allocator, packed_sdm_cow_step_layers, dense_sdm_sparse_step_layers
 
     lib = _lib.load()
-    gen = torch.Generator(device=device).manual_seed(1000 + rank)
-    banks = BATCH * HEADS
+    gen = torch.Generator(device=device).manual_seed(1000 + rank + 17 * prefix)
+    banks = batch * HEADS
     K, Wm = args.steps, args.warmup
     t_setup = time.time()
-    states = prefill_pools(gen, banks, device)
+    states = prefill_pools(gen, banks, device, prefix)
     inputs = step_inputs(gen, banks, K + Wm, device)
     torch.cuda.synchronize(device)
     setup_s = time.time() - t_setup
@@ -274,7 +287,7 @@ def run_gpu(args, rank, world, device):
     # latency of every launch to its interval): the single-token latency.
     single = []
     with torch.cuda.stream(stream):
-        for s in range(Wm, Wm + min(K, 16)):
+        for s in (range(Wm, Wm + min(K, 16)) if extras else ()):
             g1 = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g1, stream=stream):
                 packed_launch(s)
@@ -285,7 +298,7 @@ def run_gpu(args, rank, world, device):
             e1.record(stream)
             torch.cuda.synchronize(device)
             single.append(e0.elapsed_time(e1))
-    single_ms = statistics.median(single)
+    single_ms = statistics.median(single) if single else None
 
     # Warm-L2 trace: all K steps captured in ONE graph and replayed back to
     # back (no host in the loop; the pool state stays L2-resident).  The
@@ -312,7 +325,7 @@ def run_gpu(args, rank, world, device):
             torch.cuda.synchronize(device)
             return e0.elapsed_time(e1)
 
-        warm = time_graph(trace_graph(packed_launch))
+        warm = time_graph(trace_graph(packed_launch)) if extras else None
 
         # Dense-table control, same routes, same timing disciplines.
         mems = [st.materialize_dense() for st in states]
@@ -323,7 +336,7 @@ def run_gpu(args, rank, world, device):
             _lib.check(lib.cow_dense_step(dptrs, dbanks, step_structs[s], LAYERS, SLOTS, WIDTH, _lib.F32, WRITES,
                                           READS, _lib.I64, _lib.F32, stream.cuda_stream), "cow_dense_step")
 
-        dense_warm = time_graph(trace_graph(dense_launch))
+        dense_warm = time_graph(trace_graph(dense_launch)) if extras else None
         dgraph, dev_ev = flushed_trace(dense_launch)
         with torch.cuda.stream(stream):
             dgraph.replay()
@@ -345,9 +358,18 @@ def run_gpu(args, rank, world, device):
             return g
 
         base = time_graph(flushed_only(None))
+        # The incremental graphs re-apply the K steps twice more to the evolved
+        # pools: prove capacity for them (pools whose slots are all private pop nothing).
+        for st in states:
+            st.prepare_step_capacity(banks * WRITES * 2 * K)
         incremental = {"packed_us": 1e3 * (time_graph(flushed_only(packed_launch)) - base) / K,
                        "dense_us": 1e3 * (time_graph(flushed_only(dense_launch)) - base) / K}
         del mems
+
+    if not extras:
+        return dict(total_ms=total_ms, step_ms=step_ms, dense_ms=dense_ms, incremental=incremental,
+                    first_touches=first_touches, clocks=clocks.summary(), setup_s=setup_s, banks=banks,
+                    state_bytes=_sum_state_bytes(states))
 
     # End to end through the public runtime API with host buffers: every step
     # copies its packed routes from pinned host memory (one copy), runs the
@@ -395,10 +417,7 @@ def run_gpu(args, rank, world, device):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    state_bytes = {}
-    for st in states:
-        for k, v in st.storage_bytes().items():
-            state_bytes[k] = state_bytes.get(k, 0) + v
+    state_bytes = _sum_state_bytes(states)
     used = [st.used_bytes() for st in states]
     return dict(total_ms=total_ms, step_ms=step_ms, single_ms=single_ms, e2e_ms=e2e_ms, e2e_serial_ms=e2e_serial_ms,
                 warm_ms=warm, incremental=incremental,
@@ -1001,6 +1020,22 @@ def cpu_decode_rate(seconds: float, threads: int, *, warmup: int = 0, steps: int
                       f"top-{READS}/top-{WRITES}) from a post-prefix pool, {dt:.2f} s, numpy oracle"}
 
 
+def _hbm_peak():
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(peaks_path):
+        return json.load(open(peaks_path))["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def _reduce_dict(d: dict, device) -> dict:
+    """Sum of a dict of byte counts over ranks (the dict itself at one rank)."""
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    keys = sorted(d)
+    vals = reduce_over_ranks([float(d[k]) for k in keys], op="sum", device=device)
+    return {k: int(v) for k, v in zip(keys, vals)}
+
+
 def config_block(world: int) -> dict:
     return {"workload": "config 3 synthetic random-route serving screen: 7 independent SDM pools, N=256, D=128, "
                         "H=1, top-16 read/top-4 write, uniform seeded routes, prefix 2048 (sparse prefill), "
@@ -1032,6 +1067,69 @@ def _reserve_stdout() -> None:
     os.dup2(2, 1)
 
 
+def _leg_line(res, total_ms, K, batch_per_gpu, world, note) -> dict:
+    """Summary of a flushed-trace sub-leg (rank 0's own figures beside the max over ranks)."""
+    peak, peak_src = _hbm_peak()
+    per_launch = algorithmic_bytes(res["banks"] * LAYERS, res["first_touches"] // max(K, 1))
+    mean_s = res["total_ms"] / K / 1e3
+    out = {"value": batch_per_gpu * world * K / (total_ms / 1e3), "unit": "tokens/s", "ms_per_step": total_ms / K,
+           "batch_per_gpu": batch_per_gpu, "global_batch": batch_per_gpu * world, "note": note,
+           "first_touches_in_timed_steps": res["first_touches"],
+           "roofline": {"bound": "hbm", "achieved": per_launch / mean_s / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": per_launch / mean_s / 1e9 / peak, "peak_source": peak_src,
+                        "algorithmic_bytes_per_launch": per_launch, "mean_launch_us": mean_s * 1e6},
+           "retained_state": res["state_bytes"], "clocks": res["clocks"]}
+    if res.get("dense_ms") is not None:
+        out["dense_control"] = {"ms_per_step": res["dense_ms"] / K,
+                                "packed_latency_overhead_pct": 100.0 * (res["total_ms"] / res["dense_ms"] - 1.0)}
+    inc = res.get("incremental")
+    if inc is not None:
+        out["graph_incremental"] = {**inc, "packed_latency_overhead_pct": 100.0 * (inc["packed_us"] / inc["dense_us"] - 1.0)}
+    return out
+
+
+def sub_legs(args, rank, world, device, res, total_ms) -> dict:
+    """Legs of the default run beside the headline (all ranks take part; rank 0 reports).
+
+    * ``allocating_prefix16``: the screen at prefix 16, the reference's own
+      serving-screen prefix, where timed steps pop rows (about half of the
+      routed slots are still shared), with its dense control;
+    * ``strong_split``: B=64 requests in total, 64/N per GPU (N > 1);
+    * ``scaleout``: configuration 4 (1,024 requests over all GPUs, prefix
+      4,096, Zipf routes), steps capped at 32."""
+    from copy_on_write_sdm_b200.sharding import reduce_over_ranks
+
+    K = args.steps
+    legs = {}
+    if not args.legs:
+        return legs
+    r16 = run_gpu(args, rank, world, device, prefix=16, extras=False)
+    (t16,) = reduce_over_ranks([r16["total_ms"]], op="max", device=device)
+    legs["allocating_prefix16"] = _leg_line(r16, t16, K, BATCH, world,
+                                            "configuration 3 at prefix 16 (reference serving screen, "
+                                            "benchmark_serving.py:628): timed steps allocate rows")
+    if world > 1:
+        rs = run_gpu(args, rank, world, device, batch=max(1, BATCH // world), extras=False)
+        (ts,) = reduce_over_ranks([rs["total_ms"]], op="max", device=device)
+        legs["strong_split"] = {**_leg_line(rs, ts, K, max(1, BATCH // world), world,
+                                            f"B={BATCH} requests in total, {BATCH // world} per GPU"),
+                                "scaling": "strong"}
+    else:
+        legs["strong_split"] = {"value": BATCH * K / (total_ms / 1e3), "unit": "tokens/s", "scaling": "strong",
+                                "note": "at one GPU the strong split is the headline itself"}
+    torch.cuda.empty_cache()
+    so_args = argparse.Namespace(**vars(args))
+    so_args.steps, so_args.warmup = min(args.steps, 32), min(args.warmup, 4)
+    so_args.requests, so_args.prefix = SO_REQUESTS, SO_PREFIX
+    so = scaleout_line(so_args, rank, world, device, cpu_seconds=min(args.cpu_seconds, 5.0))
+    torch.cuda.empty_cache()
+    if so is not None:
+        legs["scaleout"] = {k: so[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling", "roofline",
+                                                "cpu_baseline", "retained_state", "first_touches_in_timed_steps",
+                                                "mean_touched_rows_per_bank", "clocks", "config", "setup_s")}
+    return legs
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1046,6 +1144,8 @@ def main() -> int:
     ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
     ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
     ap.add_argument("--trim-every", type=int, default=0, help="churn: trim the pools every this many steps")
+    ap.add_argument("--no-legs", dest="legs", action="store_false",
+                    help="screen: skip the prefix-16, strong-split and configuration-4 legs")
     ap.add_argument("--churn-warm-prefix", type=int, default=CH_WARM_PREFIX,
                     help="churn: prefix tokens of the initial batch")
     args = ap.parse_args()
@@ -1074,10 +1174,8 @@ def main() -> int:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
-        # rank 0's stdout carries exactly one JSON line: keep NCCL's version
-        # banner (NCCL_DEBUG=VERSION) off it
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL's own output (version banner, NCCL_DEBUG lines) reaches stderr:
+        # _reserve_stdout keeps the result line alone on stdout.
         torch.distributed.init_process_group("nccl", device_id=device)
     torch.backends.cuda.matmul.allow_tf32 = False
     if args.workload == "scaleout":
@@ -1092,6 +1190,8 @@ def main() -> int:
 
     # Job time = the slowest rank (each rank owns its own 64 requests).
     total_ms, e2e_ms = reduce_over_ranks([res["total_ms"], res["e2e_ms"]], op="max", device=device)
+    state_all = _reduce_dict(res["state_bytes"], device)
+    legs = sub_legs(args, rank, world, device, res, total_ms)
     if rank != 0:
         torch.distributed.destroy_process_group()
         return 0
@@ -1099,11 +1199,7 @@ def main() -> int:
     K = args.steps
     tokens = BATCH * world * K
     value = tokens / (total_ms / 1e3)
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(peaks_path):
-        peak, peak_src = json.load(open(peaks_path))["hbm_gbs"], "measured"
-    else:
-        peak, peak_src = 6650.0, "fallback"
+    peak, peak_src = _hbm_peak()
     per_launch = algorithmic_bytes(BATCH * HEADS * LAYERS, res["first_touches"] // max(K, 1))
     mean_launch_s = (res["total_ms"] / K) / 1e3
     achieved = per_launch / mean_launch_s / 1e9
@@ -1145,9 +1241,11 @@ def main() -> int:
             "packed_latency_overhead_pct": 100.0 * (res["warm_ms"] / res["dense_warm_ms"] - 1.0),
             "note": "all K steps in one CUDA graph, back to back, pool state L2-resident"},
         "retained_state": {"allocated_rows": res["allocated_rows"], "capacity_rows": res["capacity_rows"],
-                           "live_value_bytes": res["live_value_bytes"], **res["state_bytes"]},
+                           "live_value_bytes": res["live_value_bytes"], **res["state_bytes"],
+                           "all_gpus": state_all},
         "first_touches_in_timed_steps": res["first_touches"],
         "setup_s": res["setup_s"],
+        **legs,
     }
     emit(line)
     if world > 1:
@@ -1155,22 +1253,23 @@ def main() -> int:
     return 0
 
 
-def main_scaleout(args, rank, world, device) -> int:
+def scaleout_line(args, rank, world, device, *, cpu_seconds) -> dict | None:
+    """Configuration 4 (strong scaling: ``args.requests`` over all ranks); rank 0
+    returns the result line, the other ranks None."""
     from copy_on_write_sdm_b200.sharding import reduce_over_ranks
 
     res = run_gpu_scaleout(args, rank, world, device)
-    (total_ms,) = reduce_over_ranks([res["total_ms"]], op="max", device=device)
+    total_ms = reduce_over_ranks([res["total_ms"]], op="max", device=device)[0]
+    state_bytes = _reduce_dict(res["state_bytes"], device)
     if rank != 0:
-        torch.distributed.destroy_process_group()
-        return 0
+        return None
     K = args.steps
     tokens = res["requests"] * world * K
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak, peak_src = (json.load(open(peaks_path))["hbm_gbs"], "measured") if os.path.exists(peaks_path) else (6650.0, "fallback")
+    peak, peak_src = _hbm_peak()
     per_launch = algorithmic_bytes(res["banks"] * LAYERS, res["first_touches"] // max(K, 1))
     mean_s = res["total_ms"] / K / 1e3
     achieved = per_launch / mean_s / 1e9
-    line = {
+    return {
         "metric": METRIC, "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -1184,14 +1283,22 @@ def main_scaleout(args, rank, world, device) -> int:
                      "traffic": TRAFFIC_SCALEOUT["bytes_per_launch_per_bank"] * res["banks"] * LAYERS,
                      "traffic_source": TRAFFIC_SCALEOUT["source"], "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": per_launch,
-                     "mean_launch_us": mean_s * 1e6, "kernel": "cow_decode_kernel<f32,1,4,1>"},
-        "e2e": None, "gpu_launches": K, "clocks": res["clocks"],
-        "cpu_baseline": cpu_scaleout_rate(args.cpu_seconds, res["requests"] * world, args.prefix),
+                     "mean_launch_us": mean_s * 1e6, "kernel": "cow_count_kernel + cow_decode_kernel<f32,1,4,1>",
+                     "timing": "rank 0's launches, each timed by its own CUDA event pair on the launching stream"},
+        "gpu_launches": 2 * K, "clocks": res["clocks"],
+        "cpu_baseline": cpu_scaleout_rate(cpu_seconds, res["requests"] * world, args.prefix),
         "mean_touched_rows_per_bank": res["mean_touched_rows_per_bank"],
-        "first_touches_in_timed_steps": res["first_touches"], "retained_state": res["state_bytes"],
+        "first_touches_in_timed_steps": res["first_touches"],
+        "retained_state": {"all_gpus": state_bytes, "rank0": res["state_bytes"]},
         "setup_s": res["setup_s"],
     }
-    emit(line)
+
+
+def main_scaleout(args, rank, world, device) -> int:
+    line = scaleout_line(args, rank, world, device, cpu_seconds=args.cpu_seconds)
+    if line is not None:
+        line["e2e"] = None
+        emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0

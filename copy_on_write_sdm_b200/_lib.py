@@ -105,6 +105,8 @@ _SIGNATURES = {
     "cow_decode_scratch_bytes": (c_int64, [c_int64, c_int32]),
     "cow_decode_step": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                   c_int32, c_int32, P, c_int64, P]),
+    "cow_decode_step_checked": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
+                                          c_int32, c_int32, P, c_int64, P, POINTER(c_int32)]),
     "cow_decode_step_noalloc": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                           c_int32, c_int32, P]),
     "cow_decode_step_host": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32, c_int32,

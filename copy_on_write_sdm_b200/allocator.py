@@ -52,25 +52,42 @@ class SDMCopyOnWriteStep:
 # --------------------------------------------------------------------------
 
 _DECODE_SCRATCH: dict[int, torch.Tensor] = {}
+# Buffers that decode_scratch replaced.  A CUDA graph that captured a decode
+# launch keeps the scratch address it was captured with, so a replaced buffer
+# must never go back to the caching allocator: it stays here for the life of
+# the process (a few KB to a few MB per device in all).
+_RETIRED_DECODE_SCRATCH: list[torch.Tensor] = []
 _M0_CACHE: dict[tuple, torch.Tensor] = {}
 
 
 def decode_scratch(device: torch.device, total_banks: int, layers: int) -> torch.Tensor:
     """Zero-initialised look-back scratch of the fused decode step, one per device.
 
-    The decode kernel leaves it ready for the next launch (its last block
-    recycles the header), so it is allocated once and reused, including by
-    launches captured in CUDA graphs.  Decode launches that could overlap on
-    the GPU (different streams) must pass their own ``scratch=`` buffer.
+    Every decode launch tags its scan flags with one launch epoch and advances
+    it once all its pools are closed, so one buffer serves any sequence of
+    launches on one stream, whatever their pool layouts, including launches
+    captured in CUDA graphs.  When a larger launch needs more bytes the buffer
+    is replaced (at least doubling) and the old one is kept alive, so graphs
+    that captured it stay valid.  Decode launches that could overlap on the
+    GPU (different streams) must pass their own ``scratch=`` buffer.
     """
     need = int(_lib.load().cow_decode_scratch_bytes(total_banks, layers))
     key = device.index if device.index is not None else torch.cuda.current_device()
     buf = _DECODE_SCRATCH.get(key)
     if buf is None or buf.numel() < need:
-        size = max(need, 4096)
+        size = max(need, 4096, 0 if buf is None else 2 * buf.numel())
+        if buf is not None:
+            _RETIRED_DECODE_SCRATCH.append(buf)
         buf = torch.zeros(size, dtype=torch.uint8, device=device)
         _DECODE_SCRATCH[key] = buf
     return buf
+
+
+def new_decode_scratch(device: torch.device, total_banks: int, layers: int) -> torch.Tensor:
+    """A private zero-filled decode scratch buffer for one owner (a session or
+    a captured graph), sized for ``layers`` pools of ``total_banks`` banks."""
+    need = int(_lib.load().cow_decode_scratch_bytes(total_banks, layers))
+    return torch.zeros(max(need, 4096), dtype=torch.uint8, device=device)
 
 
 def _scan_scratch(device: torch.device, n: int) -> torch.Tensor:
@@ -1154,12 +1171,15 @@ def packed_sdm_cow_step(
     backend: str = "auto",
     validate_routes: bool = True,
     collect_diagnostics: bool = True,
+    scratch: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, SDMCopyOnWriteStep | None]:
     """One exact sparse SDM write + read through the packed overlay (allocator.py:1382-1526).
 
     One fused kernel launch.  With ``validate_routes`` (or when the capacity
     is not proven) the call synchronises once to turn device status bits
     (bad index, repeated write, exhausted slab) into ``ValueError``.
+    ``scratch`` (not in the reference's signature) is an optional owner-held
+    look-back buffer (``new_decode_scratch``); the per-device one otherwise.
     """
 
     _check_backend(backend)
@@ -1168,7 +1188,7 @@ def packed_sdm_cow_step(
                   input_gate=input_gate, forget_log_gate=forget_log_gate, read_indices=read_indices,
                   read_weights=read_weights, erase_gate=erase_gate)]
     result = packed_sdm_cow_step_layers([state], steps, validate_routes=validate_routes,
-                                        collect_diagnostics=collect_diagnostics)
+                                        collect_diagnostics=collect_diagnostics, scratch=scratch)
     if not collect_diagnostics:
         return result[0], None
     outputs, firsts = result

@@ -18,7 +18,15 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kBanksPerCta = 4;  // warps per decode CTA
 constexpr int kSpinLimit = 1 << 21;
 constexpr int kLookbackPerLane = 4;  // scan flags each lane reads per look-back probe
-constexpr int kScanHeaderBytes = 8 * COW_MAX_LAYERS;  // per pool: ticket, epoch
+// Scan scratch header (32-bit words): one ticket / arrival word per pool slot,
+// then the launch epoch and the count of pools closed in the running launch.
+// Every flag a launch writes carries the launch epoch, which the last pool to
+// close advances once; flags left by any earlier launch, whatever its pool
+// layout, therefore carry an older epoch and never read as published.
+constexpr int kScanHeaderBytes = 8 * COW_MAX_LAYERS;
+constexpr int kEpochWord = COW_MAX_LAYERS;
+constexpr int kClosedWord = COW_MAX_LAYERS + 1;
+static_assert(4 * (kClosedWord + 1) <= kScanHeaderBytes, "scan header too small");
 
 // --------------------------------------------------------------------------
 // element access
@@ -192,11 +200,12 @@ struct DecodeLayer {
 
 struct DecodeLaunch {
   DecodeLayer layer[COW_MAX_LAYERS];
-  uint32_t* header;    // per pool: [ticket, epoch]
+  uint32_t* header;    // [ticket per pool slot] + launch epoch + closed-pool count
   uint64_t* flags;        // one per bank slot, pool-major (tile_begin * 4 + bank)
   uint64_t* group_flags;  // one per group of kScanGroup banks, pool-major (group_begin + group)
   int32_t layers, width, writes, reads, idx64, act_dt, total_tiles, dynamic_tiles, stage_map, read_stage_bytes;
   int32_t two_pass, counter_close;  // counter_close: pools close by arrival count (cow_decode_kernel)
+  int32_t active_pools;             // pools with at least one bank (each closes once per launch)
 };
 
 constexpr uint32_t kFlagAggregate = 1u;
@@ -204,6 +213,18 @@ constexpr uint32_t kFlagInclusive = 2u;
 
 __device__ __forceinline__ uint64_t pack_flag(uint32_t epoch, uint32_t st, uint32_t v) {
   return (static_cast<uint64_t>(epoch) << 32) | (static_cast<uint64_t>(st) << 30) | (v & 0x3fffffffu);
+}
+
+// Called once per pool and launch, after every bank of that pool has read the
+// launch epoch.  The last pool to close resets the count and advances the
+// epoch, so every pool of the launch read the same epoch and no later launch
+// can mistake one of this launch's flags for its own.
+__device__ __forceinline__ void close_pool_epoch(uint32_t* header, int active_pools, uint32_t epoch) {
+  const uint32_t closed = atomicAdd(&header[kClosedWord], 1u);
+  if (static_cast<int>(closed) == active_pools - 1) {
+    header[kClosedWord] = 0u;
+    *reinterpret_cast<volatile uint32_t*>(&header[kEpochWord]) = epoch + 1u;
+  }
 }
 
 __device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t* p) {

@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   int l = 0;
   while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l].tile_begin + P.layer[l].tiles) ++l;
   const DecodeLayer& L = P.layer[l];
-  uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
+  uint32_t* hdr = P.header + l;  // this pool's ticket / arrival word
   int tile;
   if (P.dynamic_tiles && !P.two_pass) {
     // More blocks than can be resident at once: a ticket orders the tiles by
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   int old_free = 0, excl_given = 0;
   if (lane == 0) {
     if (!P.two_pass) {
-      epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
+      epoch = *reinterpret_cast<volatile uint32_t*>(&P.header[kEpochWord]);
       old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
     }
   }
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       *L.free_count = remaining > 0 ? remaining : 0;
     }
     hdr[0] = 0u;
-    *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+    close_pool_epoch(P.header, P.active_pools, epoch);
   }
 
   // Exclusive prefix of first touches over the preceding banks of this pool
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
           *L.free_count = remaining > 0 ? remaining : 0;
         }
         if (P.dynamic_tiles) hdr[0] = 0u;
-        *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+        close_pool_epoch(P.header, P.active_pools, epoch);
       }
     }
   }
@@ -325,14 +325,14 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
   int l = 0;
   while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l].count_block_begin + P.layer[l].count_blocks) ++l;
   const DecodeLayer& L = P.layer[l];
-  uint32_t* hdr = P.header + 2 * l;  // [ticket, epoch]
+  uint32_t* hdr = P.header + l;  // this pool's block ticket
   // The decode pass may start now: it waits for this grid only where it reads
   // the prefixes.
   asm volatile("griddepcontrol.launch_dependents;");
   if (tid == 0) {
     s_blk = P.dynamic_tiles ? static_cast<int>(atomicAdd(&hdr[0], 1u))
                             : static_cast<int>(blockIdx.x) - L.count_block_begin;
-    s_epoch = *reinterpret_cast<volatile uint32_t*>(&hdr[1]);
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(&P.header[kEpochWord]);
     s_old = *reinterpret_cast<volatile int32_t*>(L.free_count);
   }
   s_bad[tid] = 0;
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
     const int remaining = s_old - inclusive;
     *L.free_count = remaining > 0 ? remaining : 0;
     if (P.dynamic_tiles) hdr[0] = 0u;
-    *reinterpret_cast<volatile uint32_t*>(&hdr[1]) = epoch + 1u;
+    close_pool_epoch(P.header, P.active_pools, epoch);
   }
 }
 
@@ -429,10 +429,11 @@ thread_local int last_cuda_error = 0;
 }  // namespace cowrt
 
 // Look-back scratch of cow_decode_step_noalloc.  Static device memory starts
-// zeroed when the module loads (ticket 0, epoch 0, every flag "not
-// published"), and each launch leaves it ready for the next one.  In host
-// code the name is only a stand-in: the device address comes from
-// cudaGetSymbolAddress below.
+// zeroed when the module loads (tickets 0, epoch 0, every flag "not
+// published").  Each launch resets the tickets it used and advances the one
+// launch epoch, so the array is ready for the next call whatever pool layout
+// that call has.  In host code the name is only a stand-in: the device
+// address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[COW_NOALLOC_SCRATCH_BYTES];
 
 namespace {
@@ -534,6 +535,7 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     tiles += L.tiles;
   }
   if (tiles == 0) return COW_OK;
+  for (int l = 0; l < layers; ++l) P.active_pools += pools[l].banks > 0 ? 1 : 0;
   int64_t groups = 0;
   for (int l = 0; l < layers; ++l) {
     P.layer[l].group_begin = groups;
@@ -615,6 +617,32 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   }
   fn<<<tiles, kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
+}
+
+int cow_decode_step_checked(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
+                            int32_t reads, int32_t index_dtype, int32_t act_dtype, void* scan_scratch,
+                            int64_t scratch_bytes, void* stream, int32_t* status_out) {
+  const int rc = cow_decode_step(pools, steps, layers, writes, reads, index_dtype, act_dtype, scan_scratch,
+                                 scratch_bytes, stream);
+  if (rc != COW_OK) return rc;
+  cudaStream_t st = as_stream(stream);
+  int32_t words[COW_MAX_LAYERS] = {};
+  for (int l = 0; l < layers; ++l) {
+    const cudaError_t e = cudaMemcpyAsync(&words[l], pools[l].status, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) {
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+  }
+  const cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    cowrt::last_cuda_error = static_cast<int>(e);
+    return COW_ERR_CUDA;
+  }
+  int32_t any = 0;
+  for (int l = 0; l < layers; ++l) any |= words[l];
+  if (status_out) *status_out = any;
+  return any != 0 ? COW_ERR_DEVICE : COW_OK;
 }
 
 int cow_decode_step_host(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,

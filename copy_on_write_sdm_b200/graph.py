@@ -30,7 +30,7 @@ from __future__ import annotations
 
 import torch
 
-from .allocator import packed_sdm_cow_step
+from .allocator import new_decode_scratch, packed_sdm_cow_step
 from .inference import FaithfulSDMDecodeState, _step_kwargs
 
 
@@ -72,6 +72,11 @@ class GraphedDecode:
         self.ids = torch.zeros(batch, 1, dtype=torch.int64, device=self.device)
         self.pos = torch.zeros(batch, dtype=torch.int64, device=self.device)
         self.logits = None
+        # Look-back scratch owned by this decoder: a captured graph keeps its
+        # address, so it must live exactly as long as the graphs that use it
+        # (a batch change replaces it and forces a new capture).
+        banks = max((st.banks for st in self.state.sdm_states), default=0)
+        self.scratch = new_decode_scratch(self.device, max(banks, 1), 1)
 
     def _tensor_key(self):
         """What the captured graph depends on: the batch, each pool object and its
@@ -103,7 +108,7 @@ class GraphedDecode:
             module = stack.sdm_layers[str(i)]
             step = module.controller(tokens)
             reading, _ = packed_sdm_cow_step(state.sdm_states[b_i], **_step_kwargs(step), validate_routes=False,
-                                             collect_diagnostics=False)
+                                             collect_diagnostics=False, scratch=self.scratch)
             tokens = module.finish_residual(tokens, step.normalized, reading[:, None], stack.sdm_mlps[str(i)])
             b_i += 1
         return model.output(model.final_norm(tokens))

@@ -33,7 +33,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .allocator import PackedSDMCopyOnWriteState, decode_scratch
+from .allocator import PackedSDMCopyOnWriteState, new_decode_scratch
 
 
 def _current_raw_stream(device_index: int) -> int:
@@ -110,7 +110,7 @@ class DecodeSession:
         self._act_code = _lib.dtype_code(act_dtype)
         self._pool_key = None
         self._pool_array = None
-        self._scratch = decode_scratch(self.device, B * len(pools), len(pools))
+        self._scratch = new_decode_scratch(self.device, B * len(pools), len(pools))  # owned by this session
         self._need = B * writes  # first touches one step can make in a pool
         self._proof_steps, self._proof_key = 0, None
         # free-count snapshots copied to the host without a synchronisation

@@ -33,7 +33,7 @@ extern "C" {
 #define COW_ERR_INVALID 1      /* bad argument (null pointer, size, alignment) */
 #define COW_ERR_UNSUPPORTED 2  /* shape outside the compiled kernels (see each entry) */
 #define COW_ERR_CUDA 3         /* a CUDA runtime call or launch failed */
-#define COW_ERR_DEVICE 4       /* a *_checked call found status bits set */
+#define COW_ERR_DEVICE 4       /* cow_decode_step_checked found status bits set */
 
 /* ---- element / index type codes -------------------------------------- */
 #define COW_F32 0
@@ -93,9 +93,14 @@ typedef struct cow_step {
 } cow_step;
 
 /* Library / ABI version and the bytes of decode scan scratch a launch of
- * `layers` pools with `total_banks` banks needs (zero-filled before first use,
- * reused across launches on one stream; calls that overlap on the GPU must
- * use distinct scratch). */
+ * `layers` pools with `total_banks` banks needs.  The scratch is zero-filled
+ * before first use and can then be reused by any sequence of launches on one
+ * stream, whatever their pool layouts: every launch tags its scan flags with
+ * one launch epoch and advances it once all its pools are closed, so flags
+ * left by an earlier launch never read as published.  (The 32-bit epoch
+ * repeats after 2^32 launches on one buffer; a flag would have to survive
+ * untouched for that long to be misread.)  Calls that overlap on the GPU must
+ * use distinct scratch. */
 int cow_abi_version(void);
 /* Text of the last CUDA error an entry point of this thread returned
  * COW_ERR_CUDA for ("no error" if none). */
@@ -129,14 +134,28 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
  *   (cudaGetSymbolAddress, with the caller's current device); make that first
  *   call before any stream capture.  `stream` must belong to the current device.
  * - Every call on a device shares the one array and keeps what the last call
- *   left there; the kernel returns it to a ready state at the end of each
- *   launch.  Calls that overlap on the GPU (e.g. on two streams) race on it.
+ *   left there.  Any sequence of calls that do not overlap may use it,
+ *   whatever their pool layouts (the launch epoch described at
+ *   cow_decode_scratch_bytes).  Calls that overlap on the GPU (e.g. on two streams)
+ *   race on it.
+ * - The resolved address is cached per device for the life of the process:
+ *   do not keep using the library across a cudaDeviceReset.
  * Calls no cudaMalloc, cudaFree or other allocating routine. */
 #define COW_ERR_SCRATCH_LIMIT 5
 #define COW_NOALLOC_SCRATCH_BYTES (1 << 20)
 int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers,
                             int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
                             void* stream);
+
+/* cow_decode_step followed by a synchronisation of `stream` and a read of
+ * every pool's status word: the reference's unproven / diagnostic path
+ * (allocator.py:1263-1319, whose _device_assert raises on overflow and bad
+ * indices).  Returns COW_ERR_DEVICE when any pool's status has bits set
+ * (the pools' statuses are OR-ed into *status_out when it is not NULL),
+ * COW_OK otherwise.  Blocks the calling thread; not for stream capture. */
+int cow_decode_step_checked(const cow_pool* pools, const cow_step* steps, int32_t layers,
+                            int32_t writes, int32_t reads, int32_t index_dtype, int32_t act_dtype,
+                            void* scan_scratch, int64_t scratch_bytes, void* stream, int32_t* status_out);
 
 /* Host-to-host decode step on `stream`: one cudaMemcpyAsync of `input_bytes`
  * from pinned `host_inputs` to `device_inputs` (the buffer the step
