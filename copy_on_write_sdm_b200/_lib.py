@@ -112,6 +112,7 @@ _SIGNATURES = {
     "cow_decode_step_host": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32, c_int32,
                                        c_int32, P, c_int64, P, P, c_int64, P, P, c_int64, P]),
     "cow_decode_step_host_piped": (c_int32, [P, P, P]),
+    "cow_decode_step_host_mapped": (c_int32, [P, P, P, P]),
     "cow_decode_step_host_overlapped": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                                   c_int32, c_int32, P, c_int64, P, P, c_int64, P, P, c_int64,
                                                   P, P, P, P, P, P]),

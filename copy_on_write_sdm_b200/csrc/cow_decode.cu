@@ -724,6 +724,61 @@ int cow_decode_step_host_piped(const cow_host_pipeline* p, const void* host_inpu
                                          p->computed, p->d2h_done);
 }
 
+int cow_decode_step_host_mapped(const cow_host_pipeline* p, const void* host_inputs, void* host_outputs,
+                                void* stream) {
+  if (!p || !host_inputs || !host_outputs || !p->steps || !p->device_inputs || !p->device_outputs ||
+      p->layers < 1 || p->layers > COW_MAX_LAYERS)
+    return COW_ERR_INVALID;
+  // Both host buffers must be page-locked and mapped for the device: the
+  // kernel dereferences them.  Pageable memory is refused before any launch.
+  void* mapped[2] = {nullptr, nullptr};
+  const void* host[2] = {host_inputs, host_outputs};
+  for (int i = 0; i < 2; ++i) {
+    cudaPointerAttributes a{};
+    const cudaError_t e = cudaPointerGetAttributes(&a, host[i]);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return COW_ERR_INVALID;
+    }
+    if (a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) return COW_ERR_INVALID;
+    mapped[i] = a.devicePointer;  // the device's address of the same bytes
+  }
+  // The step descriptors point into the device buffers; the same offsets into
+  // the caller's pinned host buffers give the kernel's inputs and outputs.
+  const char* in0 = static_cast<const char*>(p->device_inputs);
+  const char* out0 = static_cast<const char*>(p->device_outputs);
+  const char* hin = static_cast<const char*>(mapped[0]);
+  char* hout = static_cast<char*>(mapped[1]);
+  auto rebase_in = [&](const void* q) -> const void* {
+    return q == nullptr ? nullptr : hin + (static_cast<const char*>(q) - in0);
+  };
+  cow_step steps[COW_MAX_LAYERS];
+  for (int l = 0; l < p->layers; ++l) {
+    const cow_step& s = p->steps[l];
+    steps[l].write_indices = rebase_in(s.write_indices);
+    steps[l].write_weights = rebase_in(s.write_weights);
+    steps[l].values = rebase_in(s.values);
+    steps[l].input_gate = rebase_in(s.input_gate);
+    steps[l].erase_gate = rebase_in(s.erase_gate);
+    steps[l].forget_log_gate = rebase_in(s.forget_log_gate);
+    steps[l].read_indices = rebase_in(s.read_indices);
+    steps[l].read_weights = rebase_in(s.read_weights);
+    steps[l].output = hout + (static_cast<const char*>(s.output) - out0);
+    steps[l].first_touch = nullptr;
+  }
+  const int rc = cow_decode_step(p->pools, steps, p->layers, p->writes, p->reads, p->index_dtype, p->act_dtype,
+                                 p->scan_scratch, p->scratch_bytes, stream);
+  if (rc != COW_OK) return rc;
+  if (p->d2h_done) {
+    const cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(p->d2h_done), as_stream(stream));
+    if (e != cudaSuccess) {
+      cowrt::last_cuda_error = static_cast<int>(e);
+      return COW_ERR_CUDA;
+    }
+  }
+  return COW_OK;
+}
+
 int cow_decode_step_noalloc(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
                             int32_t reads, int32_t index_dtype, int32_t act_dtype, void* stream) {
   if (!pools || !steps || layers < 1 || layers > COW_MAX_LAYERS) return COW_ERR_INVALID;

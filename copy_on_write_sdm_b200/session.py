@@ -295,6 +295,38 @@ class DecodeSession:
         return pipe["host_outputs"][b], pipe["events"][b][2]
 
     @torch.no_grad()
+    def step_host_mapped(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
+        """Host-to-host step with no copy calls (``cow_decode_step_host_mapped``).
+
+        The decode kernel reads ``host_step`` (pinned bytes in the ``inputs``
+        layout) over PCIe and writes the readouts straight into a pinned host
+        buffer: one kernel launch per token.  Returns that buffer ``[L, B, D]``
+        and the event that marks the readouts' arrival; the buffer is reused
+        two steps later, and ``host_step`` must stay untouched until the event
+        has completed.  Steps decode in call order on the current stream.
+        """
+        if host_step.numel() != self.step_bytes or host_step.dtype != torch.uint8 \
+                or host_step.device.type != "cpu" or not host_step.is_contiguous():
+            raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
+        ptr = host_step.data_ptr()
+        pipe = self._pipe if self._pipe is not None else self._pipeline()
+        b = pipe["k"] & 1
+        pipe["k"] += 1
+        self._prove()
+        pools = self._pools()
+        if pipe["desc_pools"] is not pools:
+            for d in pipe["descs"]:
+                d.pools = ctypes.cast(pools, ctypes.POINTER(_lib.CowPool))
+            pipe["desc_pools"] = pools
+        out = pipe["host_outputs"][b]
+        rc = self._lib.cow_decode_step_host_mapped(pipe["desc_ptrs"][b], ptr, out.data_ptr(), self._stream_handle())
+        if rc:
+            if rc == _lib.ERR_INVALID:
+                raise ValueError("mapped host steps must live in pinned (page-locked) host memory")
+            _lib.check(rc, "cow_decode_step_host_mapped")
+        return out, pipe["events"][b][2]
+
+    @torch.no_grad()
     def step_host(self, host_step: torch.Tensor | None = None) -> torch.Tensor:
         """Host-to-host step: copy ``host_step`` (pinned bytes in the ``inputs`` layout,
         default ``host_inputs``) to the device, decode, copy the readouts back into

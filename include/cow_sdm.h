@@ -211,6 +211,19 @@ typedef struct cow_host_pipeline {
  * step instead of twenty-one. */
 int cow_decode_step_host_piped(const cow_host_pipeline* pipe, const void* host_inputs, void* compute_stream);
 
+/* Host-to-host decode step with no copy calls: the fused decode kernel reads
+ * the step's inputs straight from `host_inputs` and writes the readouts
+ * straight into `host_outputs` (zero-copy access to page-locked host memory
+ * over PCIe; both buffers must be pinned with cudaHostAlloc / cudaHostRegister
+ * and laid out like `pipe`'s device buffers: every step pointer of `pipe`
+ * is rebased from device_inputs / device_outputs onto them).  One kernel
+ * launch per token and no runtime copy calls; when `pipe->d2h_done` is not
+ * NULL it is recorded on `stream` after the launch and marks the readouts'
+ * arrival.  Decode steps stay in call order on `stream`.  The caller must not
+ * touch `host_inputs` / `host_outputs` until that event has completed. */
+int cow_decode_step_host_mapped(const cow_host_pipeline* pipe, const void* host_inputs, void* host_outputs,
+                                void* stream);
+
 /* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
  * allocator.py:368-460): the same math on dense [banks,slots,width] tables.
  * memories[l] has dtype mem_dtype; same limits as cow_decode_step. */

@@ -134,3 +134,51 @@ def test_pipelined_host_steps_match_sequential(dev):
         assert fp == int(q.free_count) and torch.equal(p.free_rows[:fp], q.free_rows[:fp])
         assert p.growth_events == q.growth_events > 0
         q.validate_invariants()
+
+
+def test_mapped_host_steps_match_sequential(dev):
+    """step_host_mapped: the decode kernel reads the pinned host step and writes
+    the readouts to pinned host memory itself.  Readouts, maps, stacks and
+    growth must equal the sequential step_host run; pageable memory is refused
+    before anything launches."""
+    from copy_on_write_sdm_b200 import DecodeSession
+
+    layers, banks, slots, width, W, R = 3, 40, 256, 128, 4, 16
+    quantum = O.growth_quantum_rows(banks, W, 3)
+    seq = DecodeSession(_pools(dev, layers, banks, slots, width, quantum, 5), writes=W, reads=R)
+    mapped = DecodeSession(_pools(dev, layers, banks, slots, width, quantum, 5), writes=W, reads=R)
+    rng = np.random.default_rng(6)
+    steps = 12
+    host = torch.empty(steps, seq.step_bytes, dtype=torch.uint8, pin_memory=True)
+    for i in range(steps):
+        xs = [O.synthetic_step_inputs(rng, banks, slots, width, W, R) for _ in range(layers)]
+        for l, x in enumerate(xs):
+            for k, v in x.items():
+                seq.host_views[l][k].copy_(torch.from_numpy(v))
+        host[i].copy_(seq.host_inputs)
+    want = []
+    for i in range(steps):
+        seq.step_host(host[i])
+        torch.cuda.synchronize(dev)
+        want.append(seq.host_outputs.clone())
+    got, pending = [], []
+    for i in range(steps):
+        pending.append(mapped.step_host_mapped(host[i]))
+        if len(pending) == 2:
+            o, e = pending.pop(0)
+            e.synchronize()
+            got.append(o.clone())
+    for o, e in pending:
+        e.synchronize()
+        got.append(o.clone())
+    for a, b in zip(want, got):
+        assert torch.equal(a, b)
+    for p, q in zip(seq.pools, mapped.pools):
+        assert torch.equal(p.logical_to_physical, q.logical_to_physical)
+        fp = int(p.free_count)
+        assert fp == int(q.free_count) and torch.equal(p.free_rows[:fp], q.free_rows[:fp])
+        assert p.growth_events == q.growth_events > 0
+        q.validate_invariants()
+    pageable = torch.empty(seq.step_bytes, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="pinned"):
+        mapped.step_host_mapped(pageable)
