@@ -304,7 +304,7 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     # back (no host in the loop; the pool state stays L2-resident).  The
     # routes are re-applied to the evolved state; with every slot of every
     # bank already private nothing is allocated.
-    warm = dense_warm = dense_ms = incremental = None
+    warm = dense_warm = dense_ms = incremental = eager = None
     if rank == 0:
         def trace_graph(launch):
             g = torch.cuda.CUDAGraph()
@@ -357,12 +357,32 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
                             launch(s)
             return g
 
+        # The same flushed steps launched eagerly, each between its own event
+        # pair on the launching stream (the 256 MiB flush before each step
+        # keeps the host's submissions ahead of the device, so no host gap
+        # falls inside an interval).
+        def eager_flushed(launch):
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+            with torch.cuda.stream(stream):
+                for i, s in enumerate(range(Wm, Wm + K)):
+                    flush.fill_(float(i))
+                    evs[i][0].record(stream)
+                    launch(s)
+                    evs[i][1].record(stream)
+            torch.cuda.synchronize(device)
+            return 1e3 * sum(a.elapsed_time(b) for a, b in evs) / K
+
+        eager = None
+        if extras:
+            eager = {"packed_us": eager_flushed(packed_launch), "dense_us": eager_flushed(dense_launch)}
         base = time_graph(flushed_only(None))
         # The incremental graphs re-apply the K steps twice more to the evolved
         # pools: prove capacity for them (pools whose slots are all private pop nothing).
         for st in states:
             st.prepare_step_capacity(banks * WRITES * 2 * K)
-        incremental = {"packed_us": 1e3 * (time_graph(flushed_only(packed_launch)) - base) / K,
+        tiny = torch.zeros(1, device=device)
+        incremental = {"empty_kernel_us": 1e3 * (time_graph(flushed_only(lambda s: tiny.add_(1.0))) - base) / K,
+                       "packed_us": 1e3 * (time_graph(flushed_only(packed_launch)) - base) / K,
                        "dense_us": 1e3 * (time_graph(flushed_only(dense_launch)) - base) / K}
         del mems
 
@@ -385,6 +405,7 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
                 v.copy_(inputs[k][s, l])
         host_steps[i].copy_(sess.inputs)
     torch.cuda.synchronize(device)
+    sess.register_host_steps(host_steps)
     h2d = sess.step_bytes
     d2h = sess.host_outputs.numel() * sess.host_outputs.element_size()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -427,17 +448,50 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     torch.cuda.synchronize(device)
     with torch.cuda.stream(stream):
         e0.record(stream)
+        t0 = time.perf_counter()
         for i in range(K):
             sess.step_host_mapped(host_steps[i])
+        host_s = time.perf_counter() - t0
         e1.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_mapped_ms = e0.elapsed_time(e1)
+    # Device time of the same zero-copy launches with no host in the loop (one
+    # CUDA graph of K mapped steps): separates PCIe / kernel time from host time.
+    for st in states:  # prove the two replays below up front (the graph bakes the pool tensors in)
+        st.prepare_step_capacity(banks * WRITES * 2 * K)
+    with torch.cuda.stream(stream):
+        sess.step_host_mapped(host_steps[0])  # refreshes the descriptors' pool array
+    torch.cuda.synchronize(device)
+    pipe = sess._pipeline()
+    gdescs = []
+    for d in pipe["descs"]:  # the same descriptors without the arrival event (nothing to record in a graph)
+        g = _lib.CowHostPipeline()
+        ctypes.memmove(ctypes.addressof(g), ctypes.addressof(d), ctypes.sizeof(g))
+        g.d2h_done = None
+        gdescs.append(g)
+    mapped_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(mapped_graph, stream=stream):
+            for i in range(K):
+                b = i & 1
+                _lib.check(lib.cow_decode_step_host_mapped(ctypes.addressof(gdescs[b]), host_steps[i].data_ptr(),
+                                                           pipe["host_outputs"][b].data_ptr(), stream.cuda_stream),
+                           "cow_decode_step_host_mapped")
+        mapped_graph.replay()
+        torch.cuda.synchronize(device)
+        e0.record(stream)
+        mapped_graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    mapped_device = {"us_per_step": 1e3 * e0.elapsed_time(e1) / K, "host_us_per_step": 1e6 * host_s / K,
+                     "note": "us_per_step: K mapped launches replayed as one CUDA graph (no host in the loop); "
+                             "host_us_per_step: host time of the step_host_mapped calls in the e2e loop"}
 
     state_bytes = _sum_state_bytes(states)
     used = [st.used_bytes() for st in states]
     return dict(total_ms=total_ms, step_ms=step_ms, single_ms=single_ms, e2e_ms=e2e_ms, e2e_serial_ms=e2e_serial_ms,
-                e2e_mapped_ms=e2e_mapped_ms,
+                e2e_mapped_ms=e2e_mapped_ms, mapped_device=mapped_device, eager=eager,
                 warm_ms=warm, incremental=incremental,
                 dense_ms=dense_ms,
                 dense_warm_ms=dense_warm,
@@ -525,14 +579,16 @@ def run_gpu_scaleout(args, rank, world, device):
     K, Wm = args.steps, args.warmup
     gen = torch.Generator(device=device).manual_seed(4000 + rank)
     t0 = time.time()
+    hashed_leg = getattr(args, "hash_leg", False)
+    total_steps = K + Wm + (K if hashed_leg else 0)
     states, zipfs, touched = [], [], []
     for _ in range(LAYERS):
-        st, z, a = scaleout_pool(gen, requests, args.prefix, banks * WRITES * (K + Wm), device)
+        st, z, a = scaleout_pool(gen, requests, args.prefix, banks * WRITES * total_steps, device)
         states.append(st)
         zipfs.append(z)
         touched.append(a)
     steps = []
-    for s in range(K + Wm):
+    for s in range(total_steps):
         per = []
         for l in range(LAYERS):
             z = zipfs[l]
@@ -555,7 +611,8 @@ def run_gpu_scaleout(args, rank, world, device):
                             x["input_gate"].data_ptr(), x["input_gate"].data_ptr(), x["forget_log_gate"].data_ptr(),
                             x["read_indices"].data_ptr(), x["read_weights"].data_ptr(), out.data_ptr(), None)
 
-    c_steps = [(_lib.CowStep * LAYERS)(*[cstep(steps[s][l], outputs[l]) for l in range(LAYERS)]) for s in range(K + Wm)]
+    c_steps = [(_lib.CowStep * LAYERS)(*[cstep(steps[s][l], outputs[l]) for l in range(LAYERS)])
+               for s in range(total_steps)]
     stream = torch.cuda.Stream(device)
 
     def launch(s):
@@ -582,14 +639,35 @@ def run_gpu_scaleout(args, rank, world, device):
             torch.distributed.barrier()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     first = free_before - sum(int(st.free_count) for st in states)
+    state_bytes = _sum_state_bytes(states)
+    hashed = None
+    if hashed_leg:
+        # The same pools on hashed maps (tables sized for every bank's private
+        # slots plus the remaining steps' first touches), timed on the next K
+        # steps of the trace.
+        for st in states:
+            st.use_hash_map(headroom_rows_per_bank=WRITES * K)
+        torch.cuda.empty_cache()
+        pools = (_lib.CowPool * LAYERS)(*[st._pool() for st in states])
+        free_h = sum(int(st.free_count) for st in states)
+        evh = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        torch.cuda.synchronize(device)
+        with torch.cuda.stream(stream):
+            for i in range(K):
+                evh[i][0].record(stream)
+                launch(Wm + K + i)
+                evh[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        hms = [a.elapsed_time(b) for a, b in evh]
+        hashed = {"total_ms": sum(hms), "first_touches": free_h - sum(int(st.free_count) for st in states),
+                  "table_slots": [st.map_table_slots for st in states],
+                  "map_bytes": sum(st.storage_bytes()["logical_to_physical"] for st in states),
+                  "dense_map_bytes": state_bytes["logical_to_physical"],
+                  "status": sum(st.status() for st in states)}
     for st in states:
         st.validate_invariants()
-    state_bytes = {}
-    for st in states:
-        for k, v in st.storage_bytes().items():
-            state_bytes[k] = state_bytes.get(k, 0) + v
     return dict(total_ms=sum(step_ms), step_ms=step_ms, first_touches=first, clocks=clocks.summary(),
-                setup_s=setup_s, state_bytes=state_bytes, requests=requests, banks=banks,
+                setup_s=setup_s, state_bytes=state_bytes, requests=requests, banks=banks, hashed=hashed,
                 mean_touched_rows_per_bank=sum(touched) / (LAYERS * banks))
 
 
@@ -1139,12 +1217,14 @@ def sub_legs(args, rank, world, device, res, total_ms) -> dict:
     so_args = argparse.Namespace(**vars(args))
     so_args.steps, so_args.warmup = min(args.steps, 32), min(args.warmup, 4)
     so_args.requests, so_args.prefix = SO_REQUESTS, SO_PREFIX
+    so_args.hash_leg = True
     so = scaleout_line(so_args, rank, world, device, cpu_seconds=min(args.cpu_seconds, 5.0))
     torch.cuda.empty_cache()
     if so is not None:
-        legs["scaleout"] = {k: so[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling", "roofline",
+        legs["scaleout"] = {k: so.get(k) for k in ("value", "unit", "ms_per_step", "steps", "scaling", "roofline",
                                                 "cpu_baseline", "retained_state", "first_touches_in_timed_steps",
-                                                "mean_touched_rows_per_bank", "clocks", "config", "setup_s")}
+                                                "mean_touched_rows_per_bank", "clocks", "config", "setup_s",
+                                                "hashed_map")}
     return legs
 
 
@@ -1160,6 +1240,7 @@ def main() -> int:
                          "scaleout: configuration 4; churn: configuration 5")
     ap.add_argument("--requests", type=int, default=SO_REQUESTS, help="scaleout: requests over all GPUs")
     ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
+    ap.add_argument("--hash-leg", action="store_true", help="scaleout: also time the pools on hashed maps")
     ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
     ap.add_argument("--trim-every", type=int, default=0, help="churn: trim the pools every this many steps")
     ap.add_argument("--no-legs", dest="legs", action="store_false",
@@ -1238,6 +1319,7 @@ def main() -> int:
                 "path": "DecodeSession.step_host_mapped: per step the capacity proof and one fused launch whose "
                         "kernel reads the step's pinned host bytes over PCIe and writes the readouts to pinned "
                         "host memory (zero-copy; the h2d/d2h bytes cross PCIe every step)",
+                "mapped_breakdown": res["mapped_device"],
                 "pipelined": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                               "path": "DecodeSession.step_host_pipelined: one pinned H2D copy, capacity proof + "
                                       "one fused launch, one D2H copy; copies of neighbouring steps overlap"},
@@ -1248,6 +1330,7 @@ def main() -> int:
             **res["incremental"],
             "packed_latency_overhead_pct": 100.0 * (res["incremental"]["packed_us"] / res["incremental"]["dense_us"] - 1.0),
             "note": "cold step's added device time in a graph of K x (L2 flush, step) minus K x flush"},
+        "eager_flushed": res["eager"],
         "single_launch": {"value": BATCH / (res["single_ms"] / 1e3), "unit": "tokens/s",
                           "ms_per_step": res["single_ms"],
                           "note": "one step per graph launch, timed alone (median); includes host submission"},
@@ -1292,7 +1375,7 @@ def scaleout_line(args, rank, world, device, *, cpu_seconds) -> dict | None:
     per_launch = algorithmic_bytes(res["banks"] * LAYERS, res["first_touches"] // max(K, 1))
     mean_s = res["total_ms"] / K / 1e3
     achieved = per_launch / mean_s / 1e9
-    return {
+    line = {
         "metric": METRIC, "value": tokens / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -1315,6 +1398,19 @@ def scaleout_line(args, rank, world, device, *, cpu_seconds) -> dict | None:
         "retained_state": {"all_gpus": state_bytes, "rank0": res["state_bytes"]},
         "setup_s": res["setup_s"],
     }
+    h = res.get("hashed")
+    if h is not None:
+        hb = algorithmic_bytes(res["banks"] * LAYERS, h["first_touches"] // max(K, 1))
+        hs = h["total_ms"] / K / 1e3
+        line["hashed_map"] = {
+            "value": res["requests"] * K / (h["total_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": h["total_ms"] / K,
+            "roofline": {"achieved": hb / hs / 1e9, "peak": peak, "frac": hb / hs / 1e9 / peak, "unit": "GB/s",
+                         "note": "algorithmic bytes as for the dense map (map lookups counted at 4 B)"},
+            "map_bytes_rank0": h["map_bytes"], "dense_map_bytes_rank0": h["dense_map_bytes"],
+            "table_slots_per_bank": h["table_slots"], "first_touches_in_timed_steps": h["first_touches"],
+            "status": h["status"],
+            "note": "rank 0: the same pools converted to per-bank hashed tables, next K steps of the same trace"}
+    return line
 
 
 def main_scaleout(args, rank, world, device) -> int:

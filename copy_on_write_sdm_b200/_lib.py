@@ -33,6 +33,8 @@ ST_MULTI_OWNER = 0x100
 ST_FREE_DUPLICATE = 0x200
 ST_NOT_COVERED = 0x400
 ST_ROW_RANGE = 0x800
+ST_MAP_FULL = 0x1000
+MAP_DENSE, MAP_HASH = 0, 1
 MAX_LAYERS, MAX_WRITES, MAX_READS, MAX_WIDTH = 8, 32, 256, 512
 
 _DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
@@ -54,7 +56,9 @@ class CowPool(ctypes.Structure):
         ("capacity", c_int64),
         ("template_count", c_int64),
         ("slab_dtype", c_int32),
-        ("_pad", c_int32),
+        ("map_kind", c_int32),
+        ("table_slots", c_int64),
+        ("free_mirror", c_void_p),
     ]
 
 
@@ -113,6 +117,11 @@ _SIGNATURES = {
                                        c_int32, P, c_int64, P, P, c_int64, P, P, c_int64, P]),
     "cow_decode_step_host_piped": (c_int32, [P, P, P]),
     "cow_decode_step_host_mapped": (c_int32, [P, P, P, P]),
+    "cow_register_host_range": (c_int32, [P, c_int64]),
+    "cow_hash_from_dense": (c_int32, [P, c_int64, c_int64, P, c_int64, P, P]),
+    "cow_hash_to_dense": (c_int32, [P, c_int64, c_int64, P, c_int64, P, P]),
+    "cow_hash_max_live": (c_int32, [P, c_int64, c_int64, P, P]),
+    "cow_unregister_host_range": (c_int32, [P]),
     "cow_decode_step_host_overlapped": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int32, c_int32,
                                                   c_int32, c_int32, P, c_int64, P, P, c_int64, P, P, c_int64,
                                                   P, P, P, P, P, P]),
@@ -241,6 +250,7 @@ _STATUS_TEXT = [
     (ST_DISCARD_LIVE, "discarded SDM banks must be released before compaction"),
     (ST_MULTI_OWNER, "one physical SDM row has multiple logical owners"),
     (ST_FREE_DUPLICATE, "free SDM row stack contains duplicates"),
+    (ST_MAP_FULL, "a hashed SDM map table has no room for a first touch"),
     (ST_NOT_COVERED, "active and free SDM rows do not partition the slab"),
     (ST_ROW_RANGE, "active and free SDM rows do not partition the slab"),
 ]

@@ -23,6 +23,7 @@ reference's deterministic CPU order, so maps and free stacks are bit-exact.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass, field
 from typing import Any, Sequence
@@ -95,10 +96,47 @@ def _scan_scratch(device: torch.device, n: int) -> torch.Tensor:
     return torch.zeros(blocks + 8, dtype=torch.int32, device=device)
 
 
+@contextlib.contextmanager
+def dense_maps(states: Sequence[PackedSDMCopyOnWriteState]):
+    """Lifecycle operations work on the dense map: hashed pools among ``states``
+    are expanded for the duration and hashed again afterwards (tables of at
+    least their previous size, larger if a bank now holds more slots)."""
+    hashed = [(st, st.map_table_slots) for st in states if st.map_table_slots]
+    for st, _ in hashed:
+        st.use_dense_map()
+    try:
+        yield
+    finally:
+        for st, t in hashed:
+            live = int((st.logical_to_physical >= 0).sum(dim=1).max()) if st.banks else 0
+            st.use_hash_map(max(t, st._table_slots_for(live)))
+
+
+def _on_dense_maps(pick):
+    """Run a lifecycle operation with the hashed pools that ``pick(args)`` names
+    expanded to dense maps."""
+    def wrap(fn):
+        def inner(*args, **kwargs):
+            states = pick(*args, **kwargs)
+            if not any(st.map_table_slots for st in states):
+                return fn(*args, **kwargs)
+            with dense_maps(states):
+                return fn(*args, **kwargs)
+        inner.__name__, inner.__doc__, inner.__wrapped__ = fn.__name__, fn.__doc__, fn
+        return inner
+    return wrap
+
+
 # --------------------------------------------------------------------------
 # the state
 # --------------------------------------------------------------------------
 
+
+# Process-wide counters of pool assignments: [any field, tensor fields].  A
+# runtime that caches proofs or descriptors over a set of pools compares one
+# integer per step instead of one counter per pool (a change to any pool
+# anywhere invalidates its cache, which is conservative).
+POOL_EPOCHS = [0, 0]
 
 _TENSOR_FIELDS = frozenset({"shared_initial_memory", "template_indices", "values", "logical_to_physical",
                             "free_rows", "free_count", "overflow_flag", "_m0_f32"})
@@ -129,6 +167,11 @@ class PackedSDMCopyOnWriteState:
     growth_rows_added: int = 0
     growth_rows_copied: int = 0
     slab_rows_moved: int = 0
+    # Hashed logical map (not in the reference): when map_table_slots > 0,
+    # logical_to_physical holds [banks, map_table_slots] int64 open-addressing
+    # tables ((slot << 32) | row, -1 empty) and hashed_slots is N.
+    map_table_slots: int = 0
+    hashed_slots: int = 0
     _m0_f32: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
     def __setattr__(self, name: str, value) -> None:
@@ -137,8 +180,10 @@ class PackedSDMCopyOnWriteState:
         object.__setattr__(self, name, value)
         d = self.__dict__
         d["_mutations"] = d.get("_mutations", 0) + 1
+        POOL_EPOCHS[0] += 1
         if name in _TENSOR_FIELDS:
             d["_tensor_version"] = d.get("_tensor_version", 0) + 1
+            POOL_EPOCHS[1] += 1
             # a slab or stack replaced other than by growth releases the growth reserve
             store = d.get("_slab_store")
             if store is not None and name in ("values", "free_rows") \
@@ -423,8 +468,90 @@ class PackedSDMCopyOnWriteState:
             self.logical_to_physical.data_ptr(), self.free_rows.data_ptr(),
             self.free_count.data_ptr(), self.overflow_flag.data_ptr(),
             self.banks, self.slots, self.width, self.capacity_rows, m0.shape[0],
-            _lib.dtype_code(self.values.dtype), 0,
+            _lib.dtype_code(self.values.dtype), _lib.MAP_HASH if self.map_table_slots else _lib.MAP_DENSE,
+            self.map_table_slots,
         )
+
+    # ---------------- hashed logical map ----------------
+
+    # Tables are sized so that no bank's table is more than this full.
+    HASH_MAX_LOAD = 0.7
+
+    @staticmethod
+    def _table_slots_for(live: int) -> int:
+        need = max(2, -(-live * 10 // 7))  # live / HASH_MAX_LOAD, rounded up
+        return 1 << (need - 1).bit_length()
+
+    @torch.no_grad()
+    def use_hash_map(self, table_slots: int | None = None, *, headroom_rows_per_bank: int = 0) -> int:
+        """Replace the dense ``[banks, N]`` map by per-bank hashed tables (no
+        counterpart in the reference, whose README names a sparse map as future
+        work).  ``table_slots`` (a power of two) defaults to the smallest size
+        that keeps every bank at most 70 % full with ``headroom_rows_per_bank``
+        more rows.  Growth pools keep their tables within that load through
+        ``prepare_step_capacity``; fixed pools must declare the rows a bank may
+        still gain as headroom.  Decode reads the tables directly; lifecycle
+        operations expand them to the dense map for their duration.  Returns
+        the table size; synchronises once."""
+        if headroom_rows_per_bank < 0:
+            raise ValueError("hash map headroom cannot be negative")
+        if self.map_table_slots:
+            if table_slots is None or table_slots == self.map_table_slots:
+                return self.map_table_slots
+            self.use_dense_map()
+        lib = _lib.load()
+        mapping = self.logical_to_physical
+        live = int((mapping >= 0).sum(dim=1).max()) if self.banks else 0
+        t = table_slots if table_slots is not None else self._table_slots_for(live + headroom_rows_per_bank)
+        if t < 2 or t & (t - 1) or t <= live:
+            raise ValueError("hash map table size must be a power of two above the live slots of every bank")
+        tables = torch.empty(self.banks, t, dtype=torch.int64, device=mapping.device)
+        status = torch.zeros((), dtype=torch.int32, device=mapping.device)
+        _lib.check(lib.cow_hash_from_dense(mapping.data_ptr(), self.banks, self.slots, tables.data_ptr(), t,
+                                           status.data_ptr(), self._stream()), "cow_hash_from_dense")
+        if int(status):
+            raise RuntimeError(f"hash map build failed: {_lib.status_text(int(status))}")
+        slots = self.slots
+        self.hashed_slots = slots
+        self.logical_to_physical = tables
+        self.map_table_slots = t
+        self.__dict__["_hash_live"] = live  # largest live count of a bank at the last exact count
+        return t
+
+    @torch.no_grad()
+    def use_dense_map(self) -> None:
+        """Expand hashed tables back to the reference's dense ``[banks, N]`` int32 map."""
+        if not self.map_table_slots:
+            return
+        lib = _lib.load()
+        tables = self.logical_to_physical
+        mapping = torch.empty(self.banks, self.hashed_slots, dtype=torch.int32, device=tables.device)
+        status = torch.zeros((), dtype=torch.int32, device=tables.device)
+        _lib.check(lib.cow_hash_to_dense(tables.data_ptr(), self.banks, self.map_table_slots, mapping.data_ptr(),
+                                         self.hashed_slots, status.data_ptr(), self._stream()), "cow_hash_to_dense")
+        self.map_table_slots = 0
+        self.logical_to_physical = mapping
+        self.hashed_slots = 0
+        if int(status):
+            raise RuntimeError(f"hash map expansion failed: {_lib.status_text(int(status))}")
+
+    def hash_max_live(self) -> int:
+        """Largest number of private slots of any bank (hashed pools; synchronises)."""
+        out = torch.empty((), dtype=torch.int32, device=self.values.device)
+        self._call("cow_hash_max_live", self.logical_to_physical.data_ptr(), self.banks, self.map_table_slots,
+                   out.data_ptr(), self._stream())
+        return int(out)
+
+    def _hash_room(self, per_bank: int) -> int:
+        """Rows every bank may still gain within the load limit, after rehashing to
+        larger tables when fewer than ``per_bank`` remain (hashed pools)."""
+        limit = int(self.map_table_slots * self.HASH_MAX_LOAD)
+        live = self.hash_max_live()
+        if live + per_bank > limit:
+            self.use_hash_map(self._table_slots_for(live + max(per_bank, live // 2)))
+            limit = int(self.map_table_slots * self.HASH_MAX_LOAD)
+        self.__dict__["_hash_live"] = live
+        return limit - live
 
     @staticmethod
     def _call(name: str, *args) -> None:
@@ -502,12 +629,20 @@ class PackedSDMCopyOnWriteState:
             if free_rows < maximum_new_rows:
                 self.grow_capacity(self.capacity_rows + maximum_new_rows - free_rows)
                 free_rows = int(self.free_count.item())
+            if self.map_table_slots and self.banks:
+                # Hashed map: the proof also never covers more steps than the
+                # fullest bank's table absorbs (one step adds at most
+                # maximum_new_rows / banks rows to a bank).
+                per_bank = -(-maximum_new_rows // self.banks)
+                room = self._hash_room(per_bank)
+                free_rows = min(free_rows, room // max(per_bank, 1) * maximum_new_rows)
             self.proven_maximum_additional_allocations = free_rows
         self.proven_maximum_additional_allocations -= maximum_new_rows
         self.capacity_is_proven = True
         return self.capacity_rows
 
     @torch.no_grad()
+    @_on_dense_maps(lambda self, *_, **__: [self])
     def trim_capacity(self, *, headroom_rows: int = 0) -> int:
         """Repack live rows to ``0..A-1`` in ``nonzero()`` order (allocator.py:776-840)."""
 
@@ -607,7 +742,7 @@ class PackedSDMCopyOnWriteState:
 
     @property
     def slots(self) -> int:
-        return self.logical_to_physical.shape[1]
+        return self.hashed_slots if self.map_table_slots else self.logical_to_physical.shape[1]
 
     @property
     def width(self) -> int:
@@ -662,6 +797,7 @@ class PackedSDMCopyOnWriteState:
         }
 
     @torch.no_grad()
+    @_on_dense_maps(lambda self, *_, **__: [self])
     def materialize_dense(self) -> torch.Tensor:
         """Effective ``[banks,N,D]`` table for validation, never serving (allocator.py:1004-1017)."""
 
@@ -673,6 +809,7 @@ class PackedSDMCopyOnWriteState:
         return out
 
     @torch.no_grad()
+    @_on_dense_maps(lambda self, *_, **__: [self])
     def release(self, bank_indices: torch.Tensor) -> torch.Tensor:
         """Release whole banks; rows return to the stack at ``old_free + rank`` (allocator.py:1019-1068).
 
@@ -797,6 +934,7 @@ def _bank_list(bank_indices: torch.Tensor, device, what: str) -> torch.Tensor:
 
 
 @torch.no_grad()
+@_on_dense_maps(lambda states: list(states))
 def validate_layers(states: Sequence[PackedSDMCopyOnWriteState]) -> list[dict[str, Any]]:
     """``validate_invariants`` of several pools: one call per 8 pools, one host synchronisation."""
     if not states:
@@ -817,6 +955,7 @@ def validate_layers(states: Sequence[PackedSDMCopyOnWriteState]) -> list[dict[st
 
 
 @torch.no_grad()
+@_on_dense_maps(lambda states, *_: list(states))
 def release_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> int:
     """``release`` on several pools: one call per 8 pools, one host synchronisation
     for the total count."""
@@ -839,6 +978,7 @@ def release_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Se
 
 
 @torch.no_grad()
+@_on_dense_maps(lambda states, *_: list(states))
 def retain_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Sequence[torch.Tensor]) -> None:
     """``retain_banks`` on several pools: one call per 8 pools, one host
     synchronisation.  Nothing changes unless every pool's selection is valid."""
@@ -868,6 +1008,7 @@ def retain_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Seq
 
 
 @torch.no_grad()
+@_on_dense_maps(lambda states, others: [*states, *others])
 def append_layers(states: Sequence[PackedSDMCopyOnWriteState],
                   others: Sequence[PackedSDMCopyOnWriteState]) -> list[int]:
     """``append_banks_from`` on several pools: one host synchronisation (plus the

@@ -37,7 +37,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .allocator import PackedSDMCopyOnWriteState, validate_layers
+from .allocator import PackedSDMCopyOnWriteState, dense_maps, validate_layers
 from .inference import FaithfulSDMDecodeState, _banks_per_state
 
 MAGIC = b"COWSDMC1"
@@ -187,12 +187,13 @@ def export_requests(state: FaithfulSDMDecodeState, sequence_indices: Sequence[in
         raise ValueError("checkpointed request is invalid, duplicated, or inactive")
     heads = [state._heads(st, state.batch) for st in state.sdm_states]
     layers = []
-    for st, banks in zip(state.sdm_states, _banks_per_state(idx, heads)):
-        sub = st.logical_to_physical.index_select(0, banks).reshape(-1)
-        live = torch.nonzero(sub >= 0).reshape(-1)
-        rows = st.values.index_select(0, sub.index_select(0, live).to(torch.int64))
-        layers.append(LayerCheckpoint(live, rows, st.template_indices.index_select(0, banks), st.slots,
-                                      st.growth_quantum_rows))
+    with dense_maps(state.sdm_states):  # hashed pools export through their dense form
+        for st, banks in zip(state.sdm_states, _banks_per_state(idx, heads)):
+            sub = st.logical_to_physical.index_select(0, banks).reshape(-1)
+            live = torch.nonzero(sub >= 0).reshape(-1)
+            rows = st.values.index_select(0, sub.index_select(0, live).to(torch.int64))
+            layers.append(LayerCheckpoint(live, rows, st.template_indices.index_select(0, banks), st.slots,
+                                          st.growth_quantum_rows))
     ckpt = ServingCheckpoint(
         layout=state.layout, capacity=state.capacity, activation_dtype=state.activation_dtype,
         positions=state.current_positions().index_select(0, idx), sdm_layer_positions=state.sdm_layer_positions,

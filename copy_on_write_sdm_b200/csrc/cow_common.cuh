@@ -165,6 +165,47 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int li
   return false;
 }
 
+// --------------------------------------------------------------------------
+// hashed logical maps (cow_pool.map_kind == COW_MAP_HASH)
+// --------------------------------------------------------------------------
+//
+// A bank's private slots live in an open-addressing table of T = 2^log_t
+// 64-bit entries, (slot << 32) | physical row, all ones when empty, probed
+// linearly from a multiplicative hash of the slot.  Only one warp touches a
+// bank's table during a decode step, and entries are never deleted inside a
+// step, so a lookup stops at the first empty entry.
+constexpr unsigned long long kHashEmpty = ~0ull;
+
+__device__ __forceinline__ uint32_t hash_home(int slot, int log_t) {
+  return (static_cast<uint32_t>(slot) * 2654435761u) >> (32 - log_t);
+}
+
+// Physical row of `slot` in the bank's table, -1 when the slot is shared.
+__device__ __forceinline__ int hash_find(const unsigned long long* table, int log_t, int slot) {
+  const uint32_t mask = (1u << log_t) - 1u;
+  uint32_t i = hash_home(slot, log_t);
+  for (uint32_t n = 0; n <= mask; ++n) {
+    const unsigned long long e = table[i];
+    if (e == kHashEmpty) return -1;
+    if (static_cast<int>(e >> 32) == slot) return static_cast<int>(static_cast<uint32_t>(e));
+    i = (i + 1u) & mask;
+  }
+  return -1;
+}
+
+// Claim an empty entry for `slot` -> `phys`; false when the table is full.
+__device__ __forceinline__ bool hash_insert(unsigned long long* table, int log_t, int slot, int phys) {
+  const uint32_t mask = (1u << log_t) - 1u;
+  const unsigned long long entry =
+      (static_cast<unsigned long long>(static_cast<uint32_t>(slot)) << 32) | static_cast<uint32_t>(phys);
+  uint32_t i = hash_home(slot, log_t);
+  for (uint32_t n = 0; n <= mask; ++n) {
+    if (table[i] == kHashEmpty && atomicCAS(table + i, kHashEmpty, entry) == kHashEmpty) return true;
+    i = (i + 1u) & mask;
+  }
+  return false;
+}
+
 // Largest logical table whose map row a decode warp may stage in shared memory.
 constexpr int kStageSlots = 1024;
 
@@ -196,7 +237,17 @@ struct DecodeLayer {
   int64_t banks, slots, capacity, template_count, group_begin;
   int32_t tile_begin, tiles;
   int32_t count_block_begin, count_blocks;  // two-pass launches: blocks of cow_count_kernel
+  int32_t split_begin;                      // split launches: first block (= bank 0) of this pool
+  unsigned long long* free_mirror;          // optional host word: (launch epoch << 32) | free count
+  int32_t log_t;                            // hashed map: log2 entries per bank's table (0: dense map)
 };
+
+// Free count of a closed pool, mirrored to the pool's host word (if any).
+__device__ __forceinline__ void mirror_free(const DecodeLayer& L, uint32_t epoch, int free_rows) {
+  if (L.free_mirror != nullptr)
+    *reinterpret_cast<volatile unsigned long long*>(L.free_mirror) =
+        (static_cast<unsigned long long>(epoch) << 32) | static_cast<uint32_t>(free_rows);
+}
 
 struct DecodeLaunch {
   DecodeLayer layer[COW_MAX_LAYERS];
@@ -349,7 +400,10 @@ template <bool kDense, int RC, class M>
 __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int32_t* map,
                                             int64_t row, int64_t map_row, int64_t N, int W, int R,
                                             int idx64, int adt, int lane, unsigned& first_mask,
-                                            int& error_bits, int32_t* staged = nullptr) {
+                                            int& error_bits, int32_t* staged = nullptr, int log_t = 0) {
+  // Hashed maps: `map` points at the pool's [banks, 2^log_t] uint64 tables.
+  const unsigned long long* table =
+      log_t ? reinterpret_cast<const unsigned long long*>(map) + (map_row << log_t) : nullptr;
   // The first 256 map entries come through registers (their latency is the
   // route loads' latency), any further ones through cp.async.
   constexpr int kRegStage = 2;
@@ -396,7 +450,7 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
     mrow = staged;
   }
   int wp = -1;
-  if (!kDense && lane < W) wp = mrow[wi];
+  if (!kDense && lane < W) wp = log_t ? hash_find(table, log_t, wi) : mrow[wi];
   int ri[RC], rp[RC];
 #pragma unroll
   for (int c = 0; c < RC; ++c) {
@@ -406,7 +460,7 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
     rp[c] = -1;
     if (r < R) {
       bad |= !ok;
-      if (!kDense) rp[c] = mrow[ri[c]];
+      if (!kDense) rp[c] = log_t ? hash_find(table, log_t, ri[c]) : mrow[ri[c]];
     }
   }
   // Out-of-range lanes get a unique sentinel so they never count as repeats.
@@ -604,6 +658,13 @@ inline int width_chunks(int64_t width) {
 inline bool check_step_shape(int64_t width, int writes, int reads) {
   return width > 0 && width % 4 == 0 && width <= COW_MAX_WIDTH && writes >= 1 && writes <= COW_MAX_WRITES &&
          reads >= 1 && reads <= COW_MAX_READS;
+}
+
+// Entry points other than the decode step work on dense [banks, slots] maps.
+inline bool dense_maps(const cow_pool* p, int64_t n) {
+  for (int64_t i = 0; p != nullptr && i < n; ++i)
+    if (p[i].map_kind != COW_MAP_DENSE) return false;
+  return true;
 }
 
 inline bool check_step_ptrs(const cow_step& s, int adt) {

@@ -20,6 +20,7 @@
 // COW_ST_WAIT_TIMEOUT instead of hanging.
 
 
+#include <cstdlib>
 #include <mutex>
 
 #include "cow_common.cuh"
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   unsigned first_mask = 0;
   int route_bits = 0;
   const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
-                                                first_mask, route_bits, P.stage_map ? s_mapw : nullptr);
+                                                first_mask, route_bits, P.stage_map ? s_mapw : nullptr, L.log_t);
   const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
   const bool bad = bad_route || bad_tmpl;
   if (bad) {
@@ -175,10 +176,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   // for this warp's row loads) is needed.
   if (lane == 0 && P.counter_close && static_cast<int64_t>(arrived >> kCloseShift) == L.banks - 1) {
     const int total = static_cast<int>(arrived & ((1u << kCloseShift) - 1u)) + count;
-    if (total > 0) {
-      const int remaining = old_free - total;
-      *L.free_count = remaining > 0 ? remaining : 0;
-    }
+    const int remaining = old_free - total > 0 ? old_free - total : 0;
+    if (total > 0) *L.free_count = remaining;
+    mirror_free(L, epoch, remaining);
     hdr[0] = 0u;
     close_pool_epoch(P.header, P.active_pools, epoch);
   }
@@ -214,10 +214,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       if (bank == L.banks - 1) {
         // Every bank of this pool has published, hence has read the starting
         // epoch and free count: close the launch for this pool.
-        if (inclusive > 0) {
-          const int remaining = old_free - inclusive;
-          *L.free_count = remaining > 0 ? remaining : 0;
-        }
+        const int remaining = old_free - inclusive > 0 ? old_free - inclusive : 0;
+        if (inclusive > 0) *L.free_count = remaining;
+        mirror_free(L, epoch, remaining);
         if (P.dynamic_tiles) hdr[0] = 0u;
         close_pool_epoch(P.header, P.active_pools, epoch);
       }
@@ -274,7 +273,12 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     const int pos = old_free - 1 - rank;
     if (pos >= 0) {
       newp = L.free_rows[pos];
-      L.map[bank * N + sm.widx[lane]] = newp;
+      if (L.log_t == 0) {
+        L.map[bank * N + sm.widx[lane]] = newp;
+      } else if (!hash_insert(reinterpret_cast<unsigned long long*>(L.map) + (bank << L.log_t), L.log_t,
+                              sm.widx[lane], newp)) {
+        atomicOr(L.status, COW_ST_MAP_FULL);
+      }
     } else {
       atomicOr(L.status, COW_ST_SLAB_EXHAUSTED);
     }
@@ -292,6 +296,196 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
             if (col < D) Elem<SDT>::st4(L.slab, static_cast<int64_t>(p) * D + col, upd[w][c]);
           }
         }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// small launches: one bank per block, split over kSplit warps
+// --------------------------------------------------------------------------
+//
+// With a few hundred banks per launch each SM sub-partition holds about one
+// warp, and the step is bound by the serial instruction chain of that warp
+// (about a thousand dependent instructions for f32 rows, W <= 4, R <= 32,
+// width <= 128), not by memory.  This variant gives each bank a block of
+// kSplit warps.  Every warp resolves the bank's routes (identical metadata,
+// no barrier) and holds all W write rows (the gated-delta update needs all of
+// them for the retrieved vector); warp k stores write rows w == k (mod kSplit)
+// and reads rows r == k (mod kSplit), with every read row bulk-copied into
+// shared memory (rows read after a write this step are fed from registers
+// and copied from M0 with weight 0, so the accumulation has no branches).
+// The kSplit partial readouts meet in shared memory.  Warp 0 alone takes
+// part in the pool's scan and close and places the first touches, exactly as
+// cow_decode_kernel does (same flags, same epoch, same pop order).
+constexpr int kSplit = 4;
+constexpr int kSplitRows = 32 / kSplit;  // read rows per warp (R <= 32)
+
+__global__ void __launch_bounds__(kSplit * 32)
+    cow_decode_split_kernel(const __grid_constant__ DecodeLaunch P) {
+  __shared__ WarpMetaT<32> s_meta[kSplit];
+  __shared__ uint64_t s_bar[kSplit];
+  __shared__ __align__(16) float s_rows[kSplit][kSplitRows][128];
+  __shared__ __align__(16) float s_rw[kSplit][kSplitRows];
+  __shared__ __align__(16) float4 s_part[kSplit][32];
+  extern __shared__ __align__(16) unsigned char dyn_smem[];  // staged map rows, N ints per warp
+
+  const int k = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int D = P.width, W = P.writes, R = P.reads;
+  int l = 0;
+  while (l + 1 < P.layers && static_cast<int>(blockIdx.x) >= P.layer[l + 1].split_begin) ++l;
+  const DecodeLayer& L = P.layer[l];
+  uint32_t* hdr = P.header + l;
+  const int64_t bank = static_cast<int64_t>(blockIdx.x) - L.split_begin;
+  const int64_t N = L.slots;
+  auto& sm = s_meta[k];
+  int32_t* const s_mapw = reinterpret_cast<int32_t*>(dyn_smem) + static_cast<int64_t>(k) * N;
+  uint64_t* const flags = P.flags + static_cast<int64_t>(L.tile_begin) * kBanksPerCta;
+
+  uint32_t epoch = 0;
+  int old_free = 0;
+  if (k == 0 && lane == 0) {
+    epoch = *reinterpret_cast<volatile uint32_t*>(&P.header[kEpochWord]);
+    old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
+  }
+  const int64_t tmpl = L.templates[bank];
+  const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
+  const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
+  const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  float4 val[1];
+  val[0] = lane * 4 < D ? ld4_rt(L.step.values, bank * D + lane * 4, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  unsigned first_mask = 0;
+  int route_bits = 0;
+  const bool bad_route = load_routes<false, 1>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
+                                               first_mask, route_bits, s_mapw);
+  const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
+  const bool bad = bad_route || bad_tmpl;
+  if (bad) {
+    if (k == 0 && lane == 0) atomicOr(L.status, route_bits | (bad_tmpl ? COW_ST_TEMPLATE_RANGE : 0));
+    first_mask = 0;
+  }
+  const int count = __popc(first_mask);
+  uint32_t arrived = 0;
+  if (k == 0) {
+    epoch = __shfl_sync(kFull, epoch, 0);
+    old_free = __shfl_sync(kFull, old_free, 0);
+    if (lane == 0) {
+      *reinterpret_cast<volatile uint64_t*>(flags + bank) = pack_flag(epoch, kFlagAggregate, static_cast<uint32_t>(count));
+      arrived = atomicAdd(&hdr[0], (1u << kCloseShift) + static_cast<uint32_t>(count));
+    }
+  }
+
+  // This warp's read rows r = k + kSplit*j: one bulk copy per row (lane j),
+  // slab rows for private slots, M0 rows otherwise (weight 0 when the slot
+  // was written this step: its updated row is added from registers).
+  const int64_t m0_base = tmpl * N;
+  const int my_rows = R > k ? (R - k + kSplit - 1) / kSplit : 0;
+  float4 upd[4][1];
+  if (!bad) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (w < W) {
+        const int phys = sm.wphys[w];
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane * 4 < D) {
+          x = phys < 0 ? ld4_m0(L.m0, (m0_base + sm.widx[w]) * D + lane * 4)
+                       : Elem<COW_F32>::ld4(L.slab, static_cast<int64_t>(phys) * D + lane * 4);
+        }
+        upd[w][0] = x;
+      }
+    }
+    uint64_t* bar = &s_bar[k];
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      mbar_arrive_expect_tx(bar, static_cast<unsigned>(my_rows) * static_cast<unsigned>(D) * 4u);
+    }
+    __syncwarp();
+    if (lane < my_rows) {
+      const int r = k + kSplit * lane;
+      const int src = sm.rsrc[r];
+      s_rw[k][lane] = src >= -1 ? sm.rw[r] : 0.f;
+      const float* row = src >= 0 ? static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D
+                                  : L.m0 + (m0_base + sm.ridx[r]) * D;
+      bulk_row_copy(&s_rows[k][lane][0], row, static_cast<unsigned>(D) * 4u, bar);
+    }
+  }
+
+  int excl = 0;
+  if (k == 0) {
+    if (lane == 0 && static_cast<int64_t>(arrived >> kCloseShift) == L.banks - 1) {
+      const int total = static_cast<int>(arrived & ((1u << kCloseShift) - 1u)) + count;
+      const int remaining = old_free - total > 0 ? old_free - total : 0;
+      if (total > 0) *L.free_count = remaining;
+      mirror_free(L, epoch, remaining);
+      hdr[0] = 0u;
+      close_pool_epoch(P.header, P.active_pools, epoch);
+    }
+    if (count > 0 || bank % kScanGroup == kScanGroup - 1) {
+      bool timed_out = false;
+      excl = pool_prefix(flags, P.group_flags + L.group_begin, bank, count, epoch, lane, timed_out);
+      if (__any_sync(kFull, timed_out) && lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+    }
+  }
+
+  float4 acc[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
+  if (!bad) {
+    gated_delta<COW_F32, 1, 4>(upd, sm, W, expf(fl), in_g, er_g, val, lane, D);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (w < W && w % kSplit == k) acc[0] = f4_axpy(sm.fwt[w], upd[w][0], acc[0]);
+    }
+    if (my_rows > 0 && !mbar_wait(&s_bar[k], 0, kSpinLimit)) {
+      if (lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+      mbar_wait(&s_bar[k], 0, kSpinLimit);
+    }
+    if (lane * 4 < D) {
+      for (int j = 0; j < my_rows; ++j)
+        acc[0] = f4_axpy(s_rw[k][j], *reinterpret_cast<const float4*>(&s_rows[k][j][lane * 4]), acc[0]);
+    }
+  }
+  s_part[k][lane] = acc[0];
+  // Every warp has consumed its copies of the write rows (the update used
+  // them), so the private rows may now be overwritten in place.
+  __syncthreads();
+  if (!bad) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (w < W && w % kSplit == k) {
+        const int phys = sm.wphys[w];
+        if (phys >= 0 && lane * 4 < D) Elem<COW_F32>::st4(L.slab, static_cast<int64_t>(phys) * D + lane * 4, upd[w][0]);
+      }
+    }
+  }
+  if (k != 0) return;
+  float4 sum = s_part[0][lane];
+#pragma unroll
+  for (int j = 1; j < kSplit; ++j) {
+    const float4 x = s_part[j][lane];
+    sum = make_float4(sum.x + x.x, sum.y + x.y, sum.z + x.z, sum.w + x.w);
+  }
+  if (lane * 4 < D) st4_rt(L.step.output, bank * D + lane * 4, sum, P.act_dt);
+
+  // Place the first touches: pop free_rows[old_free - 1 - rank].
+  int newp = -1;
+  const bool first = lane < W && ((first_mask >> lane) & 1u);
+  if (first) {
+    const int rank = excl + __popc(first_mask & ((1u << lane) - 1u));
+    const int pos = old_free - 1 - rank;
+    if (pos >= 0) {
+      newp = L.free_rows[pos];
+      L.map[bank * N + sm.widx[lane]] = newp;
+    } else {
+      atomicOr(L.status, COW_ST_SLAB_EXHAUSTED);
+    }
+  }
+  if (L.step.first_touch != nullptr && lane < W) L.step.first_touch[bank * W + lane] = (first && newp >= 0) ? 1 : 0;
+  if (first_mask != 0u) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (w < W && ((first_mask >> w) & 1u)) {
+        const int p = __shfl_sync(kFull, newp, w);
+        if (p >= 0 && lane * 4 < D) Elem<COW_F32>::st4(L.slab, static_cast<int64_t>(p) * D + lane * 4, upd[w][0]);
       }
     }
   }
@@ -391,7 +585,16 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
       for (int w0 = 0; w0 < W; w0 += 8) {
         int32_t m[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) m[u] = w0 + u < W ? L.map[bank * N + wi[w0 + u]] : 0;
+        for (int u = 0; u < 8; ++u) {
+          if (w0 + u >= W) {
+            m[u] = 0;
+          } else if (L.log_t == 0) {
+            m[u] = L.map[bank * N + wi[w0 + u]];
+          } else {
+            m[u] = hash_find(reinterpret_cast<const unsigned long long*>(L.map) + (bank << L.log_t), L.log_t,
+                             wi[w0 + u]);
+          }
+        }
 #pragma unroll
         for (int u = 0; u < 8; ++u) count += m[u] < 0 ? 1 : 0;
       }
@@ -415,8 +618,9 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
     // epoch and free count: record it for the decode pass and close the pool.
     const int inclusive = s_base + total;
     excl[static_cast<int64_t>(P.total_tiles) * kBanksPerCta + l] = s_old;
-    const int remaining = s_old - inclusive;
-    *L.free_count = remaining > 0 ? remaining : 0;
+    const int remaining = s_old - inclusive > 0 ? s_old - inclusive : 0;
+    *L.free_count = remaining;
+    mirror_free(L, epoch, remaining);
     if (P.dynamic_tiles) hdr[0] = 0u;
     close_pool_epoch(P.header, P.active_pools, epoch);
   }
@@ -477,6 +681,20 @@ constexpr int64_t kStageMaxBanks = 148 * 16;
 // Launches with at least this many banks compute the first-touch prefix in a
 // separate pass (cow_count_kernel) before the decode pass.
 constexpr int64_t kTwoPassMinBanks = 12288;
+// Launches of at most this many banks (and a shape the split kernel covers)
+// run one bank per block of kSplit warps.
+constexpr int64_t kSplitMaxBanks = 2048;
+
+// COW_DECODE_SPLIT=0 in the environment turns the split kernel off (for
+// comparisons); read once per process.
+bool split_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("COW_DECODE_SPLIT");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
 
 
 }  // namespace
@@ -498,9 +716,16 @@ int64_t cow_decode_scratch_bytes(int64_t total_banks, int32_t layers) {
   return kScanHeaderBytes + 8 * (kBanksPerCta * tiles + total_banks / kScanGroup + pools);
 }
 
-int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
-                    int32_t index_dtype, int32_t act_dtype, void* scan_scratch, int64_t scratch_bytes,
-                    void* stream) {
+}  // extern "C"
+
+namespace {
+
+// cow_decode_step's launch logic.  `allow_split` is off when the step's inputs
+// live in host memory: the split kernel reads every bank's routes once per
+// warp, which costs four PCIe round trips where one suffices.
+int decode_step_impl(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
+                     int32_t index_dtype, int32_t act_dtype, void* scan_scratch, int64_t scratch_bytes, void* stream,
+                     bool allow_split) {
   if (!pools || !steps || layers < 1 || layers > COW_MAX_LAYERS || !scan_scratch) return COW_ERR_INVALID;
   if (!valid_dtype(act_dtype) || (index_dtype != COW_I32 && index_dtype != COW_I64)) return COW_ERR_INVALID;
   const int64_t width = pools[0].width;
@@ -530,6 +755,15 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
     L.slots = p.slots;
     L.capacity = p.capacity;
     L.template_count = p.template_count;
+    L.free_mirror = reinterpret_cast<unsigned long long*>(p.free_mirror);
+    L.log_t = 0;
+    if (p.map_kind == COW_MAP_HASH) {
+      const int64_t t = p.table_slots;
+      if (t < 2 || t > (int64_t(1) << 30) || (t & (t - 1)) != 0 || p.slots >= (int64_t(1) << 31)) return COW_ERR_INVALID;
+      while ((int64_t(1) << L.log_t) < t) ++L.log_t;
+    } else if (p.map_kind != COW_MAP_DENSE) {
+      return COW_ERR_INVALID;
+    }
     L.tile_begin = tiles;
     L.tiles = static_cast<int32_t>((p.banks + kBanksPerCta - 1) / kBanksPerCta);
     tiles += L.tiles;
@@ -562,7 +796,8 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
   bool stage = true;
   int64_t total_banks = 0;
   for (int l = 0; l < layers; ++l) {
-    stage = stage && pools[l].slots <= kStageSlots && pools[l].slots % 4 == 0 && aligned16(pools[l].map);
+    stage = stage && pools[l].map_kind == COW_MAP_DENSE && pools[l].slots <= kStageSlots && pools[l].slots % 4 == 0 &&
+            aligned16(pools[l].map);
     total_banks += pools[l].banks;
   }
   P.stage_map = stage && total_banks <= kStageMaxBanks ? 1 : 0;
@@ -614,9 +849,97 @@ int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers
       fits = fits && pools[l].banks < (int64_t(1) << (32 - kCloseShift)) &&
              pools[l].banks * writes < (int64_t(1) << kCloseShift);
     P.counter_close = fits ? 1 : 0;
+    if (fits && allow_split && split_enabled() && sdt == COW_F32 && ch == 1 && rv == 0 && P.stage_map && width <= 128 &&
+        total_banks <= kSplitMaxBanks) {
+      // Small launch: one bank per block of kSplit warps (cow_decode_split_kernel).
+      const size_t split_smem = static_cast<size_t>(kSplit) * max_slots * sizeof(int32_t);
+      const int split_resident = resident_blocks(reinterpret_cast<const void*>(cow_decode_split_kernel),
+                                                 kSplit * 32, split_smem);
+      if (static_cast<int64_t>(split_resident) >= total_banks) {
+        int32_t begin = 0;
+        for (int l = 0; l < layers; ++l) {
+          P.layer[l].split_begin = begin;
+          begin += static_cast<int32_t>(pools[l].banks);
+        }
+        cow_decode_split_kernel<<<static_cast<unsigned>(total_banks), kSplit * 32, split_smem, as_stream(stream)>>>(P);
+        return launch_status();
+      }
+    }
   }
   fn<<<tiles, kBanksPerCta * 32, smem, as_stream(stream)>>>(P);
   return launch_status();
+}
+
+// Page-locked host ranges registered for zero-copy steps: host address, bytes
+// and the device's address of the same bytes.
+struct HostRange {
+  const char* host;
+  int64_t bytes;
+  char* device;
+};
+constexpr int kMaxHostRanges = 64;
+std::mutex g_host_mutex;
+HostRange g_host_ranges[kMaxHostRanges];
+int g_host_count = 0;
+
+// Device address of [q, q + bytes) when it lies in page-locked host memory:
+// a registered range first (no runtime call), else cudaPointerGetAttributes.
+char* mapped_address(const void* q, int64_t bytes) {
+  const char* c = static_cast<const char*>(q);
+  {
+    std::lock_guard<std::mutex> lock(g_host_mutex);
+    for (int i = 0; i < g_host_count; ++i) {
+      const HostRange& r = g_host_ranges[i];
+      if (c >= r.host && c + bytes <= r.host + r.bytes) return r.device + (c - r.host);
+    }
+  }
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) return nullptr;
+  return static_cast<char*>(a.devicePointer);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cow_decode_step(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes, int32_t reads,
+                    int32_t index_dtype, int32_t act_dtype, void* scan_scratch, int64_t scratch_bytes,
+                    void* stream) {
+  return decode_step_impl(pools, steps, layers, writes, reads, index_dtype, act_dtype, scan_scratch, scratch_bytes,
+                          stream, true);
+}
+
+int cow_register_host_range(const void* host, int64_t bytes) {
+  if (!host || bytes <= 0) return COW_ERR_INVALID;
+  cudaPointerAttributes first{}, last{};
+  const char* c = static_cast<const char*>(host);
+  if (cudaPointerGetAttributes(&first, host) != cudaSuccess ||
+      cudaPointerGetAttributes(&last, c + bytes - 1) != cudaSuccess) {
+    cudaGetLastError();
+    return COW_ERR_INVALID;
+  }
+  if (first.type != cudaMemoryTypeHost || last.type != cudaMemoryTypeHost || !first.devicePointer ||
+      static_cast<char*>(last.devicePointer) - static_cast<char*>(first.devicePointer) != bytes - 1)
+    return COW_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_host_mutex);
+  if (g_host_count == kMaxHostRanges) return COW_ERR_UNSUPPORTED;
+  g_host_ranges[g_host_count++] = HostRange{c, bytes, static_cast<char*>(first.devicePointer)};
+  return COW_OK;
+}
+
+int cow_unregister_host_range(const void* host) {
+  std::lock_guard<std::mutex> lock(g_host_mutex);
+  for (int i = 0; i < g_host_count; ++i) {
+    if (g_host_ranges[i].host == host) {
+      g_host_ranges[i] = g_host_ranges[--g_host_count];
+      return COW_OK;
+    }
+  }
+  return COW_ERR_INVALID;
 }
 
 int cow_decode_step_checked(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
@@ -731,18 +1054,8 @@ int cow_decode_step_host_mapped(const cow_host_pipeline* p, const void* host_inp
     return COW_ERR_INVALID;
   // Both host buffers must be page-locked and mapped for the device: the
   // kernel dereferences them.  Pageable memory is refused before any launch.
-  void* mapped[2] = {nullptr, nullptr};
-  const void* host[2] = {host_inputs, host_outputs};
-  for (int i = 0; i < 2; ++i) {
-    cudaPointerAttributes a{};
-    const cudaError_t e = cudaPointerGetAttributes(&a, host[i]);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return COW_ERR_INVALID;
-    }
-    if (a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) return COW_ERR_INVALID;
-    mapped[i] = a.devicePointer;  // the device's address of the same bytes
-  }
+  char* mapped[2] = {mapped_address(host_inputs, p->input_bytes), mapped_address(host_outputs, p->output_bytes)};
+  if (!mapped[0] || !mapped[1]) return COW_ERR_INVALID;
   // The step descriptors point into the device buffers; the same offsets into
   // the caller's pinned host buffers give the kernel's inputs and outputs.
   const char* in0 = static_cast<const char*>(p->device_inputs);
@@ -766,8 +1079,8 @@ int cow_decode_step_host_mapped(const cow_host_pipeline* p, const void* host_inp
     steps[l].output = hout + (static_cast<const char*>(s.output) - out0);
     steps[l].first_touch = nullptr;
   }
-  const int rc = cow_decode_step(p->pools, steps, p->layers, p->writes, p->reads, p->index_dtype, p->act_dtype,
-                                 p->scan_scratch, p->scratch_bytes, stream);
+  const int rc = decode_step_impl(p->pools, steps, p->layers, p->writes, p->reads, p->index_dtype, p->act_dtype,
+                                  p->scan_scratch, p->scratch_bytes, stream, false);
   if (rc != COW_OK) return rc;
   if (p->d2h_done) {
     const cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(p->d2h_done), as_stream(stream));

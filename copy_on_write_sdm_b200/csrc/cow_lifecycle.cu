@@ -607,6 +607,7 @@ extern "C" {
 int64_t cow_scan_blocks(int64_t n) { return scan_blocks_of(n) + kScanHeader; }
 
 int cow_init_pool(const cow_pool* p, void* stream) {
+  if (!dense_maps(p, 1)) return COW_ERR_UNSUPPORTED;
   if (!p || !p->map || !p->free_rows || !p->free_count || !p->status || p->capacity < 0 || p->banks < 0)
     return COW_ERR_INVALID;
   const int64_t n = p->banks * p->slots;
@@ -651,6 +652,7 @@ int cow_pack_count(const int32_t* map, int64_t n, int32_t* flags_scratch, void* 
 
 int cow_pack_apply(int32_t* map, int64_t n, int32_t* src_index, const cow_pool* pool, int32_t* flags_scratch,
                    void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if ((!map && n > 0) || !pool || !flags_scratch || !src_index) return COW_ERR_INVALID;
   ScanLaunch L{};
   L.layers = 1;
@@ -725,6 +727,7 @@ int64_t cow_release_workspace_bytes(const cow_pool* pools, const int64_t* counts
 
 int cow_release_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts,
                        int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* released, void* stream) {
+  if (!dense_maps(pools, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(pools, layers) || !bank_indices || !counts || !released) return COW_ERR_INVALID;
   const int64_t need = cow_release_workspace_bytes(pools, counts, layers);
   if (!workspace_ok(workspace, workspace_bytes, need)) return COW_ERR_INVALID;
@@ -774,6 +777,7 @@ int cow_release_layers(const cow_pool* pools, const int64_t* const* bank_indices
 
 int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count, int32_t* bank_mask,
                 int32_t* flags_scratch, int32_t* released, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if (!pool || !bank_mask || !flags_scratch || !released || count < 0 || (count > 0 && !bank_indices))
     return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
@@ -814,6 +818,7 @@ int cow_release(const cow_pool* pool, const int64_t* bank_indices, int64_t count
 
 int cow_repack(const cow_pool* pool, int32_t* new_map, void* new_slab, int32_t* new_free_rows, int64_t new_capacity,
                int32_t* src_rows, int32_t* flags_scratch, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if (!pool || !new_map || !new_slab || !new_free_rows || !src_rows || !flags_scratch) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
   ScanLaunch C{};
@@ -839,6 +844,7 @@ int cow_repack(const cow_pool* pool, int32_t* new_map, void* new_slab, int32_t* 
 
 int cow_append(const cow_pool* dst, const cow_pool* other, int32_t* admitted_map, int32_t* src_rows,
                int32_t* dst_rows, int32_t* flags_scratch, void* stream) {
+  if (!dense_maps(dst, 1) || !dense_maps(other, 1)) return COW_ERR_UNSUPPORTED;
   if (!dst || !other || !admitted_map || !src_rows || !dst_rows || !flags_scratch) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
   ScanLaunch C{};
@@ -873,6 +879,7 @@ int64_t cow_append_workspace_bytes(const cow_pool* others, int32_t layers) {
 
 int cow_append_count_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, void* workspace,
                             int64_t workspace_bytes, int32_t* counts, void* stream) {
+  if (!dense_maps(dsts, layers) || !dense_maps(others, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(dsts, layers) || !layers_ok(others, layers) || !counts) return COW_ERR_INVALID;
   if (!workspace_ok(workspace, workspace_bytes, cow_append_workspace_bytes(others, layers))) return COW_ERR_INVALID;
   ScanLaunch C{};
@@ -897,6 +904,7 @@ int cow_append_count_layers(const cow_pool* dsts, const cow_pool* others, int32_
 
 int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t layers, int32_t* const* admitted_maps,
                       void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!dense_maps(dsts, layers) || !dense_maps(others, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(dsts, layers) || !layers_ok(others, layers) || !admitted_maps) return COW_ERR_INVALID;
   if (!workspace_ok(workspace, workspace_bytes, cow_append_workspace_bytes(others, layers))) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
@@ -941,6 +949,7 @@ int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t laye
 
 int cow_retain(const cow_pool* pool, const int64_t* bank_indices, int64_t count, int32_t* new_map,
                int64_t* new_templates, int32_t* selected, int32_t* status, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if (!pool || !selected || !status || count < 0 || (count > 0 && (!bank_indices || !new_map || !new_templates)))
     return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
@@ -977,6 +986,7 @@ int64_t cow_retain_workspace_bytes(const cow_pool* pools, int32_t layers) {
 int cow_retain_layers(const cow_pool* pools, const int64_t* const* bank_indices, const int64_t* counts, int32_t layers,
                       int32_t* const* new_maps, int64_t* const* new_templates, void* workspace,
                       int64_t workspace_bytes, int32_t* status, void* stream) {
+  if (!dense_maps(pools, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(pools, layers) || !bank_indices || !counts || !new_maps || !new_templates || !status)
     return COW_ERR_INVALID;
   const int64_t need = cow_retain_workspace_bytes(pools, layers);
@@ -1060,6 +1070,7 @@ int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t inde
 
 int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,
                           void* stream) {
+  if (!dense_maps(pools, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(pools, layers)) return COW_ERR_INVALID;
   const int64_t n = pools[0].banks * pools[0].slots;
   if (!workspace_ok(workspace, workspace_bytes, cow_pack_workspace_bytes(n, layers))) return COW_ERR_INVALID;
@@ -1100,6 +1111,7 @@ int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace
 // ---- validation --------------------------------------------------------------
 
 int cow_validate(const cow_pool* pool, int32_t* counts, int32_t* status, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if (!pool || !counts || !status) return COW_ERR_INVALID;
   cudaStream_t st = as_stream(stream);
   if (pool->capacity > 0 &&
@@ -1128,6 +1140,7 @@ int64_t cow_validate_workspace_bytes(const cow_pool* pools, int32_t layers) {
 
 int cow_validate_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes, int32_t* out,
                         void* stream) {
+  if (!dense_maps(pools, layers)) return COW_ERR_UNSUPPORTED;
   if (!layers_ok(pools, layers) || !out) return COW_ERR_INVALID;
   const int64_t need = cow_validate_workspace_bytes(pools, layers);
   if (!workspace_ok(workspace, workspace_bytes, need)) return COW_ERR_INVALID;
@@ -1158,6 +1171,7 @@ int cow_validate_layers(const cow_pool* pools, int32_t layers, void* workspace, 
 }
 
 int cow_materialize(const cow_pool* pool, void* out, int32_t out_dtype, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   if (!pool || !out || !valid_dtype(out_dtype) || pool->width % 4 != 0) return COW_ERR_INVALID;
   const int64_t rows = pool->banks * pool->slots;
   if (rows == 0) return COW_OK;

@@ -124,6 +124,7 @@ extern "C" {
 int cow_prefill_recurrence_layers(const cow_pool* pools, const cow_step* prefixes, int32_t layers,
                                   int64_t time, int32_t writes, int32_t reads, int32_t index_dtype,
                                   int32_t act_dtype, void* stream) {
+  if (!dense_maps(pools, layers)) return COW_ERR_UNSUPPORTED;
   if (!pools || !prefixes || layers < 1 || layers > COW_MAX_LAYERS || time < 0 || !valid_dtype(act_dtype))
     return COW_ERR_INVALID;
   const cow_pool& p0 = pools[0];
@@ -168,6 +169,7 @@ int cow_prefill_recurrence_layers(const cow_pool* pools, const cow_step* prefixe
 
 int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t time, int32_t writes,
                            int32_t reads, int32_t index_dtype, int32_t act_dtype, void* stream) {
+  if (!dense_maps(pool, 1)) return COW_ERR_UNSUPPORTED;
   return cow_prefill_recurrence_layers(pool, prefix, 1, time, writes, reads, index_dtype, act_dtype, stream);
 }
 

@@ -33,7 +33,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .allocator import PackedSDMCopyOnWriteState, new_decode_scratch
+from .allocator import POOL_EPOCHS, PackedSDMCopyOnWriteState, new_decode_scratch
 
 
 def _current_raw_stream(device_index: int) -> int:
@@ -71,6 +71,7 @@ class DecodeSession:
         if writes > _lib.MAX_WRITES or reads > _lib.MAX_READS or p0.width % 4 or p0.width > _lib.MAX_WIDTH:
             raise ValueError("route counts or width outside the compiled kernels")
         self.pools = list(pools)
+        self._pool_dicts = [p.__dict__ for p in self.pools]
         self.writes, self.reads, self.act_dtype = writes, reads, act_dtype
         self.device = p0.values.device
         B, D = p0.banks, p0.width
@@ -113,17 +114,18 @@ class DecodeSession:
         self._scratch = new_decode_scratch(self.device, B * len(pools), len(pools))  # owned by this session
         self._need = B * writes  # first touches one step can make in a pool
         self._proof_steps, self._proof_key = 0, None
-        # free-count snapshots copied to the host without a synchronisation
-        # (see _prove): the issued-step counter, the pending snapshot and its
-        # pinned landing buffer
+        # free counts the decode kernel mirrors to the host (see _prove): the
+        # launch counter of this session's scratch, the first launch whose
+        # mirror values are trusted, and the page-locked words themselves
         self._issued = 0
-        self._snap = None
-        self._snapshots = True  # off for good once a step decodes on another stream than the current one
-        self.snapshot_proofs = 0  # pool proofs renewed from a snapshot instead of a synchronising read
-        self._snap_host = torch.empty(len(pools), dtype=torch.int32, pin_memory=pinned_host)
+        self._mirror_from = 0
+        self.snapshot_proofs = 0  # pool proofs renewed from a mirrored count instead of a synchronising read
+        self._mirror = torch.zeros(len(pools), dtype=torch.int64, pin_memory=pinned_host)
+        self._mirror_np = self._mirror.numpy()
         self._out_bytes = self.host_outputs.numel() * self.host_outputs.element_size()
         self._device_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._lib = _lib.load()
+        self._registered: list[torch.Tensor] = []  # pinned host tensors registered with the library
 
     @staticmethod
     def _views(buf: torch.Tensor, per: dict) -> dict:
@@ -133,58 +135,65 @@ class DecodeSession:
         return out
 
     def _pools(self):
-        key = tuple(p.__dict__.get("_tensor_version", 0) for p in self.pools)
-        if key != self._pool_key:
-            self._pool_array = (_lib.CowPool * len(self.pools))(*[p._pool() for p in self.pools])
-            self._pool_key = key
+        key = self._pool_key
+        if key is None or key[0] != POOL_EPOCHS[1]:
+            versions = tuple(d.get("_tensor_version", 0) for d in self._pool_dicts)
+            if key is None or key[1] != versions:
+                arr = (_lib.CowPool * len(self.pools))(*[p._pool() for p in self.pools])
+                if self._mirror.is_pinned():
+                    base = self._mirror.data_ptr()
+                    for l in range(len(self.pools)):
+                        arr[l].free_mirror = base + 8 * l
+                self._pool_array = arr
+            self._pool_key = (POOL_EPOCHS[1], versions)
         return self._pool_array
 
-    def _prove(self, on_current: bool = True) -> None:
+    def _prove(self) -> None:
         """The reference's per-step capacity proof (allocator.py:746-774) for every pool.
 
         The common case (every pool proven with rows left for this step) is one
         decrement per pool: after a full check the session knows how many steps
         every pool's proof still covers, and keeps that count while no pool was
-        assigned to since (its ``_mutations`` counter is unchanged).
+        assigned to since (the process-wide assignment counter
+        ``POOL_EPOCHS[0]`` is unchanged).
 
         When a proof runs out the reference reads ``free_count`` (a host
-        synchronisation).  Two steps before that, the session copies every
-        pool's free count to pinned host memory in the background; a pool whose
-        proof runs out then takes ``snapshot - need x (steps issued after it)``
-        as its proof when that lower bound covers the step.  Otherwise, or when
-        the snapshot has not landed or a pool changed since, the reference's
+        synchronisation).  Here every decode launch writes each pool's settled
+        free count, tagged with the launch's epoch, into a page-locked host
+        word (``cow_pool.free_mirror``; the epoch counts launches on the
+        session's own scan scratch).  A pool whose proof runs out takes
+        ``mirror - need x (launches issued after that one)`` as its proof when
+        that lower bound covers the step; otherwise, or when a pool was changed
+        from outside the session since the mirrored launch, the reference's
         synchronising check runs, so growth happens at exactly the steps where
-        the reference grows (the bound never exceeds the true free count).
-        Snapshots are taken and used only while every step decodes on the current
-        stream, which orders them with the decodes they must follow.  A step run on
-        these pools outside the session goes through ``prepare_step_capacity`` (the
-        reference's contract), whose assignment invalidates a pending snapshot."""
+        the reference grows (the bound never exceeds the true free count).  A
+        step run on these pools outside the session goes through
+        ``prepare_step_capacity`` (the reference's contract), whose assignment
+        makes the session distrust every mirror value written before it."""
         need = self._need
-        pools = self.pools
+        pools = self._pool_dicts
+        epoch = self._issued  # launch epoch of the step being proven
         self._issued += 1
-        if not on_current:
-            self._snapshots, self._snap = False, None
-        if self._proof_steps > 0 and self._proof_key == tuple(p.__dict__["_mutations"] for p in pools):
+        if self._proof_steps > 0 and self._unchanged_since(self._proof_key):
             self._proof_steps -= 1
-            for p in pools:
-                d = p.__dict__
+            for d in pools:
                 d["proven_maximum_additional_allocations"] -= need
-            if self._proof_steps <= 2 and self._snap is None and self._snapshots:
-                self._snapshot()
             return
-        snap = self._snap_bounds()
+        if not self._unchanged_since(self._proof_key):
+            self._mirror_from = epoch  # a pool changed outside the session: older mirror values are stale
+        bounds = self._mirror_bounds(epoch)
         steps = None
-        for l, p in enumerate(pools):
-            d = p.__dict__
+        for l, d in enumerate(pools):
             if d["growth_quantum_rows"]:
                 left = d["proven_maximum_additional_allocations"]
                 if left >= need and d["capacity_is_proven"]:
                     d["proven_maximum_additional_allocations"] = left - need
-                elif snap is not None and d["capacity_is_proven"] and snap[l] >= need:
-                    d["proven_maximum_additional_allocations"] = snap[l] - need
+                elif bounds is not None and d["capacity_is_proven"] and bounds[l] >= need \
+                        and not d["map_table_slots"]:  # hashed pools renew through their table check
+                    d["proven_maximum_additional_allocations"] = bounds[l] - need
                     self.snapshot_proofs += 1
                 else:
-                    p.prepare_step_capacity(need)
+                    self.pools[l].prepare_step_capacity(need)
                 left = d["proven_maximum_additional_allocations"] // need if need else 1 << 30
                 steps = left if steps is None else min(steps, left)
             elif not d["capacity_is_proven"]:
@@ -192,32 +201,39 @@ class DecodeSession:
             else:
                 steps = 0  # fixed pools keep the full check (no counter to decrement)
         self._proof_steps = steps or 0
-        self._proof_key = tuple(p.__dict__["_mutations"] for p in pools)
+        self._proof_key = self._mutation_key()
 
-    def _snapshot(self) -> None:
-        """Queue a copy of every pool's free count (after the steps issued so far) to
-        pinned host memory on the current stream (not while it is being captured)."""
-        if torch.cuda.is_current_stream_capturing():
-            return
-        counts = torch.cat([p.free_count.reshape(1) for p in self.pools])
-        self._snap_host.copy_(counts, non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record()
-        self._snap = (ev, self._issued - 1, tuple(p.__dict__["_mutations"] for p in self.pools))
+    def _mirror_bounds(self, epoch: int):
+        """Per-pool lower bounds on the free rows before launch ``epoch``, from the
+        mirrored free counts of launches this session may trust; None if none."""
+        out = []
+        any_valid = False
+        for v in self._mirror_np.tolist():
+            at, free = (v >> 32) & 0xFFFFFFFF, v & 0xFFFFFFFF
+            if v == 0 or at < self._mirror_from or at >= epoch:
+                out.append(-1)
+                continue
+            any_valid = True
+            # every launch issued after the mirrored one pops at most `need` rows per pool
+            out.append(free - self._need * (epoch - 1 - at))
+        return out if any_valid else None
 
-    def _snap_bounds(self):
-        """Per-pool lower bounds on the free rows before the step being issued, from a
-        landed snapshot taken since the pools last changed; None otherwise."""
-        snap, self._snap = self._snap, None
-        if snap is None:
-            return None
-        ev, at, key = snap
-        if key != tuple(p.__dict__["_mutations"] for p in self.pools) or torch.cuda.is_current_stream_capturing() \
-                or not ev.query():
-            return None
-        # every step issued after the snapshot pops at most `need` rows per pool
-        charged = self._need * (self._issued - 1 - at)
-        return [int(c) - charged for c in self._snap_host.tolist()]
+    def _mutation_key(self) -> list:
+        """[process-wide assignment count, per-pool assignment counts] now."""
+        return [POOL_EPOCHS[0], tuple(d["_mutations"] for d in self._pool_dicts)]
+
+    def _unchanged_since(self, key) -> bool:
+        """No pool of this session was assigned to since ``key`` was taken: one
+        integer compare when no pool anywhere changed, else the per-pool counts
+        (and the key is moved forward so the next check is cheap again)."""
+        if key is None:
+            return False
+        if key[0] == POOL_EPOCHS[0]:
+            return True
+        if key[1] == tuple(d["_mutations"] for d in self._pool_dicts):
+            key[0] = POOL_EPOCHS[0]
+            return True
+        return False
 
     def _stream_handle(self) -> int:
         return _current_raw_stream(self._device_index)
@@ -227,7 +243,7 @@ class DecodeSession:
         """One decode token for every bank of every pool; returns ``outputs`` ``[L, B, D]`` (device)."""
         current = self._stream_handle()
         handle = stream.cuda_stream if stream is not None else current
-        self._prove(on_current=handle == current)
+        self._prove()
         _lib.check(self._lib.cow_decode_step(self._pools(), self._steps, len(self.pools), self.writes, self.reads,
                                              _lib.I64, self._act_code, self._scratch.data_ptr(),
                                              self._scratch.numel(), handle), "cow_decode_step")
@@ -260,6 +276,8 @@ class DecodeSession:
                 self.step_bytes, host_outputs[b].data_ptr(), outputs[b].data_ptr(), self._out_bytes,
                 h2d.cuda_stream, d2h.cuda_stream, events[b][0].cuda_event, events[b][1].cuda_event,
                 events[b][2].cuda_event) for b in range(2))
+            for t in host_outputs:
+                self._register(t)
             self._pipe = {
                 "inputs": inputs, "outputs": outputs, "steps": steps, "host_outputs": host_outputs,
                 "h2d": h2d, "d2h": d2h, "events": events, "k": 0, "descs": descs,
@@ -277,8 +295,8 @@ class DecodeSession:
         reused two steps later.  Steps decode strictly in call order on the
         current stream; the copies run on two side streams.
         """
-        if host_step.numel() != self.step_bytes or host_step.dtype != torch.uint8 \
-                or host_step.device.type != "cpu" or not host_step.is_contiguous():
+        if host_step.nbytes != self.step_bytes or host_step.dtype is not torch.uint8 \
+                or host_step.is_cuda or not host_step.is_contiguous():
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
         pipe = self._pipe if self._pipe is not None else self._pipeline()
         b = pipe["k"] & 1
@@ -294,6 +312,35 @@ class DecodeSession:
             _lib.check(rc, "cow_decode_step_host_piped")
         return pipe["host_outputs"][b], pipe["events"][b][2]
 
+    def _register(self, t: torch.Tensor) -> None:
+        if t.is_pinned() and self._lib.cow_register_host_range(t.data_ptr(), t.numel() * t.element_size()) == 0:
+            self._registered.append(t)  # held until close(): the library keeps its address
+
+    def register_host_steps(self, host_steps: torch.Tensor) -> None:
+        """Register a pinned buffer of host steps (e.g. ``[K, step_bytes]`` uint8) for
+        ``step_host_mapped``: steps inside it skip the per-call pinned-memory query.
+        The session holds the tensor until ``close()``."""
+        if not host_steps.is_pinned() or not host_steps.is_contiguous():
+            raise ValueError("host steps must be a contiguous pinned tensor")
+        _lib.check(self._lib.cow_register_host_range(host_steps.data_ptr(),
+                                                     host_steps.numel() * host_steps.element_size()),
+                   "cow_register_host_range")
+        self._registered.append(host_steps)
+
+    def close(self) -> None:
+        """Forget the host ranges this session registered (idempotent)."""
+        lib = getattr(self, "_lib", None)
+        for t in getattr(self, "_registered", ()):
+            if lib is not None:
+                lib.cow_unregister_host_range(t.data_ptr())
+        self._registered = []
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
     @torch.no_grad()
     def step_host_mapped(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
         """Host-to-host step with no copy calls (``cow_decode_step_host_mapped``).
@@ -305,8 +352,8 @@ class DecodeSession:
         two steps later, and ``host_step`` must stay untouched until the event
         has completed.  Steps decode in call order on the current stream.
         """
-        if host_step.numel() != self.step_bytes or host_step.dtype != torch.uint8 \
-                or host_step.device.type != "cpu" or not host_step.is_contiguous():
+        if host_step.nbytes != self.step_bytes or host_step.dtype is not torch.uint8 \
+                or host_step.is_cuda or not host_step.is_contiguous():
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
         ptr = host_step.data_ptr()
         pipe = self._pipe if self._pipe is not None else self._pipeline()
@@ -332,7 +379,7 @@ class DecodeSession:
         default ``host_inputs``) to the device, decode, copy the readouts back into
         ``host_outputs`` (asynchronously on the current stream) and return it."""
         src = self.host_inputs if host_step is None else host_step
-        if src.numel() != self.step_bytes or src.dtype != torch.uint8 or src.device.type != "cpu" \
+        if src.numel() != self.step_bytes or src.dtype != torch.uint8 or src.is_cuda \
                 or not src.is_contiguous():
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
         self._prove()

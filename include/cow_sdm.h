@@ -54,6 +54,7 @@ extern "C" {
 #define COW_ST_FREE_DUPLICATE 0x200   /* validate: free stack holds a row twice */
 #define COW_ST_NOT_COVERED 0x400      /* validate: a row is neither live nor free */
 #define COW_ST_ROW_RANGE 0x800        /* validate: a map / stack entry lies outside capacity */
+#define COW_ST_MAP_FULL 0x1000        /* a hashed map's bank table had no empty entry for a first touch */
 
 #define COW_MAX_LAYERS 8
 #define COW_MAX_WRITES 32
@@ -71,8 +72,22 @@ typedef struct cow_pool {
   int32_t* status;
   int64_t banks, slots, width, capacity, template_count;
   int32_t slab_dtype; /* COW_F32 / COW_BF16 / COW_F16 */
-  int32_t _pad;
+  int32_t map_kind;   /* COW_MAP_DENSE (0): map is [banks, slots] int32;
+                         COW_MAP_HASH (1): map is [banks, table_slots] uint64
+                         open-addressing tables (see cow_hash_from_dense) */
+  int64_t table_slots; /* hashed maps: entries per bank, a power of two (0 for dense maps) */
+  /* Optional (may be NULL): a page-locked host word the decode step writes
+   * once per launch after the pool's free count is settled:
+   * (launch epoch << 32) | free count.  The launch epoch is the scan
+   * scratch's launch counter (0 for the first launch on zero-filled scratch,
+   * +1 per launch), so a runtime that owns its scratch knows which step a
+   * value belongs to and can renew its capacity proof without reading the
+   * device. */
+  uint64_t* free_mirror;
 } cow_pool;
+
+#define COW_MAP_DENSE 0
+#define COW_MAP_HASH 1
 
 /* One decode step's routes for one pool (the arguments of
  * packed_sdm_cow_step, allocator.py:1382-1396).  Index tensors are [banks,W] /
@@ -223,6 +238,35 @@ int cow_decode_step_host_piped(const cow_host_pipeline* pipe, const void* host_i
  * touch `host_inputs` / `host_outputs` until that event has completed. */
 int cow_decode_step_host_mapped(const cow_host_pipeline* pipe, const void* host_inputs, void* host_outputs,
                                 void* stream);
+
+/* Register / forget a page-locked host range for cow_decode_step_host_mapped:
+ * steps whose host buffers lie inside a registered range skip the per-call
+ * pointer query (two runtime calls per token).  Registration checks that the
+ * whole range is page-locked and mapped for the current device; the caller
+ * keeps the memory alive and unregisters it before freeing it.  At most 64
+ * ranges per process.  No counterpart in the reference (host-side serving
+ * plumbing). */
+int cow_register_host_range(const void* host, int64_t bytes);
+int cow_unregister_host_range(const void* host);
+
+/* Hashed logical maps (cow_pool.map_kind == COW_MAP_HASH).  No counterpart
+ * in the reference, which keeps only the dense [banks, slots] int32 map
+ * (allocator.py:496-504) and names a sparse map as future work.  Each bank
+ * owns an open-addressing table of table_slots (a power of two) uint64
+ * entries, (slot << 32) | physical row, all ones when empty.
+ * cow_decode_step reads and extends hashed pools directly (a first touch
+ * that finds its bank's table full sets COW_ST_MAP_FULL and maps nothing);
+ * every other entry point taking a cow_pool needs a dense map and returns
+ * COW_ERR_UNSUPPORTED for a hashed one.
+ *   cow_hash_from_dense: tables [banks, table_slots] <- every map entry >= 0
+ *                        (the tables are cleared first)
+ *   cow_hash_to_dense:   map [banks, slots] <- -1 everywhere, then every entry
+ *   cow_hash_max_live:   *out <- the largest number of entries in one bank */
+int cow_hash_from_dense(const int32_t* map, int64_t banks, int64_t slots, void* tables, int64_t table_slots,
+                        int32_t* status, void* stream);
+int cow_hash_to_dense(const void* tables, int64_t banks, int64_t table_slots, int32_t* map, int64_t slots,
+                      int32_t* status, void* stream);
+int cow_hash_max_live(const void* tables, int64_t banks, int64_t table_slots, int32_t* out, void* stream);
 
 /* Dense-table control (dense_sdm_sparse_step, allocator.py:1529-1633, kernel
  * allocator.py:368-460): the same math on dense [banks,slots,width] tables.

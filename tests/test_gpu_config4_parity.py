@@ -61,7 +61,18 @@ class Zipf:
         return torch.cat(out)
 
 
-def test_config4_shape_two_pass_decode_matches_oracle(dev):
+def _dense_map(st):
+    """The pool's logical-to-physical map in the reference's dense form."""
+    from copy_on_write_sdm_b200.allocator import dense_maps
+
+    with dense_maps([st]):
+        return st.logical_to_physical.cpu().numpy()
+
+
+@pytest.mark.parametrize("map_kind", ["dense", "hash"])
+def test_config4_shape_two_pass_decode_matches_oracle(dev, map_kind):
+    """``hash``: the same trace on per-bank hashed tables (sized for the prefix
+    plus the trace's first touches); maps compared in their dense form."""
     from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState, _lib, packed_sdm_cow_step_layers
 
     lib = _lib.load()
@@ -100,6 +111,9 @@ def test_config4_shape_two_pass_decode_matches_oracle(dev):
     np.testing.assert_array_equal(st.free_rows[:fc].cpu().numpy(), np.arange(touched, touched + extra))
     ref = O.OracleState(shared_initial_memory=m0_np, template_indices=tmpl, values=slab,
                         logical_to_physical=mp.copy(), free_rows=st.free_rows.cpu().numpy().copy(), free_count=fc)
+    if map_kind == "hash":
+        t = st.use_hash_map(headroom_rows_per_bank=W * STEPS)
+        assert st.storage_bytes()["logical_to_physical"] == banks * t * 8 < banks * SLOTS * 4 // 8
     first_total = 0
     for step in range(STEPS):
         x = dict(write_indices=zipf.distinct(banks, W, gen), read_indices=zipf.distinct(banks, R, gen),
@@ -116,12 +130,12 @@ def test_config4_shape_two_pass_decode_matches_oracle(dev):
         assert int(st.free_count) == ref.free_count
         assert st.status() == 0
         if step % 4 == 3:
-            np.testing.assert_array_equal(st.logical_to_physical.cpu().numpy(), ref.logical_to_physical)
+            np.testing.assert_array_equal(_dense_map(st), ref.logical_to_physical)
             fc = int(st.free_count)
             np.testing.assert_array_equal(st.free_rows[:fc].cpu().numpy(), ref.free_stack())
     # Zipf routes over a 192-token prefix: a mix of private reuse and first touches.
     assert 0 < first_total < banks * W * STEPS
-    mp = st.logical_to_physical.cpu().numpy()
+    mp = _dense_map(st)
     b, s = np.nonzero(mp >= 0)
     rows = mp[b, s]
     del b, s

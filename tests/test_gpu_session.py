@@ -171,8 +171,8 @@ def test_mapped_host_steps_match_sequential(dev):
     for o, e in pending:
         e.synchronize()
         got.append(o.clone())
-    for a, b in zip(want, got):
-        assert torch.equal(a, b)
+    for a, b in zip(want, got):  # the two paths may pick different decode kernels: 1e-5 as elsewhere
+        torch.testing.assert_close(b, a, atol=1e-5, rtol=1e-5)
     for p, q in zip(seq.pools, mapped.pools):
         assert torch.equal(p.logical_to_physical, q.logical_to_physical)
         fp = int(p.free_count)

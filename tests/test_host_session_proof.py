@@ -1,13 +1,19 @@
-"""The session's capacity proof on the host, without a GPU: a proof renewed from a
-background free-count snapshot is used only when its lower bound
-(snapshot - need x steps issued since) covers the step; otherwise, or after a
-pool changed, or once a step decoded on another stream, the reference's
-synchronising ``prepare_step_capacity`` runs."""
+"""The session's capacity proof on the host, without a GPU.
+
+Every decode launch mirrors each pool's settled free count, tagged with the
+launch's epoch, into a page-locked host word.  A proof renewed from that
+mirror (mirror - need x launches issued since) is used only when the bound
+covers the step; otherwise, or when a pool changed outside the session after
+the mirrored launch, the reference's synchronising ``prepare_step_capacity``
+runs.  Here a fake "kernel" writes the mirror the way the decode kernel does.
+"""
 
 from __future__ import annotations
 
-import pytest
+import numpy as np
 import torch
+
+from copy_on_write_sdm_b200.allocator import POOL_EPOCHS
 
 
 class _Pool:
@@ -19,6 +25,7 @@ class _Pool:
         d["growth_quantum_rows"] = quantum
         d["proven_maximum_additional_allocations"] = 0
         d["capacity_is_proven"] = True
+        d["map_table_slots"] = 0
         d["_mutations"] = 0
         self.free_count = torch.tensor(free, dtype=torch.int32)
         self.exact_calls = 0
@@ -26,75 +33,80 @@ class _Pool:
     def prepare_step_capacity(self, need: int) -> None:
         self.exact_calls += 1
         d = self.__dict__
-        d["_mutations"] += 1  # the reference path assigns, which bumps the counter
+        d["_mutations"] += 1  # the reference path assigns, which bumps the counters
+        POOL_EPOCHS[0] += 1
         d["proven_maximum_additional_allocations"] = int(self.free_count) - need
 
 
-class _Event:
-    def record(self, *a):
-        pass
-
-    def query(self):
-        return True
-
-
-@pytest.fixture()
-def session(monkeypatch):
+def make_session(frees, need=4):
     from copy_on_write_sdm_b200.session import DecodeSession
 
-    monkeypatch.setattr(torch.cuda, "Event", _Event)
-    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
-
-    def make(frees, need=4):
-        s = object.__new__(DecodeSession)
-        s.pools = [_Pool(f) for f in frees]
-        s._need = need
-        s._proof_steps, s._proof_key = 0, None
-        s._issued, s._snap, s._snapshots, s.snapshot_proofs = 0, None, True, 0
-        s._snap_host = torch.empty(len(frees), dtype=torch.int32)
-        return s
-    return make
+    s = object.__new__(DecodeSession)
+    s.pools = [_Pool(f) for f in frees]
+    s._pool_dicts = [p.__dict__ for p in s.pools]
+    s._need = need
+    s._proof_steps, s._proof_key = 0, None
+    s._issued, s._mirror_from, s.snapshot_proofs = 0, 0, 0
+    s._mirror_np = np.zeros(len(frees), dtype=np.int64)
+    return s
 
 
-def _run(s, steps, pops=4, on_current=True):
-    """Issue `steps` proofs; each step then pops `pops` rows from every pool."""
+def _run(s, steps, pops=4, lag=0):
+    """Issue ``steps`` proofs; each step then pops ``pops`` rows from every pool,
+    and the launch ``lag`` steps back mirrors its free counts (lag > 0: the host
+    runs ahead of the device)."""
     for _ in range(steps):
-        s._prove(on_current=on_current)
-        for p in s.pools:
+        epoch = s._issued
+        s._prove()
+        for l, p in enumerate(s.pools):
             p.free_count -= pops
+            hist = p.__dict__.setdefault("_history", [])
+            hist.append((epoch, int(p.free_count)))
+            if len(hist) > lag:
+                at, free = hist[-1 - lag]
+                s._mirror_np[l] = (at << 32) | free
 
 
-def test_snapshot_bound_replaces_the_synchronising_read(session):
-    s = session([40, 400])
+def test_mirror_bound_replaces_the_synchronising_read():
+    s = make_session([40, 400])
     _run(s, 1)
     assert [p.exact_calls for p in s.pools] == [1, 1]
-    _run(s, 12, pops=1)  # few first touches: the bounds keep covering the steps
+    _run(s, 12, pops=1, lag=2)  # few first touches: the bounds keep covering the steps
     assert s.snapshot_proofs > 0
+    assert [p.exact_calls for p in s.pools] == [1, 1]
     # every pool's proof never exceeds its true free rows
     for p in s.pools:
         assert p.__dict__["proven_maximum_additional_allocations"] <= int(p.free_count)
 
 
-def test_insufficient_bound_falls_back_to_the_exact_check(session):
-    s = session([9, 9])  # the snapshot bound soon drops below one step's need
+def test_bound_never_exceeds_the_true_free_rows_when_the_host_runs_ahead():
+    s = make_session([200, 60, 1000], need=8)
+    for lag in (0, 1, 3, 5):
+        _run(s, 20, pops=8, lag=lag)
+        for p in s.pools:
+            assert p.__dict__["proven_maximum_additional_allocations"] <= int(p.free_count)
+
+
+def test_insufficient_bound_falls_back_to_the_exact_check():
+    s = make_session([9, 9])  # the mirrored bound soon drops below one step's need
     _run(s, 4, pops=4)
     assert all(p.exact_calls >= 2 for p in s.pools)
     assert s.snapshot_proofs == 0
 
 
-def test_pool_change_invalidates_a_pending_snapshot(session):
-    s = session([40])
-    _run(s, 1, pops=0)
-    while s._snap is None:
-        _run(s, 1, pops=0)
-    s.pools[0].__dict__["_mutations"] += 1  # e.g. an admission assigned to the pool
-    assert s._snap_bounds() is None
-
-
-def test_another_stream_turns_snapshots_off(session):
-    s = session([400])
+def test_pool_change_outside_the_session_distrusts_older_mirror_values():
+    s = make_session([400])
     _run(s, 3, pops=0)
-    _run(s, 1, pops=0, on_current=False)
-    assert s._snapshots is False and s._snap is None
-    _run(s, 30, pops=1)
-    assert s.snapshot_proofs == 0
+    s.pools[0].__dict__["_mutations"] += 1  # e.g. an admission assigned to the pool
+    POOL_EPOCHS[0] += 1
+    s._proof_steps = 0  # the proof ran out: the next step takes the slow path
+    s.pools[0].__dict__["proven_maximum_additional_allocations"] = 0
+    before = s.pools[0].exact_calls
+    s._prove()
+    assert s._mirror_from == 3
+    assert s.pools[0].exact_calls == before + 1  # mirror values of launches 0..2 are not used
+
+
+def test_unset_mirror_words_are_ignored():
+    s = make_session([100, 100])
+    assert s._mirror_bounds(5) is None
