@@ -479,7 +479,7 @@ class PackedSDMCopyOnWriteState:
 
     @staticmethod
     def _table_slots_for(live: int) -> int:
-        need = max(2, -(-live * 10 // 7))  # live / HASH_MAX_LOAD, rounded up
+        need = max(4, -(-live * 10 // 7))  # live / HASH_MAX_LOAD, rounded up
         return 1 << (need - 1).bit_length()
 
     @torch.no_grad()
@@ -503,7 +503,7 @@ class PackedSDMCopyOnWriteState:
         mapping = self.logical_to_physical
         live = int((mapping >= 0).sum(dim=1).max()) if self.banks else 0
         t = table_slots if table_slots is not None else self._table_slots_for(live + headroom_rows_per_bank)
-        if t < 2 or t & (t - 1) or t <= live:
+        if t < 4 or t & (t - 1) or t <= live:
             raise ValueError("hash map table size must be a power of two above the live slots of every bank")
         tables = torch.empty(self.banks, t, dtype=torch.int64, device=mapping.device)
         status = torch.zeros((), dtype=torch.int32, device=mapping.device)

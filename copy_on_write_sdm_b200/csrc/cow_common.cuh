@@ -170,38 +170,49 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int li
 // --------------------------------------------------------------------------
 //
 // A bank's private slots live in an open-addressing table of T = 2^log_t
-// 64-bit entries, (slot << 32) | physical row, all ones when empty, probed
-// linearly from a multiplicative hash of the slot.  Only one warp touches a
-// bank's table during a decode step, and entries are never deleted inside a
-// step, so a lookup stops at the first empty entry.
+// 64-bit entries, (slot << 32) | physical row, all ones when empty.  Entries
+// form buckets of four (32 bytes, one memory sector); a slot is looked for from
+// its home bucket (a multiplicative hash of the slot) onwards, bucket by
+// bucket, each bucket read with two 16-byte loads.  Only one warp touches a
+// bank's table during a decode step, lookups of a step precede its inserts,
+// and entries are never deleted inside a step, so a lookup stops at the first
+// empty entry.  T >= 4.
 constexpr unsigned long long kHashEmpty = ~0ull;
 
-__device__ __forceinline__ uint32_t hash_home(int slot, int log_t) {
-  return (static_cast<uint32_t>(slot) * 2654435761u) >> (32 - log_t);
+__device__ __forceinline__ uint32_t hash_home(int slot, int log_buckets) {
+  return log_buckets == 0 ? 0u : (static_cast<uint32_t>(slot) * 2654435761u) >> (32 - log_buckets);
 }
 
 // Physical row of `slot` in the bank's table, -1 when the slot is shared.
 __device__ __forceinline__ int hash_find(const unsigned long long* table, int log_t, int slot) {
-  const uint32_t mask = (1u << log_t) - 1u;
-  uint32_t i = hash_home(slot, log_t);
+  const uint32_t mask = (1u << (log_t - 2)) - 1u;
+  uint32_t b = hash_home(slot, log_t - 2);
   for (uint32_t n = 0; n <= mask; ++n) {
-    const unsigned long long e = table[i];
-    if (e == kHashEmpty) return -1;
-    if (static_cast<int>(e >> 32) == slot) return static_cast<int>(static_cast<uint32_t>(e));
-    i = (i + 1u) & mask;
+    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(table + 4 * static_cast<int64_t>(b));
+    const ulonglong2 lo = q[0], hi = q[1];
+    const unsigned long long e[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (e[k] == kHashEmpty) return -1;
+      if (static_cast<int>(e[k] >> 32) == slot) return static_cast<int>(static_cast<uint32_t>(e[k]));
+    }
+    b = (b + 1u) & mask;
   }
   return -1;
 }
 
-// Claim an empty entry for `slot` -> `phys`; false when the table is full.
+// Claim the first empty entry from `slot`'s home bucket on; false when the
+// table is full.
 __device__ __forceinline__ bool hash_insert(unsigned long long* table, int log_t, int slot, int phys) {
-  const uint32_t mask = (1u << log_t) - 1u;
+  const uint32_t mask = (1u << (log_t - 2)) - 1u;
   const unsigned long long entry =
       (static_cast<unsigned long long>(static_cast<uint32_t>(slot)) << 32) | static_cast<uint32_t>(phys);
-  uint32_t i = hash_home(slot, log_t);
+  uint32_t b = hash_home(slot, log_t - 2);
   for (uint32_t n = 0; n <= mask; ++n) {
-    if (table[i] == kHashEmpty && atomicCAS(table + i, kHashEmpty, entry) == kHashEmpty) return true;
-    i = (i + 1u) & mask;
+    unsigned long long* q = table + 4 * static_cast<int64_t>(b);
+    for (int k = 0; k < 4; ++k)
+      if (q[k] == kHashEmpty && atomicCAS(q + k, kHashEmpty, entry) == kHashEmpty) return true;
+    b = (b + 1u) & mask;
   }
   return false;
 }

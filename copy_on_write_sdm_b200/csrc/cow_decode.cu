@@ -759,7 +759,7 @@ int decode_step_impl(const cow_pool* pools, const cow_step* steps, int32_t layer
     L.log_t = 0;
     if (p.map_kind == COW_MAP_HASH) {
       const int64_t t = p.table_slots;
-      if (t < 2 || t > (int64_t(1) << 30) || (t & (t - 1)) != 0 || p.slots >= (int64_t(1) << 31)) return COW_ERR_INVALID;
+      if (t < 4 || t > (int64_t(1) << 30) || (t & (t - 1)) != 0 || p.slots >= (int64_t(1) << 31)) return COW_ERR_INVALID;
       while ((int64_t(1) << L.log_t) < t) ++L.log_t;
     } else if (p.map_kind != COW_MAP_DENSE) {
       return COW_ERR_INVALID;

@@ -20,7 +20,7 @@ namespace {
 constexpr int kHashThreads = 256;
 
 int hash_log2(int64_t t) {
-  if (t < 2 || t > (int64_t(1) << 30) || (t & (t - 1)) != 0) return -1;
+  if (t < 4 || t > (int64_t(1) << 30) || (t & (t - 1)) != 0) return -1;
   int k = 0;
   while ((int64_t(1) << k) < t) ++k;
   return k;

@@ -75,7 +75,7 @@ typedef struct cow_pool {
   int32_t map_kind;   /* COW_MAP_DENSE (0): map is [banks, slots] int32;
                          COW_MAP_HASH (1): map is [banks, table_slots] uint64
                          open-addressing tables (see cow_hash_from_dense) */
-  int64_t table_slots; /* hashed maps: entries per bank, a power of two (0 for dense maps) */
+  int64_t table_slots; /* hashed maps: entries per bank, a power of two >= 4 (0 for dense maps) */
   /* Optional (may be NULL): a page-locked host word the decode step writes
    * once per launch after the pool's free count is settled:
    * (launch epoch << 32) | free count.  The launch epoch is the scan
@@ -252,8 +252,9 @@ int cow_unregister_host_range(const void* host);
 /* Hashed logical maps (cow_pool.map_kind == COW_MAP_HASH).  No counterpart
  * in the reference, which keeps only the dense [banks, slots] int32 map
  * (allocator.py:496-504) and names a sparse map as future work.  Each bank
- * owns an open-addressing table of table_slots (a power of two) uint64
- * entries, (slot << 32) | physical row, all ones when empty.
+ * owns an open-addressing table of table_slots (a power of two, >= 4) uint64
+ * entries, (slot << 32) | physical row, all ones when empty, probed in
+ * 32-byte buckets of four from a multiplicative hash of the slot.
  * cow_decode_step reads and extends hashed pools directly (a first touch
  * that finds its bank's table full sets COW_ST_MAP_FULL and maps nothing);
  * every other entry point taking a cow_pool needs a dense map and returns

@@ -76,7 +76,7 @@ def test_round_trip_dense_hash_dense(dev):
 
 @pytest.mark.parametrize("banks,layers", [(64, 3), (2048, 1)])
 def test_growth_pool_decode_with_rehash_matches_oracle(dev, banks, layers):
-    """Tables start at two entries per bank; the capacity proof rehashes them as
+    """Tables start at four entries per bank; the capacity proof rehashes them as
     banks fill (several times over the trace) and the trace stays exact."""
     from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState, packed_sdm_cow_step_layers
 
@@ -87,7 +87,7 @@ def test_growth_pool_decode_with_rehash_matches_oracle(dev, banks, layers):
     for _ in range(layers):
         m0 = (0.02 * rng.standard_normal((1, slots, WIDTH))).astype(np.float32)
         st = PackedSDMCopyOnWriteState.allocate(cu(m0, dev), banks=banks, capacity_rows=q, growth_quantum_rows=q)
-        assert st.use_hash_map() == 2
+        assert st.use_hash_map() == 4
         states.append(st)
         refs.append(O.allocate(m0, banks=banks, capacity_rows=q, growth_quantum_rows=q))
     sizes = set()
@@ -198,6 +198,6 @@ def test_session_on_hashed_pools(dev):
         torch.cuda.synchronize(dev)
         torch.testing.assert_close(a.host_outputs, b.host_outputs, atol=ATOL, rtol=RTOL)
     for p, r in zip(a.pools, b.pools):
-        assert p.map_table_slots > 2
+        assert p.map_table_slots > 4
         same_pool(p, r)
         p.validate_invariants()
