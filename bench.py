@@ -645,6 +645,8 @@ def run_gpu_scaleout(args, rank, world, device):
         # The same pools on hashed maps (tables sized for every bank's private
         # slots plus the remaining steps' first touches), timed on the next K
         # steps of the trace.
+        if getattr(args, "hash_max_load", 0.0):
+            type(states[0]).HASH_MAX_LOAD = args.hash_max_load
         for st in states:
             st.use_hash_map(headroom_rows_per_bank=WRITES * K)
         torch.cuda.empty_cache()
@@ -1258,6 +1260,8 @@ def main() -> int:
     ap.add_argument("--requests", type=int, default=SO_REQUESTS, help="scaleout: requests over all GPUs")
     ap.add_argument("--prefix", type=int, default=SO_PREFIX, help="scaleout: prefix tokens")
     ap.add_argument("--hash-leg", action="store_true", help="scaleout: also time the pools on hashed maps")
+    ap.add_argument("--hash-max-load", type=float, default=0.0,
+                    help="scaleout: largest fill of a bank's hashed table (default: the library's 0.7)")
     ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
     ap.add_argument("--trim-every", type=int, default=0, help="churn: trim the pools every this many steps")
     ap.add_argument("--no-legs", dest="legs", action="store_false",

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import math
 from dataclasses import dataclass, field
 from typing import Any, Sequence
 
@@ -477,9 +478,9 @@ class PackedSDMCopyOnWriteState:
     # Tables are sized so that no bank's table is more than this full.
     HASH_MAX_LOAD = 0.7
 
-    @staticmethod
-    def _table_slots_for(live: int) -> int:
-        need = max(4, -(-live * 10 // 7))  # live / HASH_MAX_LOAD, rounded up
+    @classmethod
+    def _table_slots_for(cls, live: int) -> int:
+        need = max(4, math.ceil(live / cls.HASH_MAX_LOAD))
         return 1 << (need - 1).bit_length()
 
     @torch.no_grad()

@@ -47,7 +47,7 @@ def same_pool(a, b):
     assert torch.equal(a.free_rows[:fa], b.free_rows[:fb])
     assert a.capacity_rows == b.capacity_rows
     live = torch.from_numpy(mb[mb >= 0]).long().to(a.values.device)
-    torch.testing.assert_close(a.values[live], b.values[live], atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(a.values[live].float(), b.values[live].float(), atol=ATOL, rtol=RTOL)
 
 
 def test_round_trip_dense_hash_dense(dev):
@@ -201,3 +201,34 @@ def test_session_on_hashed_pools(dev):
         assert p.map_table_slots > 4
         same_pool(p, r)
         p.validate_invariants()
+
+
+@pytest.mark.parametrize("slab_dtype,width,w,r", [(torch.bfloat16, 128, 4, 16), (torch.float32, 256, 8, 64),
+                                                  (torch.float32, 64, 32, 256)])
+def test_hashed_decode_other_variants_match_dense_twin(dev, slab_dtype, width, w, r):
+    """Hashed tables under the other compiled decode variants (bf16 slab, wide
+    rows, W up to 32, R up to 256) against a dense twin on the same routes."""
+    from copy_on_write_sdm_b200 import PackedSDMCopyOnWriteState, packed_sdm_cow_step
+
+    rng = np.random.default_rng(width + w)
+    banks, slots = 96, 1024
+    q = O.growth_quantum_rows(banks, w, 2)
+    m0 = cu((0.02 * rng.standard_normal((2, slots, width))).astype(np.float32), dev)
+    tmpl = torch.arange(2, device=dev, dtype=torch.int64).repeat(banks // 2)
+
+    def make():
+        return PackedSDMCopyOnWriteState.allocate(m0, banks=banks, capacity_rows=q, growth_quantum_rows=q,
+                                                  template_indices=tmpl, state_dtype=slab_dtype)
+
+    hashed, dense = make(), make()
+    hashed.use_hash_map()
+    for _ in range(12):
+        x = {k: cu(v, dev) for k, v in O.synthetic_step_inputs(rng, banks, slots, width, w, r).items()}
+        outs = []
+        for st in (hashed, dense):
+            st.prepare_step_capacity(banks * w)
+            outs.append(packed_sdm_cow_step(st, **x, collect_diagnostics=False)[0])
+        torch.testing.assert_close(outs[0], outs[1], atol=ATOL, rtol=RTOL)
+    same_pool(hashed, dense)
+    assert hashed.status() == 0 and hashed.map_table_slots > 4
+    hashed.validate_invariants()
