@@ -59,11 +59,14 @@ L2_FLUSH_BYTES = 256 << 20
 # DRAM traffic per launch of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum); the capture commands and
 # figures are in profiles/.
-TRAFFIC_SCREEN = {"bytes_per_launch": 5_376_683,
-                  "source": "ncu, cow_decode_kernel, this bench's default run, cold L2 (mean of 3 launches)"}
-TRAFFIC_SCALEOUT = {"bytes_per_launch_per_bank": 14_256,
-                    "source": "ncu at 224 requests (12,544 banks, prefix 256): cow_count_kernel 8.56 MB + "
-                              "cow_decode_kernel 170.27 MB per step, scaled by banks"}
+TRAFFIC_SCREEN = {"bytes_per_launch": 5_430_000,
+                  "source": "ncu, cow_decode_split_kernel, bench.py --steps 4 --warmup 3 --no-legs, cold caches: "
+                            "dram__bytes.sum.per_second x gpu__time_duration.sum, 2 launches "
+                            "(profiles/decode_split_kernel_config3.md)"}
+TRAFFIC_SCALEOUT = {"bytes_per_launch_per_bank": 14_435,
+                    "source": "ncu at 224 requests (12,544 banks, prefix 256): cow_count_kernel 8.57 MB + "
+                              "cow_decode_kernel 172.5 MB per step, scaled by banks "
+                              "(profiles/decode_kernel_config4_hashed.md)"}
 
 
 def algorithmic_bytes(banks: int, first_touches: int, *, idx_bytes=8, val_bytes=4, act_bytes=4) -> int:
@@ -1341,7 +1344,7 @@ def main() -> int:
                      "frac": achieved / peak, "traffic": TRAFFIC_SCREEN["bytes_per_launch"],
                      "traffic_source": TRAFFIC_SCREEN["source"], "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": per_launch, "mean_launch_us": mean_launch_s * 1e6,
-                     "kernel": "cow_decode_kernel<f32,1,4,1>"},
+                     "kernel": "cow_decode_split_kernel"},
         "e2e": _e2e_block(tokens, res, e2e_ms, e2e_mapped_ms),
         "gpu_launches": K,
         "graph_incremental": None if res["incremental"] is None else {
