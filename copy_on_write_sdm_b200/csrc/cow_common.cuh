@@ -407,67 +407,57 @@ __device__ __forceinline__ int pool_prefix(const uint64_t* bank_flags, uint64_t*
 // With `staged` (a per-warp shared buffer of N <= kStageSlots ints, N % 4 == 0)
 // the bank's whole map row is copied into shared memory in the first round,
 // so the map lookups cost no second dependent trip to memory.
-template <bool kDense, int RC, class M>
-__device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int32_t* map,
-                                            int64_t row, int64_t map_row, int64_t N, int W, int R,
-                                            int idx64, int adt, int lane, unsigned& first_mask,
-                                            int& error_bits, int32_t* staged = nullptr, int log_t = 0) {
-  // Hashed maps: `map` points at the pool's [banks, 2^log_t] uint64 tables.
-  const unsigned long long* table =
-      log_t ? reinterpret_cast<const unsigned long long*>(map) + (map_row << log_t) : nullptr;
-  // The first 256 map entries come through registers (their latency is the
-  // route loads' latency), any further ones through cp.async.
-  constexpr int kRegStage = 2;
-  int4 mtmp[kRegStage];
-  if (!kDense && staged != nullptr) {
-    const int4* src = reinterpret_cast<const int4*>(map + map_row * N);
-#pragma unroll
-    for (int k = 0; k < kRegStage; ++k) {
-      const int i = lane + 32 * k;
-      if (i < static_cast<int>(N >> 2)) mtmp[k] = __ldcg(src + i);
-    }
-    for (int i = lane + 32 * kRegStage; i < static_cast<int>(N >> 2); i += 32) cp_async16(staged + 4 * i, src + i);
-  }
-  int64_t wraw = 0;
-  float wwv = 0.f;
-  if (lane < W) {
-    wraw = ld_index(st.write_indices, row * W + lane, idx64);
-    wwv = ld1_rt(st.write_weights, row * W + lane, adt);
-  }
+// A token's raw routes, loaded into registers (lane w: write slot w; lane l:
+// read slots l, l+32, ...) before anything depends on them.
+template <int RC>
+struct RouteRaw {
+  int64_t wraw;
+  float wwv;
   int64_t rraw[RC];
   float rwv[RC];
+};
+
+template <int RC>
+__device__ __forceinline__ void load_route_raw(RouteRaw<RC>& q, const cow_step& st, int64_t row, int W, int R,
+                                               int idx64, int adt, int lane) {
+  q.wraw = 0;
+  q.wwv = 0.f;
+  if (lane < W) {
+    q.wraw = ld_index(st.write_indices, row * W + lane, idx64);
+    q.wwv = ld1_rt(st.write_weights, row * W + lane, adt);
+  }
 #pragma unroll
   for (int c = 0; c < RC; ++c) {
     const int r = c * 32 + lane;
-    rraw[c] = 0;
-    rwv[c] = 0.f;
+    q.rraw[c] = 0;
+    q.rwv[c] = 0.f;
     if (r < R) {
-      rraw[c] = ld_index(st.read_indices, row * R + r, idx64);
-      rwv[c] = ld1_rt(st.read_weights, row * R + r, adt);
+      q.rraw[c] = ld_index(st.read_indices, row * R + r, idx64);
+      q.rwv[c] = ld1_rt(st.read_weights, row * R + r, adt);
     }
   }
-  const bool wok = lane < W && wraw >= 0 && wraw < N;
+}
+
+// Validate raw routes, look their slots up in the map (`mrow`: the bank's
+// dense map row, global or staged; `table`: its hashed table when log_t > 0)
+// and write the warp's metadata.  Returns a warp-uniform "bad" flag (an index
+// out of range or a repeated write address); `first_mask` has bit w set for
+// first touches.
+template <bool kDense, int RC, class M>
+__device__ __forceinline__ bool finish_routes(M& sm, const RouteRaw<RC>& q, const int32_t* mrow,
+                                              const unsigned long long* table, int log_t, int64_t N, int W, int R,
+                                              int lane, unsigned& first_mask, int& error_bits) {
+  const bool wok = lane < W && q.wraw >= 0 && q.wraw < N;
   bool bad = lane < W && !wok;
-  const int wi = wok ? static_cast<int>(wraw) : 0;
-  const int32_t* mrow = map + map_row * N;
-  if (!kDense && staged != nullptr) {
-#pragma unroll
-    for (int k = 0; k < kRegStage; ++k) {
-      const int i = lane + 32 * k;
-      if (i < static_cast<int>(N >> 2)) reinterpret_cast<int4*>(staged)[i] = mtmp[k];
-    }
-    if (N > 128 * kRegStage) cp_async_wait_all();
-    __syncwarp();
-    mrow = staged;
-  }
+  const int wi = wok ? static_cast<int>(q.wraw) : 0;
   int wp = -1;
   if (!kDense && lane < W) wp = log_t ? hash_find(table, log_t, wi) : mrow[wi];
   int ri[RC], rp[RC];
 #pragma unroll
   for (int c = 0; c < RC; ++c) {
     const int r = c * 32 + lane;
-    const bool ok = rraw[c] >= 0 && rraw[c] < N;
-    ri[c] = ok ? static_cast<int>(rraw[c]) : 0;
+    const bool ok = q.rraw[c] >= 0 && q.rraw[c] < N;
+    ri[c] = ok ? static_cast<int>(q.rraw[c]) : 0;
     rp[c] = -1;
     if (r < R) {
       bad |= !ok;
@@ -480,7 +470,7 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
   first_mask = __ballot_sync(kFull, lane < W && wp < 0 && !kDense);
   sm.widx[lane] = lane < W ? wi : -1;
   sm.wphys[lane] = wp;
-  sm.ww[lane] = wwv;
+  sm.ww[lane] = q.wwv;
   sm.fwt[lane] = 0.f;
   __syncwarp();
   // Reads of a slot written this step see the updated row (read-after-write,
@@ -503,8 +493,8 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
       const int fw = fwv[c];
       sm.ridx[r] = ri[c];
       sm.rsrc[r] = fw >= 0 ? -(fw + 2) : (rp[c] >= 0 ? rp[c] : -1);
-      sm.rw[r] = rwv[c];
-      if (fw >= 0) atomicAdd(&sm.fwt[fw], rwv[c]);
+      sm.rw[r] = q.rwv[c];
+      if (fw >= 0) atomicAdd(&sm.fwt[fw], q.rwv[c]);
     }
   }
   const bool any_dup = __any_sync(kFull, dup);
@@ -512,6 +502,43 @@ __device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int
   error_bits = (any_dup ? COW_ST_DUPLICATE_WRITE : 0) | (any_oob ? COW_ST_INDEX_RANGE : 0);
   __syncwarp();
   return any_dup || any_oob;
+}
+
+template <bool kDense, int RC, class M>
+__device__ __forceinline__ bool load_routes(M& sm, const cow_step& st, const int32_t* map,
+                                            int64_t row, int64_t map_row, int64_t N, int W, int R,
+                                            int idx64, int adt, int lane, unsigned& first_mask,
+                                            int& error_bits, int32_t* staged = nullptr, int log_t = 0) {
+  // Hashed maps: `map` points at the pool's [banks, 2^log_t] uint64 tables.
+  const unsigned long long* table =
+      log_t ? reinterpret_cast<const unsigned long long*>(map) + (map_row << log_t) : nullptr;
+  // The first 256 map entries come through registers (their latency is the
+  // route loads' latency), any further ones through cp.async.
+  constexpr int kRegStage = 2;
+  int4 mtmp[kRegStage];
+  if (!kDense && staged != nullptr) {
+    const int4* src = reinterpret_cast<const int4*>(map + map_row * N);
+#pragma unroll
+    for (int k = 0; k < kRegStage; ++k) {
+      const int i = lane + 32 * k;
+      if (i < static_cast<int>(N >> 2)) mtmp[k] = __ldcg(src + i);
+    }
+    for (int i = lane + 32 * kRegStage; i < static_cast<int>(N >> 2); i += 32) cp_async16(staged + 4 * i, src + i);
+  }
+  RouteRaw<RC> q;
+  load_route_raw<RC>(q, st, row, W, R, idx64, adt, lane);
+  const int32_t* mrow = map + map_row * N;
+  if (!kDense && staged != nullptr) {
+#pragma unroll
+    for (int k = 0; k < kRegStage; ++k) {
+      const int i = lane + 32 * k;
+      if (i < static_cast<int>(N >> 2)) reinterpret_cast<int4*>(staged)[i] = mtmp[k];
+    }
+    if (N > 128 * kRegStage) cp_async_wait_all();
+    __syncwarp();
+    mrow = staged;
+  }
+  return finish_routes<kDense, RC>(sm, q, mrow, table, log_t, N, W, R, lane, first_mask, error_bits);
 }
 
 // Gated-delta update of the W write rows (allocator.py:1489-1501): the rows

@@ -26,10 +26,35 @@ struct PrefillLaunch {
   int32_t layers, width, writes, reads, idx64, act_dt;
 };
 
+// One token's gates and value row.
+template <int CH>
+struct PrefillToken {
+  float fl, in_g, er_g;
+  float4 val[CH];
+};
+
+template <int CH>
+__device__ __forceinline__ void load_prefill_token(PrefillToken<CH>& k, const cow_step& st, int64_t row, int D,
+                                                   int adt, int lane) {
+  k.fl = ld1_rt(st.forget_log_gate, row, adt);
+  k.in_g = ld1_rt(st.input_gate, row, adt);
+  k.er_g = ld1_rt(st.erase_gate, row, adt);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    k.val[c] = col < D ? ld4_rt(st.values, row * D + col, adt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// One warp walks one bank's T tokens.  The map is fixed during the walk (all
+// written slots were placed beforehand), so only the row contents carry the
+// token-to-token dependence: token t+1's routes, gates and values are loaded
+// a token ahead and its map lookups run while token t's rows are in flight,
+// leaving one dependent round trip (the rows) per token.
 template <int SDT, int CH, int WMAX, int RC>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_prefill_kernel(const __grid_constant__ PrefillLaunch P) {
-  __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta];
+  __shared__ WarpMetaT<32 * RC> s_meta[kBanksPerCta][2];  // per warp: metadata of tokens t and t+1
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int l = 0;
@@ -39,7 +64,6 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   if (bank >= Ly.banks) return;
   const int D = P.width, W = P.writes, R = P.reads;
   const int64_t N = P.slots, T = P.time;
-  auto& sm = s_meta[warp];
   const int64_t tmpl = Ly.templates[bank];
   if (tmpl < 0 || tmpl >= Ly.template_count) {
     if (lane == 0) atomicOr(Ly.status, COW_ST_TEMPLATE_RANGE);
@@ -49,31 +73,32 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
   const cow_step& st = Ly.step;
   const float* m0 = Ly.m0;
   void* slab = Ly.slab;
-  for (int64_t t = 0; t < T; ++t) {
-    // Token t of bank b is row b*T + t of every [banks,T,...] input.  The map
-    // is fixed during the walk (all written slots were placed beforehand), so
-    // only the row contents carry the token-to-token dependence.
-    const int64_t row = bank * T + t;
-    const float fl = ld1_rt(st.forget_log_gate, row, P.act_dt);
-    const float in_g = ld1_rt(st.input_gate, row, P.act_dt);
-    const float er_g = ld1_rt(st.erase_gate, row, P.act_dt);
-    float4 val[CH];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      val[c] = col < D ? ld4_rt(st.values, row * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+  const int32_t* mrow = Ly.map + bank * N;
+  // Token t of bank b is row b*T + t of every [banks,T,...] input.
+  RouteRaw<RC> raw;
+  PrefillToken<CH> cur, next;
+  load_route_raw<RC>(raw, st, bank * T, W, R, P.idx64, P.act_dt, lane);
+  load_prefill_token<CH>(cur, st, bank * T, D, P.act_dt, lane);
+  {
     unsigned first_mask;
     int route_bits;
-    const bool bad = load_routes<false, RC>(sm, st, Ly.map, row, bank, N, W, R, P.idx64, P.act_dt, lane,
-                                            first_mask, route_bits);
+    const bool bad = finish_routes<false, RC>(s_meta[warp][0], raw, mrow, nullptr, 0, N, W, R, lane, first_mask,
+                                              route_bits);
     // Every written slot was placed before the walk, so an unmapped write
     // slot means the mark pass and the routes disagree.
     if (bad || first_mask != 0u) {
       if (lane == 0) atomicOr(Ly.status, route_bits ? route_bits : COW_ST_INDEX_RANGE);
       return;
     }
-    const float alpha = expf(fl);
+  }
+  if (T > 1) {
+    load_route_raw<RC>(raw, st, bank * T + 1, W, R, P.idx64, P.act_dt, lane);
+    load_prefill_token<CH>(next, st, bank * T + 1, D, P.act_dt, lane);
+  }
+  for (int64_t t = 0; t < T; ++t) {
+    const int64_t row = bank * T + t;
+    auto& sm = s_meta[warp][t & 1];
+    // This token's rows: write rows and the first read group in flight ...
     float4 upd[WMAX][CH];
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
@@ -90,7 +115,22 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     float4 v0[ReadGroup<CH>::G][CH];
     float wt0[ReadGroup<CH>::G];
     load_read_group<SDT, CH>(v0, wt0, sm, 0, R, slab, 0, m0, m0_base, lane, D);
-    gated_delta<SDT, CH, WMAX>(upd, sm, W, alpha, in_g, er_g, val, lane, D);
+    // ... while the next token's map lookups resolve, and the token after
+    // that has its routes, gates and value row requested.
+    int next_bits = 0;
+    bool next_bad = false;
+    if (t + 1 < T) {
+      unsigned first_mask;
+      next_bad = finish_routes<false, RC>(s_meta[warp][(t + 1) & 1], raw, mrow, nullptr, 0, N, W, R, lane,
+                                          first_mask, next_bits);
+      next_bad = next_bad || first_mask != 0u;
+    }
+    PrefillToken<CH> after = next;
+    if (t + 2 < T) {
+      load_route_raw<RC>(raw, st, row + 2, W, R, P.idx64, P.act_dt, lane);
+      load_prefill_token<CH>(after, st, row + 2, D, P.act_dt, lane);
+    }
+    gated_delta<SDT, CH, WMAX>(upd, sm, W, expf(cur.fl), cur.in_g, cur.er_g, cur.val, lane, D);
 #pragma unroll
     for (int w = 0; w < WMAX; ++w) {
       if (w < W) {
@@ -114,6 +154,12 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
       if (col < D) st4_rt(st.output, row * D + col, acc[c], P.act_dt);
     }
     __syncwarp();
+    if (next_bad) {
+      if (lane == 0) atomicOr(Ly.status, next_bits ? next_bits : COW_ST_INDEX_RANGE);
+      return;
+    }
+    cur = next;
+    next = after;
   }
 }
 
