@@ -317,7 +317,9 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 // and copied from M0 with weight 0, so the accumulation has no branches).
 // The kSplit partial readouts meet in shared memory.  Warp 0 alone takes
 // part in the pool's scan and close and places the first touches, exactly as
-// cow_decode_kernel does (same flags, same epoch, same pop order).
+// cow_decode_kernel does (same flags, same epoch, same pop order).  Its
+// activations are f32 and its indices int64 at compile time (the common
+// serving case), which removes the per-load dtype dispatch.
 constexpr int kSplit = 4;
 constexpr int kSplitRows = 32 / kSplit;  // read rows per warp (R <= 32)
 
@@ -350,14 +352,14 @@ __global__ void __launch_bounds__(kSplit * 32)
     old_free = *reinterpret_cast<volatile int32_t*>(L.free_count);
   }
   const int64_t tmpl = L.templates[bank];
-  const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
-  const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
-  const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  const float fl = ld1_rt(L.step.forget_log_gate, bank, COW_F32);
+  const float in_g = ld1_rt(L.step.input_gate, bank, COW_F32);
+  const float er_g = ld1_rt(L.step.erase_gate, bank, COW_F32);
   float4 val[1];
-  val[0] = lane * 4 < D ? ld4_rt(L.step.values, bank * D + lane * 4, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  val[0] = lane * 4 < D ? ld4_rt(L.step.values, bank * D + lane * 4, COW_F32) : make_float4(0.f, 0.f, 0.f, 0.f);
   unsigned first_mask = 0;
   int route_bits = 0;
-  const bool bad_route = load_routes<false, 1>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
+  const bool bad_route = load_routes<false, 1>(sm, L.step, L.map, bank, bank, N, W, R, 1, COW_F32, lane,
                                                first_mask, route_bits, s_mapw);
   const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
   const bool bad = bad_route || bad_tmpl;
@@ -464,7 +466,7 @@ __global__ void __launch_bounds__(kSplit * 32)
     const float4 x = s_part[j][lane];
     sum = make_float4(sum.x + x.x, sum.y + x.y, sum.z + x.z, sum.w + x.w);
   }
-  if (lane * 4 < D) st4_rt(L.step.output, bank * D + lane * 4, sum, P.act_dt);
+  if (lane * 4 < D) st4_rt(L.step.output, bank * D + lane * 4, sum, COW_F32);
 
   // Place the first touches: pop free_rows[old_free - 1 - rank].
   int newp = -1;
@@ -849,7 +851,7 @@ int decode_step_impl(const cow_pool* pools, const cow_step* steps, int32_t layer
       fits = fits && pools[l].banks < (int64_t(1) << (32 - kCloseShift)) &&
              pools[l].banks * writes < (int64_t(1) << kCloseShift);
     P.counter_close = fits ? 1 : 0;
-    if (fits && allow_split && split_enabled() && sdt == COW_F32 && ch == 1 && rv == 0 && P.stage_map && width <= 128 &&
+    if (fits && allow_split && split_enabled() && sdt == COW_F32 && act_dtype == COW_F32 && index_dtype == COW_I64 && ch == 1 && rv == 0 && P.stage_map && width <= 128 &&
         total_banks <= kSplitMaxBanks) {
       // Small launch: one bank per block of kSplit warps (cow_decode_split_kernel).
       const size_t split_smem = static_cast<size_t>(kSplit) * max_slots * sizeof(int32_t);
