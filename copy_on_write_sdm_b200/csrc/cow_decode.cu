@@ -36,9 +36,13 @@ namespace {
 // below it (the host enables this when both fields fit).
 constexpr int kCloseShift = 18;
 
-template <int SDT, int CH, int WMAX, int RC>
+// kF32I64: activations f32 and indices int64 at compile time (the common
+// serving case; the launcher picks it for the f32 / W <= 4 / R <= 32 variant).
+template <int SDT, int CH, int WMAX, int RC, bool kF32I64 = false>
 __global__ void __launch_bounds__(kBanksPerCta * 32)
     cow_decode_kernel(const __grid_constant__ DecodeLaunch P) {
+  const int act_dt = kF32I64 ? COW_F32 : P.act_dt;
+  const int idx64 = kF32I64 ? 1 : P.idx64;
   // Common shapes (f32 rows, R <= 32, width <= 128) copy their read rows into
   // shared memory with bulk copies (one per row, on a per-warp mbarrier)
   // rather than holding them in registers.
@@ -90,18 +94,18 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
     }
   }
   const int64_t tmpl = L.templates[bank];
-  const float fl = ld1_rt(L.step.forget_log_gate, bank, P.act_dt);
-  const float in_g = ld1_rt(L.step.input_gate, bank, P.act_dt);
-  const float er_g = ld1_rt(L.step.erase_gate, bank, P.act_dt);
+  const float fl = ld1_rt(L.step.forget_log_gate, bank, act_dt);
+  const float in_g = ld1_rt(L.step.input_gate, bank, act_dt);
+  const float er_g = ld1_rt(L.step.erase_gate, bank, act_dt);
   float4 val[CH];
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int col = (c * 32 + lane) * 4;
-    val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, P.act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
+    val[c] = col < D ? ld4_rt(L.step.values, bank * D + col, act_dt) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   unsigned first_mask = 0;
   int route_bits = 0;
-  const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, P.idx64, P.act_dt, lane,
+  const bool bad_route = load_routes<false, RC>(sm, L.step, L.map, bank, bank, N, W, R, idx64, act_dt, lane,
                                                 first_mask, route_bits, P.stage_map ? s_mapw : nullptr, L.log_t);
   const bool bad_tmpl = tmpl < 0 || tmpl >= L.template_count;
   const bool bad = bad_route || bad_tmpl;
@@ -262,7 +266,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int col = (c * 32 + lane) * 4;
-    if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], P.act_dt);
+    if (col < D) st4_rt(L.step.output, bank * D + col, acc[c], act_dt);
   }
 
   // Place the first touches: pop free_rows[old_free - 1 - rank].
@@ -792,6 +796,8 @@ int decode_step_impl(const cow_pool* pools, const cow_step* steps, int32_t layer
   const int ch = width_chunks(width);
   const int rv = route_variant(writes, reads);
   COW_SELECT_KERNEL(cow_decode_kernel, sdt, ch, rv, fn);
+  if (sdt == COW_F32 && ch == 1 && rv == 0 && act_dtype == COW_F32 && index_dtype == COW_I64)
+    fn = cow_decode_kernel<COW_F32, 1, 4, 1, true>;
   // Latency-bound launches (at most ~16 warps per SM) with small tables stage
   // each bank's map row in shared memory: N*4 extra bytes per bank buy one
   // dependent memory round trip less.
