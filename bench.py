@@ -400,6 +400,12 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     # readouts back to pinned host memory (one copy).
     from copy_on_write_sdm_b200 import DecodeSession
 
+    # Capacity is proven for every end-to-end step up front, as for the timed
+    # device trace (growing the slab by whole quanta now): each step still runs
+    # the per-step proof (one decrement per pool), but no step has to
+    # reconcile with the device's free count in the middle of the stream.
+    for st in states:
+        st.prepare_step_capacity(banks * WRITES * (4 * K + 4 * Wm))
     sess = DecodeSession(states, writes=WRITES, reads=READS)
     host_steps = torch.empty(K, sess.step_bytes, dtype=torch.uint8, pin_memory=True)
     for i, s in enumerate(range(Wm, Wm + K)):
@@ -1153,7 +1159,10 @@ def config_block(world: int) -> dict:
             "growth_quantum_rows": max(16, BATCH * HEADS * WRITES * QUANTUM_STEPS),
             "parallelism": f"requests sharded, {BATCH} per GPU x {world} GPU(s), no collective",
             "l2": "flushed (256 MiB write) before every timed step, inside one CUDA graph; each step timed "
-                  "by its own device event pair"}
+                  "by its own device event pair",
+            "capacity_proof": "timed device steps and end-to-end steps are proven up front "
+                              "(prepare_step_capacity for all of them before timing); the per-step proof still "
+                              "runs in every end-to-end step"}
 
 
 _RESULT_OUT = None
