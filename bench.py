@@ -56,6 +56,7 @@ METRIC = "packed-SDM decode tokens/s at batch 64, 1/2/4/8 B200; % of HBM rooflin
 LAYERS, SLOTS, WIDTH, HEADS, READS, WRITES = 7, 256, 128, 1, 16, 4
 BATCH, PREFIX, QUANTUM_STEPS = 64, 2048, 4
 L2_FLUSH_BYTES = 256 << 20
+E2E_WARMUP = 64  # untimed host-to-host steps before each end-to-end leg
 # DRAM traffic per launch of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum); the capture commands and
 # figures are in profiles/.
@@ -405,7 +406,7 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     # the per-step proof (one decrement per pool), but no step has to
     # reconcile with the device's free count in the middle of the stream.
     for st in states:
-        st.prepare_step_capacity(banks * WRITES * (4 * K + 4 * Wm))
+        st.prepare_step_capacity(banks * WRITES * (4 * K + 4 * E2E_WARMUP))
     sess = DecodeSession(states, writes=WRITES, reads=READS)
     host_steps = torch.empty(K, sess.step_bytes, dtype=torch.uint8, pin_memory=True)
     for i, s in enumerate(range(Wm, Wm + K)):
@@ -431,8 +432,8 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     # The same through step_host_pipelined: step k+1's input copy and step
     # k-1's readout copy overlap step k's decode (three streams, in-order decode).
     with torch.cuda.stream(stream):
-        for i in range(min(Wm, K)):  # warm-up: creates the side streams and buffers
-            sess.step_host_pipelined(host_steps[i])
+        for i in range(E2E_WARMUP):  # warm-up: side streams, buffers, a steady host/device rhythm
+            sess.step_host_pipelined(host_steps[i % K])
     torch.cuda.synchronize(device)
     barrier()
     torch.cuda.synchronize(device)
@@ -450,8 +451,8 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     # pinned host bytes and writes its readouts to pinned host memory itself
     # (zero-copy over PCIe): one launch per token, no copy calls.
     with torch.cuda.stream(stream):
-        for i in range(min(Wm, K)):
-            sess.step_host_mapped(host_steps[i])
+        for i in range(E2E_WARMUP):
+            sess.step_host_mapped(host_steps[i % K])
     torch.cuda.synchronize(device)
     barrier()
     torch.cuda.synchronize(device)

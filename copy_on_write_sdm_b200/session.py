@@ -19,6 +19,10 @@ launch itself at serving batch sizes.  ``DecodeSession`` does that work once:
   k decodes and step k-1's readouts come back (the decode steps themselves
   stay in order on the compute stream).
 
+The per-step methods issue no autograd-tracked torch operations (only C
+calls and host arithmetic), so they skip ``torch.no_grad()``, whose context
+costs about 4 us per call -- as much as the rest of a step's host work.
+
 Semantics per pool are exactly ``packed_sdm_cow_step`` with
 ``validate_routes=False, collect_diagnostics=False`` (the decode path of
 inference.py:538-566); every pool must have the same bank count, width and
@@ -238,7 +242,6 @@ class DecodeSession:
     def _stream_handle(self) -> int:
         return _current_raw_stream(self._device_index)
 
-    @torch.no_grad()
     def step(self, *, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """One decode token for every bank of every pool; returns ``outputs`` ``[L, B, D]`` (device)."""
         current = self._stream_handle()
@@ -285,7 +288,6 @@ class DecodeSession:
             }
         return self._pipe
 
-    @torch.no_grad()
     def step_host_pipelined(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
         """Host-to-host step overlapped with its neighbours (``cow_decode_step_host_piped``).
 
@@ -341,7 +343,6 @@ class DecodeSession:
         except Exception:
             pass
 
-    @torch.no_grad()
     def step_host_mapped(self, host_step: torch.Tensor) -> tuple[torch.Tensor, torch.cuda.Event]:
         """Host-to-host step with no copy calls (``cow_decode_step_host_mapped``).
 
@@ -373,7 +374,6 @@ class DecodeSession:
             _lib.check(rc, "cow_decode_step_host_mapped")
         return out, pipe["events"][b][2]
 
-    @torch.no_grad()
     def step_host(self, host_step: torch.Tensor | None = None) -> torch.Tensor:
         """Host-to-host step: copy ``host_step`` (pinned bytes in the ``inputs`` layout,
         default ``host_inputs``) to the device, decode, copy the readouts back into
