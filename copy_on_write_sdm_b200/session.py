@@ -14,7 +14,7 @@ launch itself at serving batch sizes.  ``DecodeSession`` does that work once:
 * ``step()`` runs the reference's per-step capacity proof
   (``prepare_step_capacity``, allocator.py:746-774) for every pool, then one
   fused ``cow_decode_step`` launch for all pools;
-* ``step_host_pipelined()`` streams host steps through two input and two
+* ``step_host_pipelined()`` streams host steps through PIPE_DEPTH input and
   output buffers on three streams, so step k+1's inputs cross PCIe while step
   k decodes and step k-1's readouts come back (the decode steps themselves
   stay in order on the compute stream).
@@ -252,25 +252,34 @@ class DecodeSession:
                                              self._scratch.numel(), handle), "cow_decode_step")
         return self.outputs
 
+    # Buffer pairs the host-to-host pipelines rotate through: a step's input
+    # copy waits only for the decode that read its buffer PIPE_DEPTH steps
+    # earlier, so copies of several neighbouring steps can be in flight.
+    PIPE_DEPTH = 4
+
     def _pipeline(self):
         if self._pipe is None:
-            alt = torch.empty_like(self.inputs)
-            views = [self._views(alt, per) for per in self._offsets]
-            out_alt = torch.empty_like(self.outputs)
-            steps_alt = (_lib.CowStep * len(self.pools))(*[
-                _lib.CowStep(v["write_indices"].data_ptr(), v["write_weights"].data_ptr(), v["values"].data_ptr(),
-                             v["input_gate"].data_ptr(), v["input_gate"].data_ptr(), v["forget_log_gate"].data_ptr(),
-                             v["read_indices"].data_ptr(), v["read_weights"].data_ptr(), out_alt[l].data_ptr(), None)
-                for l, v in enumerate(views)])
+            n = self.PIPE_DEPTH
+            inputs = [self.inputs] + [torch.empty_like(self.inputs) for _ in range(n - 1)]
+            outputs = [self.outputs] + [torch.empty_like(self.outputs) for _ in range(n - 1)]
+            steps = [self._steps]
+            for b in range(1, n):
+                views = [self._views(inputs[b], per) for per in self._offsets]
+                steps.append((_lib.CowStep * len(self.pools))(*[
+                    _lib.CowStep(v["write_indices"].data_ptr(), v["write_weights"].data_ptr(),
+                                 v["values"].data_ptr(), v["input_gate"].data_ptr(), v["input_gate"].data_ptr(),
+                                 v["forget_log_gate"].data_ptr(), v["read_indices"].data_ptr(),
+                                 v["read_weights"].data_ptr(), outputs[b][l].data_ptr(), None)
+                    for l, v in enumerate(views)]))
             pinned = self.host_outputs.is_pinned()
             h2d, d2h = torch.cuda.Stream(self.device), torch.cuda.Stream(self.device)
-            events = [[torch.cuda.Event() for _ in range(3)] for _ in range(2)]
-            for pair in events:  # materialise the handles; a recorded-then-idle event never blocks
-                for ev in pair:
+            events = [[torch.cuda.Event() for _ in range(3)] for _ in range(n)]
+            for group in events:  # materialise the handles; a recorded-then-idle event never blocks
+                for ev in group:
                     ev.record(h2d)
             torch.cuda.synchronize(self.device)
-            host_outputs = (self.host_outputs, torch.empty_like(self.host_outputs, pin_memory=pinned))
-            inputs, outputs, steps = (self.inputs, alt), (self.outputs, out_alt), (self._steps, steps_alt)
+            host_outputs = [self.host_outputs] + [torch.empty_like(self.host_outputs, pin_memory=pinned)
+                                                  for _ in range(n - 1)]
             # one descriptor per buffer pair: every argument of the overlapped step
             # but the host input bytes and the compute stream
             descs = tuple(_lib.CowHostPipeline(
@@ -278,12 +287,12 @@ class DecodeSession:
                 _lib.I64, self._act_code, 0, self._scratch.data_ptr(), self._scratch.numel(), inputs[b].data_ptr(),
                 self.step_bytes, host_outputs[b].data_ptr(), outputs[b].data_ptr(), self._out_bytes,
                 h2d.cuda_stream, d2h.cuda_stream, events[b][0].cuda_event, events[b][1].cuda_event,
-                events[b][2].cuda_event) for b in range(2))
+                events[b][2].cuda_event) for b in range(n))
             for t in host_outputs:
                 self._register(t)
             self._pipe = {
                 "inputs": inputs, "outputs": outputs, "steps": steps, "host_outputs": host_outputs,
-                "h2d": h2d, "d2h": d2h, "events": events, "k": 0, "descs": descs,
+                "h2d": h2d, "d2h": d2h, "events": events, "k": 0, "descs": descs, "depth": n,
                 "desc_ptrs": tuple(ctypes.addressof(d) for d in descs), "desc_pools": None,
             }
         return self._pipe
@@ -294,14 +303,14 @@ class DecodeSession:
         ``host_step`` holds the step's pinned input bytes (``inputs`` layout).
         Returns the pinned host buffer that will hold this step's readouts
         ``[L, B, D]`` and the event that marks their arrival; the buffer is
-        reused two steps later.  Steps decode strictly in call order on the
+        reused PIPE_DEPTH steps later.  Steps decode strictly in call order on the
         current stream; the copies run on two side streams.
         """
         if host_step.nbytes != self.step_bytes or host_step.dtype is not torch.uint8 \
                 or host_step.is_cuda or not host_step.is_contiguous():
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
         pipe = self._pipe if self._pipe is not None else self._pipeline()
-        b = pipe["k"] & 1
+        b = pipe["k"] % pipe["depth"]
         pipe["k"] += 1
         self._prove()
         pools = self._pools()
@@ -350,7 +359,7 @@ class DecodeSession:
         layout) over PCIe and writes the readouts straight into a pinned host
         buffer: one kernel launch per token.  Returns that buffer ``[L, B, D]``
         and the event that marks the readouts' arrival; the buffer is reused
-        two steps later, and ``host_step`` must stay untouched until the event
+        PIPE_DEPTH steps later, and ``host_step`` must stay untouched until the event
         has completed.  Steps decode in call order on the current stream.
         """
         if host_step.nbytes != self.step_bytes or host_step.dtype is not torch.uint8 \
@@ -358,7 +367,7 @@ class DecodeSession:
             raise ValueError(f"host step must be {self.step_bytes} contiguous uint8 bytes on the host")
         ptr = host_step.data_ptr()
         pipe = self._pipe if self._pipe is not None else self._pipeline()
-        b = pipe["k"] & 1
+        b = pipe["k"] % pipe["depth"]
         pipe["k"] += 1
         self._prove()
         pools = self._pools()
