@@ -287,6 +287,46 @@ def model_lifecycle(name, *, seed=0):
     _save(name, out, seed)
 
 
+def model_config2(name, *, seed=2):
+    """Configuration-2-shaped reference model (vocab 50,257, layout BBBBBBBA,
+    width 128, N=256, H=1, top-16/top-4) with seeded weights shared with the
+    test (``config2_weights.py``): prefill, then decode steps.  Logits are
+    stored for a seeded subset of 4,096 vocabulary columns plus every row's
+    argmax (the full logits would be 200 KB per row)."""
+    from copy_on_write_sdm.model import LanguageModel
+
+    sys.path.insert(0, HERE)
+    from config2_weights import VOCAB, model_kwargs, seeded_params
+
+    model = LanguageModel(**model_kwargs(), activation_dtype=torch.float32)
+    shapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in seeded_params(shapes, seed).items()}, strict=True)
+    model.eval()
+    g = torch.Generator().manual_seed(seed + 1)
+    cols = torch.randperm(VOCAB, generator=g)[:4096].sort().values
+    out = {"columns": _np(cols)}
+
+    def keep(prefix, logits):
+        flat = logits.reshape(-1, VOCAB)
+        out[prefix + "_logits"] = _np(flat[:, cols])
+        out[prefix + "_argmax"] = _np(flat.argmax(-1))
+
+    prefix = torch.randint(VOCAB, (2, 12), generator=g)
+    out["prefix"] = _np(prefix)
+    with torch.no_grad():
+        logits, state = model.prefill(prefix, capacity=24, sdm_growth_quantum_rows=64)
+        keep("prefill", logits[:, -1:])
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"prefill_l{i}_", st, out)
+        steps = torch.randint(VOCAB, (4, 2, 1), generator=g)
+        out["decode_ids"] = _np(steps)
+        for t in range(4):
+            keep(f"decode{t}", model.decode(steps[t], state))
+        for i, st in enumerate(state.sdm_states):
+            _snapshot(f"decoded_l{i}_", st, out)
+    _save(name, out, seed)
+
+
 def main() -> None:
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     # Configuration 1: H=1, N=256, D=128, top-16/top-4, seed 0, B=1, prefix 16 + 32 decode.
@@ -301,6 +341,7 @@ def main() -> None:
     lifecycle_trace("lifecycle")
     prefill_handoff("prefill_handoff")
     model_lifecycle("model_lifecycle")
+    model_config2("model_config2")
 
 
 if __name__ == "__main__":
