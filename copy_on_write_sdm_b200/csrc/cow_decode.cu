@@ -529,16 +529,19 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
   // The decode pass may start now: it waits for this grid only where it reads
   // the prefixes.
   asm volatile("griddepcontrol.launch_dependents;");
+  int blk;
+  if (P.dynamic_tiles) {
+    if (tid == 0) s_blk = static_cast<int>(atomicAdd(&hdr[0], 1u));
+    __syncthreads();
+    blk = s_blk;
+  } else {
+    blk = static_cast<int>(blockIdx.x) - L.count_block_begin;
+  }
   if (tid == 0) {
-    s_blk = P.dynamic_tiles ? static_cast<int>(atomicAdd(&hdr[0], 1u))
-                            : static_cast<int>(blockIdx.x) - L.count_block_begin;
     s_epoch = *reinterpret_cast<volatile uint32_t*>(&P.header[kEpochWord]);
     s_old = *reinterpret_cast<volatile int32_t*>(L.free_count);
   }
   s_bad[tid] = 0;
-  __syncthreads();
-  const int blk = s_blk;
-  const uint32_t epoch = s_epoch;
   const int64_t bank0 = static_cast<int64_t>(blk) * kCountThreads;
   const int64_t bank = bank0 + tid;
   const int64_t N = L.slots;
@@ -546,40 +549,58 @@ __global__ void __launch_bounds__(kCountThreads) cow_count_kernel(const __grid_c
   const int nb = static_cast<int>(L.banks - bank0 < kCountThreads ? L.banks - bank0 : kCountThreads);
   const cow_step& st = L.step;
   // Route indices of the block's banks are contiguous: the whole block reads
-  // them with consecutive threads on consecutive elements.
-  // Loads of kCountUnroll elements go out before any of them is checked.
-  for (int e0 = 0; e0 < nb * W; e0 += kCountThreads * kCountUnroll) {
-    int64_t raw[kCountUnroll];
+  // them with consecutive threads on consecutive elements.  The first round of
+  // write and read indices and the templates go out together, before anything
+  // waits (one memory round trip for the common W <= 8, R <= 16).
+  constexpr int kReadUnroll = 16;
+  int64_t wraw[kCountUnroll], rraw[kReadUnroll];
 #pragma unroll
-    for (int u = 0; u < kCountUnroll; ++u) {
-      const int e = e0 + u * kCountThreads + tid;
-      raw[u] = e < nb * W ? ld_index(st.write_indices, bank0 * W + e, P.idx64) : 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kCountUnroll; ++u) {
-      const int e = e0 + u * kCountThreads + tid;
-      if (e < nb * W) {
-        const bool ok = raw[u] >= 0 && raw[u] < N;
-        s_wi[e] = ok ? static_cast<int>(raw[u]) : -1 - (e % W);  // distinct sentinels never count as repeats
-        if (!ok) s_bad[e / W] = 1;
-      }
-    }
+  for (int u = 0; u < kCountUnroll; ++u) {
+    const int e = u * kCountThreads + tid;
+    wraw[u] = e < nb * W ? ld_index(st.write_indices, bank0 * W + e, P.idx64) : 0;
   }
-  for (int e0 = 0; e0 < nb * R; e0 += kCountThreads * kCountUnroll) {
-    int64_t raw[kCountUnroll];
 #pragma unroll
-    for (int u = 0; u < kCountUnroll; ++u) {
-      const int e = e0 + u * kCountThreads + tid;
-      raw[u] = e < nb * R ? ld_index(st.read_indices, bank0 * R + e, P.idx64) : 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kCountUnroll; ++u) {
-      const int e = e0 + u * kCountThreads + tid;
-      if (e < nb * R && (raw[u] < 0 || raw[u] >= N)) s_bad[e / R] = 1;
-    }
+  for (int u = 0; u < kReadUnroll; ++u) {
+    const int e = u * kCountThreads + tid;
+    rraw[u] = e < nb * R ? ld_index(st.read_indices, bank0 * R + e, P.idx64) : 0;
   }
   int64_t tmpl = 0;
   if (tid < nb) tmpl = L.templates[bank];
+  __syncthreads();  // s_bad cleared, epoch and free count read
+  const uint32_t epoch = s_epoch;
+  auto take_write = [&](int e, int64_t raw) {
+    if (e < nb * W) {
+      const bool ok = raw >= 0 && raw < N;
+      s_wi[e] = ok ? static_cast<int>(raw) : -1 - (e % W);  // distinct sentinels never count as repeats
+      if (!ok) s_bad[e / W] = 1;
+    }
+  };
+  auto take_read = [&](int e, int64_t raw) {
+    if (e < nb * R && (raw < 0 || raw >= N)) s_bad[e / R] = 1;
+  };
+#pragma unroll
+  for (int u = 0; u < kCountUnroll; ++u) take_write(u * kCountThreads + tid, wraw[u]);
+#pragma unroll
+  for (int u = 0; u < kReadUnroll; ++u) take_read(u * kCountThreads + tid, rraw[u]);
+  // Further rounds (W > 8 or R > 16 with full blocks).
+  for (int e0 = kCountThreads * kCountUnroll; e0 < nb * W; e0 += kCountThreads * kCountUnroll) {
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      wraw[u] = e < nb * W ? ld_index(st.write_indices, bank0 * W + e, P.idx64) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) take_write(e0 + u * kCountThreads + tid, wraw[u]);
+  }
+  for (int e0 = kCountThreads * kReadUnroll; e0 < nb * R; e0 += kCountThreads * kReadUnroll) {
+#pragma unroll
+    for (int u = 0; u < kReadUnroll; ++u) {
+      const int e = e0 + u * kCountThreads + tid;
+      rraw[u] = e < nb * R ? ld_index(st.read_indices, bank0 * R + e, P.idx64) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kReadUnroll; ++u) take_read(e0 + u * kCountThreads + tid, rraw[u]);
+  }
   __syncthreads();
   int count = 0;
   if (tid < nb) {
