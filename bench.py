@@ -418,51 +418,55 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     sess.register_host_steps(host_steps)
     h2d = sess.step_bytes
     d2h = sess.host_outputs.numel() * sess.host_outputs.element_size()
+    # The host-to-host legs run on the device's default stream, the stream a
+    # serving process that never creates one submits to (its runtime calls
+    # cost the host measurably less there than on a created stream).
+    host_stream = torch.cuda.default_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(device)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
+    with torch.cuda.stream(host_stream):
+        e0.record(host_stream)
         for i in range(K):
             sess.step_host(host_steps[i])
-        e1.record(stream)
+        e1.record(host_stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_serial_ms = e0.elapsed_time(e1)
     # The same through step_host_pipelined: step k+1's input copy and step
     # k-1's readout copy overlap step k's decode (three streams, in-order decode).
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(host_stream):
         for i in range(E2E_WARMUP):  # warm-up: side streams, buffers, a steady host/device rhythm
             sess.step_host_pipelined(host_steps[i % K])
     torch.cuda.synchronize(device)
     barrier()
     torch.cuda.synchronize(device)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
+    with torch.cuda.stream(host_stream):
+        e0.record(host_stream)
         last = None
         for i in range(K):
             _, last = sess.step_host_pipelined(host_steps[i])
-        stream.wait_event(last)
-        e1.record(stream)
+        host_stream.wait_event(last)
+        e1.record(host_stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
     # The same through step_host_mapped: the decode kernel reads each step's
     # pinned host bytes and writes its readouts to pinned host memory itself
     # (zero-copy over PCIe): one launch per token, no copy calls.
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(host_stream):
         for i in range(E2E_WARMUP):
             sess.step_host_mapped(host_steps[i % K])
     torch.cuda.synchronize(device)
     barrier()
     torch.cuda.synchronize(device)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
+    with torch.cuda.stream(host_stream):
+        e0.record(host_stream)
         t0 = time.perf_counter()
         for i in range(K):
             sess.step_host_mapped(host_steps[i])
         host_s = time.perf_counter() - t0
-        e1.record(stream)
+        e1.record(host_stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_mapped_ms = e0.elapsed_time(e1)
