@@ -1039,15 +1039,17 @@ int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps
   cudaStream_t cs = as_stream(compute_stream), hs = as_stream(h2d_stream), ds = as_stream(d2h_stream);
   cudaEvent_t e_h2d = static_cast<cudaEvent_t>(h2d_done), e_comp = static_cast<cudaEvent_t>(computed),
               e_d2h = static_cast<cudaEvent_t>(d2h_done);
-  // The buffers of this step were last used two steps ago: its decode read the
-  // inputs (e_comp) and its readout copy read the outputs (e_d2h).  Waiting
-  // on an event that was never recorded returns at once.
-  cudaError_t e = cudaStreamWaitEvent(hs, e_comp, 0);
+  // The buffers of this step were last used by the step that recorded this
+  // pair's events: its decode read the inputs and its readout copy, which
+  // itself waited for that decode, read the outputs.  One wait on that readout
+  // copy (e_d2h) therefore frees both buffers; the decode then waits only for
+  // this step's input copy, which follows it on the copy stream.  Waiting on
+  // an event that was never recorded returns at once.
+  cudaError_t e = cudaStreamWaitEvent(hs, e_d2h, 0);
   if (e == cudaSuccess) e = cudaMemcpyAsync(device_inputs, host_inputs, static_cast<size_t>(input_bytes),
                                             cudaMemcpyHostToDevice, hs);
   if (e == cudaSuccess) e = cudaEventRecord(e_h2d, hs);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, e_h2d, 0);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, e_d2h, 0);
   if (e != cudaSuccess) {
     cowrt::last_cuda_error = static_cast<int>(e);
     return COW_ERR_CUDA;

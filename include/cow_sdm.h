@@ -184,14 +184,15 @@ int cow_decode_step_host(const cow_pool* pools, const cow_step* steps, int32_t l
                          const void* device_outputs, int64_t output_bytes, void* stream);
 
 /* cow_decode_step_host with the copies on their own streams, for a runtime
- * that alternates two input / output buffer pairs: the input copy runs on
- * `h2d_stream` once the decode that last read `device_inputs` is done
- * (`computed`, recorded by that step), the decode on `compute_stream` after
- * the copy (`h2d_done`) and after the readout copy that last read
- * `device_outputs` (`d2h_done`), the readout copy on `d2h_stream`.  All three
- * events (cudaEvent_t) belong to this buffer pair and are recorded again
- * here.  Decode steps stay in call order on `compute_stream`; the copies of
- * neighbouring steps overlap them. */
+ * that rotates through several input / output buffer pairs: the input copy
+ * runs on `h2d_stream` once the readout copy that last read this pair's
+ * `device_outputs` is done (`d2h_done`; that copy waited for the decode that
+ * read `device_inputs`, so both buffers are free), the decode on
+ * `compute_stream` after the input copy (`h2d_done`), the readout copy on
+ * `d2h_stream` after the decode (`computed`).  All three events
+ * (cudaEvent_t) belong to this buffer pair and are recorded again here.
+ * Decode steps stay in call order on `compute_stream`; the copies of
+ * neighbouring steps overlap them.  Nine runtime calls per step. */
 int cow_decode_step_host_overlapped(const cow_pool* pools, const cow_step* steps, int32_t layers, int32_t writes,
                                     int32_t reads, int32_t index_dtype, int32_t act_dtype, void* scan_scratch,
                                     int64_t scratch_bytes, void* device_inputs, const void* host_inputs,
