@@ -139,6 +139,9 @@ _SIGNATURES = {
                                          c_int32, c_int32, c_int32, P]),
     "cow_prefill_recurrence_layers": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int64, c_int32,
                                                 c_int32, c_int32, c_int32, P]),
+    "cow_prefill_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32, c_int64, c_int32, c_int32]),
+    "cow_prefill_recurrence_layers_ws": (c_int32, [POINTER(CowPool), POINTER(CowStep), c_int32, c_int64, c_int32,
+                                                   c_int32, c_int32, c_int32, P, c_int64, P]),
     "cow_grow": (c_int32, [P, P, c_int64, P, P, c_int64, c_int64, c_int32, P, P, P]),
     "cow_grow_in_place": (c_int32, [P, c_int64, c_int64, P, P, P]),
     "cow_release": (c_int32, [POINTER(CowPool), P, c_int64, P, P, P, P]),

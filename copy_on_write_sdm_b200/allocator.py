@@ -26,6 +26,7 @@ from __future__ import annotations
 import contextlib
 import ctypes
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Any, Sequence
 
@@ -896,6 +897,10 @@ def _check_template_range(lo, hi, m0: torch.Tensor) -> None:
 
 
 _WORKSPACE: dict[int, torch.Tensor] = {}
+# The prefill walks its prefix on routes resolved beforehand by a parallel pass
+# (cow_prefill_recurrence_layers_ws); COW_PREFILL_RESOLVED=0 selects the walk
+# that resolves each token's routes itself, for comparisons.
+_PREFILL_RESOLVED = os.environ.get("COW_PREFILL_RESOLVED", "1") != "0"
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
@@ -1131,8 +1136,14 @@ def from_prefix_routes_layers(
     pools = _pool_array(states)
     _lib.check(lib.cow_pack_apply_layers(pools, n, ws.data_ptr(), ws.numel(), stream), "cow_pack_apply_layers")
     structs = (_lib.CowStep * n)(*[step.struct for step in steps])
-    _lib.check(lib.cow_prefill_recurrence_layers(pools, structs, n, time, writes, reads, idx_code, act_code,
-                                                 stream), "cow_prefill_recurrence_layers")
+    if _PREFILL_RESOLVED:
+        rws = _workspace(device, lib.cow_prefill_workspace_bytes(pools, n, time, writes, reads))
+        _lib.check(lib.cow_prefill_recurrence_layers_ws(pools, structs, n, time, writes, reads, idx_code, act_code,
+                                                        rws.data_ptr(), rws.numel(), stream),
+                   "cow_prefill_recurrence_layers_ws")
+    else:
+        _lib.check(lib.cow_prefill_recurrence_layers(pools, structs, n, time, writes, reads, idx_code, act_code,
+                                                     stream), "cow_prefill_recurrence_layers")
     # Route errors met during the walk are ValueErrors (as in the reference's
     # prefill); anything else is an invariant failure.
     vws = _workspace(device, lib.cow_validate_workspace_bytes(pools, n))

@@ -93,12 +93,28 @@ class FaithfulSDMDecodeState:
             raise AssertionError("SDM serving banks do not divide by batch")
         return state.banks // batch
 
+    def _active_host(self) -> list[bool]:
+        """``active_sequences`` as a host list, read from the device only when the
+        tensor was replaced or changed in place since this object last knew it."""
+        act = self.active_sequences
+        cached = self.__dict__.get("_active_of")
+        if cached is not None and cached[0] is act and cached[1] == act._version:
+            return cached[2]
+        host = act.tolist()
+        self.__dict__["_active_of"] = (act, act._version, host)  # holds the tensor: its identity stays unique
+        return host
+
+    def _set_active(self, tensor: torch.Tensor, host: list[bool]) -> None:
+        self.active_sequences = tensor
+        self.__dict__["_active_of"] = (tensor, tensor._version, host)
+
     @torch.no_grad()
     def release(self, sequence_indices: torch.Tensor | Sequence[int] | None = None) -> int:
         """Return the private rows of finished requests to every layer's pool (inference.py:71-114)."""
+        active = self._active_host()
         if sequence_indices is None:
-            chosen = self.active_sequences.nonzero().flatten()
-            host = chosen.tolist()
+            host = [i for i, a in enumerate(active) if a]
+            chosen = torch.tensor(host, dtype=torch.int64).to(self.device)
         elif isinstance(sequence_indices, torch.Tensor):
             chosen = sequence_indices.to(device=self.device, dtype=torch.int64)
             host = chosen.tolist() if chosen.ndim == 1 else None
@@ -111,21 +127,26 @@ class FaithfulSDMDecodeState:
         if chosen.numel() == 0:
             return 0
         if (min(host) < 0 or max(host) >= self.batch or len(set(host)) != len(host)
-                or not bool(self.active_sequences[chosen].all())):
+                or not all(active[i] for i in host)):
             raise ValueError("released sequence is invalid, duplicated, or inactive")
         total = release_layers(self.sdm_states,
                                _banks_per_state(chosen, [self._heads(st, self.batch) for st in self.sdm_states]))
         self.active_sequences[chosen] = False
+        after = list(active)
+        for i in host:
+            after[i] = False
+        self._set_active(self.active_sequences, after)
         return total
 
     @torch.no_grad()
     def compact(self) -> torch.Tensor:
         """Drop released request slots; live rows stay where they are (inference.py:116-159)."""
         before = self.batch
-        keep = self.active_sequences.nonzero().flatten()
-        if keep.numel() == before:
+        kept = [i for i, a in enumerate(self._active_host()) if a]
+        if len(kept) == before:
             # Nothing was released: every gather below would be the identity,
             # so only the checks and the position update remain.
+            keep = torch.arange(before, device=self.device)
             for state in self.sdm_states:
                 self._heads(state, before)
             if not before:
@@ -133,17 +154,18 @@ class FaithfulSDMDecodeState:
             elif self.positions is not None:
                 self.position = self._max_position()
             return keep
-        positions = self.current_positions()
+        keep = torch.tensor(kept, dtype=torch.int64).to(self.device)
         if before:
             retain_layers(self.sdm_states,
                           _banks_per_state(keep, [self._heads(st, before) for st in self.sdm_states]))
         self.dense_keys = tuple(t[keep].contiguous() for t in self.dense_keys)
         self.dense_values = tuple(t[keep].contiguous() for t in self.dense_values)
-        kept_positions = positions[keep].contiguous()
         if self.positions is not None:
-            self.positions = kept_positions
-        self.active_sequences = torch.ones(keep.numel(), device=self.device, dtype=torch.bool)
-        self.position = (self._max_position() if self.positions is not None else int(kept_positions.max().item())) \
+            self.positions = self.positions[keep].contiguous()
+        self._set_active(torch.ones(keep.numel(), device=self.device, dtype=torch.bool), [True] * keep.numel())
+        # With one shared position the survivors keep it; otherwise the
+        # largest survivor position (one read).
+        self.position = (self._max_position() if self.positions is not None else self.position) \
             if keep.numel() else 0
         return keep
 
@@ -165,8 +187,16 @@ class FaithfulSDMDecodeState:
         self.dense_keys = tuple(torch.cat(p, dim=0).contiguous() for p in zip(self.dense_keys, incoming.dense_keys))
         self.dense_values = tuple(torch.cat(p, dim=0).contiguous()
                                   for p in zip(self.dense_values, incoming.dense_values))
+        total = self.batch + incoming.batch
+        if self.positions is None and incoming.positions is None and self.batch and incoming.batch:
+            # Both sides hold one position each: known on the host.
+            if self.position != incoming.position:
+                self.positions = torch.cat((self.current_positions(), incoming.current_positions())).contiguous()
+                self.position = max(self.position, incoming.position)
+            self._set_active(torch.ones(total, device=self.device, dtype=torch.bool), [True] * total)
+            return incoming.batch
         merged = torch.cat((self.current_positions(), incoming.current_positions())).contiguous()
-        self.active_sequences = torch.ones(merged.numel(), device=self.device, dtype=torch.bool)
+        self._set_active(torch.ones(merged.numel(), device=self.device, dtype=torch.bool), [True] * total)
         if merged.numel():
             # all positions equal <=> min == max; one read for both
             lo, hi = torch.stack((merged.min(), merged.max())).tolist()

@@ -330,6 +330,23 @@ int cow_prefill_recurrence(const cow_pool* pool, const cow_step* prefix, int64_t
 int cow_prefill_recurrence_layers(const cow_pool* pools, const cow_step* prefixes, int32_t layers,
                                   int64_t time, int32_t writes, int32_t reads, int32_t index_dtype,
                                   int32_t act_dtype, void* stream);
+/* The same recurrence in two passes per time chunk: a parallel pass resolves
+ * the routes of every (bank, token) of the chunk against the fixed map into
+ * records in `workspace` (index checks, map lookups, repeated-write check,
+ * read-after-write folding), then one warp per bank walks the chunk's tokens
+ * on those records, so a token's serial chain holds only its rows and
+ * arithmetic.  Same results and status bits as cow_prefill_recurrence_layers
+ * (same operations in the same order).  The workspace (16-byte aligned) must
+ * hold the records of at least one token of every bank; the walk covers T in
+ * chunks of as many tokens as fit (at most 256 MiB of records per chunk).
+ * cow_prefill_workspace_bytes gives the size that covers the longest chunk
+ * (-1 for invalid arguments).  Replaces the dense prefix recurrence of
+ * sdm.py:474-529 as used by prefill_faithful_sdm_stack (inference.py:369-456). */
+int64_t cow_prefill_workspace_bytes(const cow_pool* pools, int32_t layers, int64_t time, int32_t writes,
+                                    int32_t reads);
+int cow_prefill_recurrence_layers_ws(const cow_pool* pools, const cow_step* prefixes, int32_t layers,
+                                     int64_t time, int32_t writes, int32_t reads, int32_t index_dtype,
+                                     int32_t act_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* grow_capacity (allocator.py:692-744): copy rows [0,old_cap) into the new
  * slab, the old free stack below arange(old_cap,new_cap) in the new stack,

@@ -70,6 +70,10 @@ def test_multi_pool_and_host_step_entry_points_reject_bad_arguments():
     assert lib.cow_validate_layers(pools, 2, ws, 16, out, None) == _lib.ERR_INVALID
     assert lib.cow_pack_apply_layers(pools, 0, ws, 16, None) == _lib.ERR_INVALID
     assert lib.cow_prefill_recurrence_layers(pools, None, 2, 4, 4, 16, 1, 0, None) == _lib.ERR_INVALID
+    # resolved-route prefill: records of (4 + 3*4 + 3*16) words per (bank, token), 8 banks, 4 tokens
+    assert lib.cow_prefill_workspace_bytes(pools, 2, 4, 4, 16) == 8 * 4 * 64 * 4
+    assert lib.cow_prefill_workspace_bytes(pools, 2, 4, 0, 16) == -1
+    assert lib.cow_prefill_recurrence_layers_ws(pools, None, 2, 4, 4, 16, 1, 0, ws, 16, None) == _lib.ERR_INVALID
     # host-to-host steps: negative sizes, missing buffers or events
     assert lib.cow_decode_step_host(pools, None, 1, 4, 16, 1, 0, None, 0, None, None, -1, None, None, 0,
                                     None) == _lib.ERR_INVALID
