@@ -551,7 +551,7 @@ int64_t cow_prefill_workspace_bytes(const cow_pool* pools, int32_t layers, int64
     return -1;
   const int64_t banks = total_banks_of(pools, layers);
   const int64_t per_token = banks * prefill_record_words(writes, reads) * 4;
-  if (per_token == 0 || time == 0) return 16;
+  if (per_token == 0 || time == 0 || banks > kWalkSplitMaxBanks) return 16;
   int64_t tc = kPrefillRecordCap / per_token;
   if (tc < 1) tc = 1;
   if (tc > time) tc = time;
@@ -568,6 +568,16 @@ int cow_prefill_recurrence_layers_ws(const cow_pool* pools, const cow_step* pref
                                    C.bank_begin, blocks);
   if (status != COW_OK || blocks == 0) return status;
   const int64_t banks = total_banks_of(pools, layers);
+  if (banks > kWalkSplitMaxBanks) {
+    // Thousands of banks fill the GPU with one-warp walks and are bound by
+    // row bandwidth: the walk that resolves each token's routes a token ahead
+    // costs no route records (about 10 % less time there).
+    void (*fn)(PrefillLaunch) = nullptr;
+    COW_SELECT_KERNEL(cow_prefill_kernel, pools[0].slab_dtype, width_chunks(pools[0].width),
+                      route_variant(writes, reads), fn);
+    fn<<<static_cast<unsigned>(blocks), kBanksPerCta * 32, 0, as_stream(stream)>>>(P);
+    return launch_status();
+  }
   C.rec_words = prefill_record_words(writes, reads);
   const int64_t per_token = banks * C.rec_words * 4;
   if (!workspace || !aligned16(workspace) || workspace_bytes < per_token) return COW_ERR_INVALID;
@@ -582,7 +592,7 @@ int cow_prefill_recurrence_layers_ws(const cow_pool* pools, const cow_step* pref
   void (*walk)(PrefillLaunch, PrefillChunk) = nullptr;
   COW_SELECT_KERNEL(cow_prefill_walk_kernel, pools[0].slab_dtype, width_chunks(pools[0].width), rv, walk);
   const bool split = pools[0].slab_dtype == COW_F32 && pools[0].width <= 128 && rv == 0 && reads <= 32 &&
-                     banks <= kWalkSplitMaxBanks && split_walk_enabled();
+                     split_walk_enabled();
   const size_t smem = static_cast<size_t>(split ? 1 : kBanksPerCta) * 2 * C.rec_words * 4;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(split ? reinterpret_cast<const void*>(cow_prefill_split_walk_kernel)

@@ -333,14 +333,19 @@ int cow_prefill_recurrence_layers(const cow_pool* pools, const cow_step* prefixe
 /* The same recurrence in two passes per time chunk: a parallel pass resolves
  * the routes of every (bank, token) of the chunk against the fixed map into
  * records in `workspace` (index checks, map lookups, repeated-write check,
- * read-after-write folding), then one warp per bank walks the chunk's tokens
- * on those records, so a token's serial chain holds only its rows and
- * arithmetic.  Same results and status bits as cow_prefill_recurrence_layers
- * (same operations in the same order).  The workspace (16-byte aligned) must
- * hold the records of at least one token of every bank; the walk covers T in
- * chunks of as many tokens as fit (at most 256 MiB of records per chunk).
- * cow_prefill_workspace_bytes gives the size that covers the longest chunk
- * (-1 for invalid arguments).  Replaces the dense prefix recurrence of
+ * read-after-write folding), then the walk runs the chunk's tokens on those
+ * records, so a token's serial chain holds only its rows and arithmetic.
+ * Same rows, maps and status bits as cow_prefill_recurrence_layers (same
+ * operations in the same order).  Cohorts of f32 rows, width <= 128, W <= 4
+ * and R <= 32 walk with four warps per bank, whose partial readouts are
+ * summed in another order: readings agree within rounding.  The workspace
+ * (16-byte aligned) must hold the records of at least one token of every
+ * bank; the walk covers T in chunks of as many tokens as fit (at most
+ * 256 MiB of records per chunk).  cow_prefill_workspace_bytes gives the size
+ * that covers the longest chunk (-1 for invalid arguments).  Launches of more
+ * than 2,048 banks, which fill the GPU and are bound by row bandwidth, run
+ * the per-token walk of cow_prefill_recurrence_layers and need no workspace
+ * (the size is then 16).  Replaces the dense prefix recurrence of
  * sdm.py:474-529 as used by prefill_faithful_sdm_stack (inference.py:369-456). */
 int64_t cow_prefill_workspace_bytes(const cow_pool* pools, int32_t layers, int64_t time, int32_t writes,
                                     int32_t reads);
