@@ -316,9 +316,10 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 // kSplit warps.  Every warp resolves the bank's routes (identical metadata,
 // no barrier) and holds all W write rows (the gated-delta update needs all of
 // them for the retrieved vector); warp k stores write rows w == k (mod kSplit)
-// and reads rows r == k (mod kSplit), with every read row bulk-copied into
-// shared memory (rows read after a write this step are fed from registers
-// and copied from M0 with weight 0, so the accumulation has no branches).
+// and reads rows r == k (mod kSplit) into registers (kBulk: bulk-copied into
+// shared memory instead, rows read after a write this step then copied from
+// M0 with weight 0); rows read after a write this step are fed from the
+// updated registers.
 // The kSplit partial readouts meet in shared memory.  Warp 0 alone takes
 // part in the pool's scan and close and places the first touches, exactly as
 // cow_decode_kernel does (same flags, same epoch, same pop order).  Its
@@ -327,6 +328,7 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 constexpr int kSplit = 4;
 constexpr int kSplitRows = 32 / kSplit;  // read rows per warp (R <= 32)
 
+template <bool kBulk>
 __global__ void __launch_bounds__(kSplit * 32)
     cow_decode_split_kernel(const __grid_constant__ DecodeLaunch P) {
   __shared__ WarpMetaT<32> s_meta[kSplit];
@@ -388,6 +390,8 @@ __global__ void __launch_bounds__(kSplit * 32)
   const int64_t m0_base = tmpl * N;
   const int my_rows = R > k ? (R - k + kSplit - 1) / kSplit : 0;
   float4 upd[4][1];
+  float4 rrow[kBulk ? 1 : kSplitRows];
+  float rwt[kBulk ? 1 : kSplitRows];
   if (!bad) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
@@ -401,19 +405,37 @@ __global__ void __launch_bounds__(kSplit * 32)
         upd[w][0] = x;
       }
     }
-    uint64_t* bar = &s_bar[k];
-    if (lane == 0) {
-      mbar_init(bar, 1);
-      mbar_arrive_expect_tx(bar, static_cast<unsigned>(my_rows) * static_cast<unsigned>(D) * 4u);
-    }
-    __syncwarp();
-    if (lane < my_rows) {
-      const int r = k + kSplit * lane;
-      const int src = sm.rsrc[r];
-      s_rw[k][lane] = src >= -1 ? sm.rw[r] : 0.f;
-      const float* row = src >= 0 ? static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D
-                                  : L.m0 + (m0_base + sm.ridx[r]) * D;
-      bulk_row_copy(&s_rows[k][lane][0], row, static_cast<unsigned>(D) * 4u, bar);
+    if constexpr (kBulk) {
+      uint64_t* bar = &s_bar[k];
+      if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_arrive_expect_tx(bar, static_cast<unsigned>(my_rows) * static_cast<unsigned>(D) * 4u);
+      }
+      __syncwarp();
+      if (lane < my_rows) {
+        const int r = k + kSplit * lane;
+        const int src = sm.rsrc[r];
+        s_rw[k][lane] = src >= -1 ? sm.rw[r] : 0.f;
+        const float* row = src >= 0 ? static_cast<const float*>(L.slab) + static_cast<int64_t>(src) * D
+                                    : L.m0 + (m0_base + sm.ridx[r]) * D;
+        bulk_row_copy(&s_rows[k][lane][0], row, static_cast<unsigned>(D) * 4u, bar);
+      }
+    } else {
+      // Read rows straight into registers (a warp has at most kSplitRows):
+      // rows written this step are skipped (their updated value is added from
+      // registers), so the weights and the sum order match the bulk variant.
+#pragma unroll
+      for (int j = 0; j < kSplitRows; ++j) {
+        const int r = k + kSplit * j;
+        const int src = r < R ? sm.rsrc[r] : -2;
+        rwt[j] = src >= -1 ? sm.rw[r] : 0.f;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane * 4 < D) {
+          if (src >= 0) x = Elem<COW_F32>::ld4(L.slab, static_cast<int64_t>(src) * D + lane * 4);
+          else if (src == -1) x = ld4_m0(L.m0, (m0_base + sm.ridx[r]) * D + lane * 4);
+        }
+        rrow[j] = x;
+      }
     }
   }
 
@@ -441,13 +463,20 @@ __global__ void __launch_bounds__(kSplit * 32)
     for (int w = 0; w < 4; ++w) {
       if (w < W && w % kSplit == k) acc[0] = f4_axpy(sm.fwt[w], upd[w][0], acc[0]);
     }
-    if (my_rows > 0 && !mbar_wait(&s_bar[k], 0, kSpinLimit)) {
-      if (lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
-      mbar_wait(&s_bar[k], 0, kSpinLimit);
-    }
-    if (lane * 4 < D) {
-      for (int j = 0; j < my_rows; ++j)
-        acc[0] = f4_axpy(s_rw[k][j], *reinterpret_cast<const float4*>(&s_rows[k][j][lane * 4]), acc[0]);
+    if constexpr (kBulk) {
+      if (my_rows > 0 && !mbar_wait(&s_bar[k], 0, kSpinLimit)) {
+        if (lane == 0) atomicOr(L.status, COW_ST_WAIT_TIMEOUT);
+        mbar_wait(&s_bar[k], 0, kSpinLimit);
+      }
+      if (lane * 4 < D) {
+        for (int j = 0; j < my_rows; ++j)
+          acc[0] = f4_axpy(s_rw[k][j], *reinterpret_cast<const float4*>(&s_rows[k][j][lane * 4]), acc[0]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSplitRows; ++j) {
+        if (j < my_rows) acc[0] = f4_axpy(rwt[j], rrow[j], acc[0]);
+      }
     }
   }
   s_part[k][lane] = acc[0];
@@ -714,6 +743,16 @@ constexpr int64_t kSplitMaxBanks = 2048;
 
 // COW_DECODE_SPLIT=0 in the environment turns the split kernel off (for
 // comparisons); read once per process.
+// COW_DECODE_SPLIT_BULK=1 stages the split kernel's read rows by bulk copies
+// into shared memory instead of loading them into registers (comparisons).
+bool split_bulk_rows() {
+  static const bool on = [] {
+    const char* v = std::getenv("COW_DECODE_SPLIT_BULK");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
 bool split_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("COW_DECODE_SPLIT");
@@ -882,15 +921,15 @@ int decode_step_impl(const cow_pool* pools, const cow_step* steps, int32_t layer
         total_banks <= kSplitMaxBanks) {
       // Small launch: one bank per block of kSplit warps (cow_decode_split_kernel).
       const size_t split_smem = static_cast<size_t>(kSplit) * max_slots * sizeof(int32_t);
-      const int split_resident = resident_blocks(reinterpret_cast<const void*>(cow_decode_split_kernel),
-                                                 kSplit * 32, split_smem);
+      void (*split_fn)(DecodeLaunch) = split_bulk_rows() ? cow_decode_split_kernel<true> : cow_decode_split_kernel<false>;
+      const int split_resident = resident_blocks(reinterpret_cast<const void*>(split_fn), kSplit * 32, split_smem);
       if (static_cast<int64_t>(split_resident) >= total_banks) {
         int32_t begin = 0;
         for (int l = 0; l < layers; ++l) {
           P.layer[l].split_begin = begin;
           begin += static_cast<int32_t>(pools[l].banks);
         }
-        cow_decode_split_kernel<<<static_cast<unsigned>(total_banks), kSplit * 32, split_smem, as_stream(stream)>>>(P);
+        split_fn<<<static_cast<unsigned>(total_banks), kSplit * 32, split_smem, as_stream(stream)>>>(P);
         return launch_status();
       }
     }
