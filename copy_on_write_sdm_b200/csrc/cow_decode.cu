@@ -325,7 +325,12 @@ __global__ void __launch_bounds__(kBanksPerCta * 32)
 // cow_decode_kernel does (same flags, same epoch, same pop order).  Its
 // activations are f32 and its indices int64 at compile time (the common
 // serving case), which removes the per-load dtype dispatch.
-constexpr int kSplit = 4;
+// Warps per bank (a compile-time choice; measured on the batch-64 screen: 2 warps
+// 7.3 us, 4 warps 5.8 us, 8 warps 6.2 us per step).
+#ifndef COW_SPLIT_WARPS
+#define COW_SPLIT_WARPS 4
+#endif
+constexpr int kSplit = COW_SPLIT_WARPS;
 constexpr int kSplitRows = 32 / kSplit;  // read rows per warp (R <= 32)
 
 template <bool kBulk>
