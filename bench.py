@@ -63,10 +63,10 @@ E2E_WARMUP = 64  # untimed host-to-host steps before each end-to-end leg
 # DRAM traffic per launch of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum); the capture commands and
 # figures are in profiles/.
-TRAFFIC_SCREEN = {"bytes_per_launch": 5_430_000,
-                  "source": "ncu, cow_decode_split_kernel, bench.py --steps 4 --warmup 3 --no-legs, cold caches: "
-                            "dram__bytes.sum.per_second x gpu__time_duration.sum, 2 launches "
-                            "(profiles/decode_split_kernel_config3.md)"}
+TRAFFIC_SCREEN = {"bytes_per_launch": 5_364_224,
+                  "source": "ncu, cow_decode_split_kernel (read rows in registers), bench.py --steps 4 --warmup 3 "
+                            "--no-legs, two flushed launches: dram__bytes_read.sum 5.36 MB + dram__bytes_write.sum "
+                            "0 (stores still in L2 at kernel end) (profiles/decode_split_kernel_config3.md)"}
 TRAFFIC_SCALEOUT = {"bytes_per_launch_per_bank": 14_435,
                     "source": "ncu at 224 requests (12,544 banks, prefix 256): cow_count_kernel 8.57 MB + "
                               "cow_decode_kernel 172.5 MB per step, scaled by banks "
