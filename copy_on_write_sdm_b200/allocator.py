@@ -980,7 +980,7 @@ def release_layers(states: Sequence[PackedSDMCopyOnWriteState], bank_indices: Se
         ws = _workspace(device, lib.cow_release_workspace_bytes(pools, counts, b - a))
         _lib.check(lib.cow_release_layers(pools, _ptrs(idx[a:b]), counts, b - a, ws.data_ptr(), ws.numel(),
                                           released[a:].data_ptr(), stream), "cow_release_layers")
-    return int(released.sum())
+    return sum(released.tolist())
 
 
 @torch.no_grad()

@@ -39,10 +39,17 @@ def _banks_of(requests: torch.Tensor, heads: int) -> torch.Tensor:
     return (requests[:, None] * heads + torch.arange(heads, device=requests.device)[None, :]).reshape(-1)
 
 
-def _banks_per_state(requests: torch.Tensor, heads: Sequence[int]) -> list[torch.Tensor]:
-    """``_banks_of`` for every pool, computed once per distinct head count."""
+def _banks_per_state(requests: torch.Tensor, heads: Sequence[int],
+                     host: Sequence[int] | None = None) -> list[torch.Tensor]:
+    """``_banks_of`` for every pool, computed once per distinct head count;
+    from the host copy of ``requests`` (one small copy, no kernels) when given."""
     cache: dict[int, torch.Tensor] = {}
-    return [cache[h] if h in cache else cache.setdefault(h, _banks_of(requests, h)) for h in heads]
+    for h in heads:
+        if h not in cache:
+            cache[h] = (_banks_of(requests, h) if host is None else
+                        torch.tensor([r * h + j for r in host for j in range(h)], dtype=torch.int64)
+                        .to(requests.device))
+    return [cache[h] for h in heads]
 
 
 @dataclass
@@ -130,7 +137,7 @@ class FaithfulSDMDecodeState:
                 or not all(active[i] for i in host)):
             raise ValueError("released sequence is invalid, duplicated, or inactive")
         total = release_layers(self.sdm_states,
-                               _banks_per_state(chosen, [self._heads(st, self.batch) for st in self.sdm_states]))
+                               _banks_per_state(chosen, [self._heads(st, self.batch) for st in self.sdm_states], host))
         self.active_sequences[chosen] = False
         after = list(active)
         for i in host:
@@ -157,7 +164,7 @@ class FaithfulSDMDecodeState:
         keep = torch.tensor(kept, dtype=torch.int64).to(self.device)
         if before:
             retain_layers(self.sdm_states,
-                          _banks_per_state(keep, [self._heads(st, before) for st in self.sdm_states]))
+                          _banks_per_state(keep, [self._heads(st, before) for st in self.sdm_states], kept))
         self.dense_keys = tuple(t[keep].contiguous() for t in self.dense_keys)
         self.dense_values = tuple(t[keep].contiguous() for t in self.dense_values)
         if self.positions is not None:
