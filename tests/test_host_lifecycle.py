@@ -1,6 +1,6 @@
 """Host-side lifecycle bookkeeping that needs no GPU: the maximum request
-position is read from the positions tensor once and read again only when that
-tensor is replaced or changed in place."""
+position and the active-request flags are read from their tensors once and
+read again only when a tensor is replaced or changed in place."""
 
 from __future__ import annotations
 
@@ -60,3 +60,42 @@ def test_slab_reserve_is_released_when_the_slab_is_replaced():
     assert st.__dict__.get("_slab_store") is store and st.capacity_rows == 24
     st.values = torch.zeros(20, 8)  # replaced by other means: the reserve goes
     assert "_slab_store" not in st.__dict__
+
+
+def test_active_flags_mirror_follows_the_tensor():
+    """The host list of active requests is read from the tensor once and again
+    only when the tensor is replaced or changed in place."""
+    state = _state(torch.tensor([3, 9, 5]))
+    assert state._active_host() == [True, True, True]
+    state.active_sequences[1] = False  # a caller's in-place write: the version moves
+    assert state._active_host() == [True, False, True]
+    state.active_sequences = torch.tensor([False, True])  # replaced
+    assert state._active_host() == [False, True]
+
+
+def test_active_flags_mirror_is_not_reread_while_unchanged(monkeypatch):
+    state = _state(torch.tensor([1, 2, 3]))
+    state._active_host()
+    calls = []
+    original = torch.Tensor.tolist
+
+    def counting_tolist(self, *a, **k):
+        calls.append(1)
+        return original(self, *a, **k)
+
+    monkeypatch.setattr(torch.Tensor, "tolist", counting_tolist)
+    for _ in range(3):
+        assert state._active_host() == [True, True, True]
+    assert calls == []
+
+
+def test_compact_without_releases_keeps_every_request_and_reads_no_flags(monkeypatch):
+    state = _state(torch.tensor([4, 6]))
+    state._active_host()
+    def no_read(self, *a, **k):
+        raise AssertionError("the active flags were read again")
+
+    monkeypatch.setattr(torch.Tensor, "tolist", no_read)
+    keep = state.compact()
+    monkeypatch.undo()
+    assert keep.tolist() == [0, 1] and state.position == 6
