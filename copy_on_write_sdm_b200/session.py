@@ -52,7 +52,9 @@ class DecodeSession:
     """Fused decode over ``pools`` with packed input/output buffers.
 
     Buffer layout (``inputs``, one flat byte buffer, per pool, in order):
-    write_indices ``[B,W]`` int64, read_indices ``[B,R]`` int64,
+    write_indices ``[B,W]``, read_indices ``[B,R]`` (``index_dtype``, int64 by
+    default; int32 moves 4 bytes less per index across PCIe in the host-to-host
+    steps),
     write_weights ``[B,W]``, read_weights ``[B,R]``, values ``[B,D]``,
     input_gate ``[B]``, forget_log_gate ``[B]`` (activation dtype).  The
     per-pool views are in ``self.views[l]`` (a dict of tensors keyed by the
@@ -64,9 +66,12 @@ class DecodeSession:
               "forget_log_gate")
 
     def __init__(self, pools: Sequence[PackedSDMCopyOnWriteState], *, writes: int, reads: int,
-                 act_dtype: torch.dtype = torch.float32, pinned_host: bool = True) -> None:
+                 act_dtype: torch.dtype = torch.float32, pinned_host: bool = True,
+                 index_dtype: torch.dtype = torch.int64) -> None:
         if not 1 <= len(pools) <= _lib.MAX_LAYERS:
             raise ValueError(f"between 1 and {_lib.MAX_LAYERS} pools per session")
+        if index_dtype not in (torch.int32, torch.int64):
+            raise ValueError("route indices must be int32 or int64")
         p0 = pools[0]
         for p in pools:
             _lib.require_cuda(p.values, "SDM COW state")
@@ -80,7 +85,7 @@ class DecodeSession:
         self.device = p0.values.device
         B, D = p0.banks, p0.width
         act = torch.tensor([], dtype=act_dtype).element_size()
-        shapes = {"write_indices": ((B, writes), torch.int64), "read_indices": ((B, reads), torch.int64),
+        shapes = {"write_indices": ((B, writes), index_dtype), "read_indices": ((B, reads), index_dtype),
                   "write_weights": ((B, writes), act_dtype), "read_weights": ((B, reads), act_dtype),
                   "values": ((B, D), act_dtype), "input_gate": ((B,), act_dtype),
                   "forget_log_gate": ((B,), act_dtype)}
@@ -93,7 +98,7 @@ class DecodeSession:
                 n = 1
                 for s in shape:
                     n *= s
-                nbytes = n * (8 if dtype == torch.int64 else act)
+                nbytes = n * (dtype.itemsize if name.endswith("indices") else act)
                 per[name] = (off, shape, dtype, nbytes)
                 off += (nbytes + 15) // 16 * 16
             offsets.append(per)
@@ -113,6 +118,7 @@ class DecodeSession:
                          None)
             for l, v in enumerate(self.views)])
         self._act_code = _lib.dtype_code(act_dtype)
+        self._idx_code = _lib.I64 if index_dtype == torch.int64 else _lib.I32
         self._pool_key = None
         self._pool_array = None
         self._scratch = new_decode_scratch(self.device, B * len(pools), len(pools))  # owned by this session
@@ -248,7 +254,7 @@ class DecodeSession:
         handle = stream.cuda_stream if stream is not None else current
         self._prove()
         _lib.check(self._lib.cow_decode_step(self._pools(), self._steps, len(self.pools), self.writes, self.reads,
-                                             _lib.I64, self._act_code, self._scratch.data_ptr(),
+                                             self._idx_code, self._act_code, self._scratch.data_ptr(),
                                              self._scratch.numel(), handle), "cow_decode_step")
         return self.outputs
 
@@ -284,7 +290,7 @@ class DecodeSession:
             # but the host input bytes and the compute stream
             descs = tuple(_lib.CowHostPipeline(
                 None, ctypes.cast(steps[b], ctypes.POINTER(_lib.CowStep)), len(self.pools), self.writes, self.reads,
-                _lib.I64, self._act_code, 0, self._scratch.data_ptr(), self._scratch.numel(), inputs[b].data_ptr(),
+                self._idx_code, self._act_code, 0, self._scratch.data_ptr(), self._scratch.numel(), inputs[b].data_ptr(),
                 self.step_bytes, host_outputs[b].data_ptr(), outputs[b].data_ptr(), self._out_bytes,
                 h2d.cuda_stream, d2h.cuda_stream, events[b][0].cuda_event, events[b][1].cuda_event,
                 events[b][2].cuda_event) for b in range(n))
@@ -394,7 +400,7 @@ class DecodeSession:
         self._prove()
         out = self.host_outputs
         _lib.check(self._lib.cow_decode_step_host(
-            self._pools(), self._steps, len(self.pools), self.writes, self.reads, _lib.I64, self._act_code,
+            self._pools(), self._steps, len(self.pools), self.writes, self.reads, self._idx_code, self._act_code,
             self._scratch.data_ptr(), self._scratch.numel(), self.inputs.data_ptr(), src.data_ptr(), self.step_bytes,
             out.data_ptr(), self.outputs.data_ptr(), self._out_bytes, self._stream_handle()),
             "cow_decode_step_host")
