@@ -498,8 +498,10 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     with torch.cuda.stream(host_stream):
         e0.record(host_stream)
         last = None
+        t0 = time.perf_counter()
         for i in range(K):
             _, last = sess.step_host_pipelined(host_steps[i])
+        piped_host_s = time.perf_counter() - t0
         host_stream.wait_event(last)
         e1.record(host_stream)
     torch.cuda.synchronize(device)
@@ -560,6 +562,7 @@ def run_gpu(args, rank, world, device, *, batch=BATCH, prefix=PREFIX, extras=Tru
     used = [st.used_bytes() for st in states]
     return dict(total_ms=total_ms, step_ms=step_ms, flushed_ms=flushed_ms, flushed_first_touches=flushed_first_touches,
                 single_ms=single_ms, e2e_ms=e2e_ms, e2e_serial_ms=e2e_serial_ms,
+                piped_host_us=1e6 * piped_host_s / K,
                 e2e_mapped_ms=e2e_mapped_ms, mapped_device=mapped_device, eager=eager,
                 warm_ms=warm, incremental=incremental,
                 dense_ms=dense_ms,
@@ -1253,7 +1256,10 @@ def _e2e_block(tokens, res, e2e_ms, e2e_mapped_ms) -> dict:
     time path beside it."""
     piped = {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
              "path": "DecodeSession.step_host_pipelined: one pinned H2D copy, capacity proof + one fused launch, "
-                     "one D2H copy; the copies of neighbouring steps overlap the decode on two side streams"}
+                     "one D2H copy; the copies of neighbouring steps overlap the decode on two side streams",
+             "host_us_per_step": res.get("piped_host_us"),
+             "note": "host_us_per_step: host time of the step_host_pipelined calls in the timed loop; a step "
+                     "longer than that waits on the PCIe copies (340 KB in, 229 KB out per step)"}
     mapped = {"value": tokens / (e2e_mapped_ms / 1e3), "unit": "tokens/s",
               "path": "DecodeSession.step_host_mapped: capacity proof + one fused launch whose kernel reads the "
                       "step's pinned host bytes over PCIe and writes the readouts to pinned host memory (zero-copy)",
