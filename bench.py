@@ -840,6 +840,15 @@ def churn_prefill(m0s, prompts: list[dict], first: int, requests: int, quantum: 
         sdm_layer_positions=tuple(range(LAYERS)), sdm_states=tuple(states), dense_keys=(), dense_values=())
 
 
+def churn_admit_prefix(state, prompts: list[dict], first: int, requests: int) -> None:
+    """Requests ``first .. first+requests-1`` of ``prompts`` prefilled straight into
+    the live pools of ``state`` (``FaithfulSDMDecodeState.admit_prefix``)."""
+    lo, hi = first * CH_HEADS, (first + requests) * CH_HEADS
+    device = state.device
+    templates = torch.arange(CH_HEADS, device=device, dtype=torch.int64).repeat(requests)
+    state.admit_prefix([{k: v[lo:hi] for k, v in x.items()} for x in prompts], template_indices=templates)
+
+
 def run_gpu_churn(args, rank, world, device):
     """Continuous batching over 256 live slots per GPU.
 
@@ -893,7 +902,10 @@ def run_gpu_churn(args, rank, world, device):
     # workspace allocations (tens of milliseconds), which is start-up, not churn.
     for n in (1, 2):  # two sizes: some kernels first run at the second
         state.release_and_compact(list(range(n)))
-        state.admit(churn_prefill(m0s, prompts, 0, n, quantum))
+        if args.churn_admit == "prefix":
+            churn_admit_prefix(state, prompts, 0, n)
+        else:
+            state.admit(churn_prefill(m0s, prompts, 0, n, quantum))
         remaining = np.concatenate([remaining[n:], rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=n)])
     torch.cuda.synchronize(device)
     setup_s = time.time() - t0
@@ -913,10 +925,17 @@ def run_gpu_churn(args, rank, world, device):
             stats["released_rows"] += state.release_and_compact(done.tolist())
             if next_prompt + done.size > ring_requests:
                 next_prompt = 0
-            cohort = churn_prefill(m0s, prompts, next_prompt, int(done.size), quantum)
+            if args.churn_admit == "prefix":
+                # prefill straight into the live pools (admit_prefix)
+                before = torch.stack([st.allocated_rows_tensor() for st in state.sdm_states]).sum()
+                churn_admit_prefix(state, prompts, next_prompt, int(done.size))
+                admitted_rows.append(torch.stack([st.allocated_rows_tensor() for st in state.sdm_states]).sum()
+                                     - before)
+            else:
+                cohort = churn_prefill(m0s, prompts, next_prompt, int(done.size), quantum)
+                admitted_rows.append(torch.stack([st.allocated_rows_tensor() for st in cohort.sdm_states]).sum())
+                state.admit(cohort)
             next_prompt += int(done.size)
-            admitted_rows.append(torch.stack([st.allocated_rows_tensor() for st in cohort.sdm_states]).sum())
-            state.admit(cohort)
             remaining = np.concatenate([remaining[remaining > 0],
                                         rng.integers(CH_MIN_LEN, CH_MAX_LEN + 1, size=done.size)])
         if args.trim_every and s % args.trim_every == args.trim_every - 1:
@@ -1355,6 +1374,9 @@ def main() -> int:
                     help="scaleout: largest fill of a bank's hashed table (default: the library's 0.7)")
     ap.add_argument("--quantum-steps", type=int, default=4, help="churn: growth quantum in decode steps")
     ap.add_argument("--trim-every", type=int, default=0, help="churn: trim the pools every this many steps")
+    ap.add_argument("--churn-admit", default="prefix", choices=["prefix", "prefill"],
+                    help="churn: admit cohorts by prefilling straight into the live pools (admit_prefix) or by "
+                         "prefilling pools of their own and admitting those (prefill + admit)")
     ap.add_argument("--no-legs", dest="legs", action="store_false",
                     help="screen: skip the prefix-16, strong-split and configuration-4 legs")
     ap.add_argument("--churn-warm-prefix", type=int, default=CH_WARM_PREFIX,
@@ -1551,6 +1573,8 @@ def main_churn(args, rank, world, device) -> int:
                    "live_slots_per_gpu": res["live"], "global_batch": res["live"] * world,
                    "growth_quantum_steps": args.quantum_steps, "growth_quantum_rows": res["quantum"],
                    "trim_every": args.trim_every, "initial_prefix": args.churn_warm_prefix,
+                   "admission": ("admit_prefix: cohorts prefilled straight into the live pools" if args.churn_admit
+                                 == "prefix" else "prefill pools of their own, then admit"),
                    "parallelism": f"requests sharded, {res['live']} slots per GPU x {world} GPU(s), no collective",
                    "l2": "pool state (>10 GB) exceeds L2; steps timed back to back"},
         "decode_ms_per_step": res["decode_ms"] / K, "lifecycle_ms_per_step": res["lifecycle_ms"] / K,

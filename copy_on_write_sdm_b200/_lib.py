@@ -169,6 +169,8 @@ _SIGNATURES = {
     "cow_prefill_mark_count_layers": (c_int32, [P, c_int32, c_int64, c_int64, c_int32, c_int64, P, c_int32, P,
                                                 c_int64, P, P]),
     "cow_pack_apply_layers": (c_int32, [POINTER(CowPool), c_int32, P, c_int64, P]),
+    "cow_admit_prefix_workspace_bytes": (c_int64, [c_int64, c_int64, c_int32]),
+    "cow_admit_prefix_layers": (c_int32, [POINTER(CowPool), P, P, c_int64, c_int32, P, P, c_int64, P]),
     "cow_validate_workspace_bytes": (c_int64, [POINTER(CowPool), c_int32]),
     "cow_validate_layers": (c_int32, [POINTER(CowPool), c_int32, P, c_int64, P, P]),
 }

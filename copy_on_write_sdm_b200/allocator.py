@@ -1052,30 +1052,13 @@ def append_layers(states: Sequence[PackedSDMCopyOnWriteState],
     return admitted
 
 
-@torch.no_grad()
-def from_prefix_routes_layers(
-    shared_initial_memories: Sequence[torch.Tensor],
-    prefixes: Sequence[dict],
-    *,
-    template_indices: torch.Tensor,
-    capacity_rows: int | None = None,
-    state_dtype: torch.dtype = torch.float32,
-    maximum_future_allocations: int | None = None,
-    growth_quantum_rows: int = 0,
-) -> tuple[list[PackedSDMCopyOnWriteState], list[torch.Tensor]]:
-    """Sparse prefill handoff of up to 8 independent pools (``from_prefix_routes``
-    per pool) in one set of launches with two host synchronisations.
-
-    ``prefixes[l]`` holds pool l's ``write_indices``, ``write_weights``,
-    ``values``, ``input_gate``, ``forget_log_gate``, ``read_indices``,
-    ``read_weights`` and optionally ``erase_gate`` (shapes ``[banks,T,W|R]``,
-    ``[banks,T,D]``, ``[banks,T]``); every pool has the same banks, T, W, R,
-    width and dtypes and uses ``template_indices``.
-    """
+def _prefix_steps(shared_initial_memories, prefixes, template_indices):
+    """Validated step arguments of several pools' prefixes (one set of shapes
+    and dtypes for all): ``(m0s, steps, (banks, T, W, R, width, slots, index
+    code, activation code))``."""
     n = len(prefixes)
     if len(shared_initial_memories) != n or not 1 <= n <= _lib.MAX_LAYERS:
         raise ValueError(f"between 1 and {_lib.MAX_LAYERS} pools per prefill")
-    lib = _lib.load()
     m0s, steps, shape = [], [], None
     for m0, x in zip(shared_initial_memories, prefixes):
         m0 = PackedSDMCopyOnWriteState._normalise_m0(m0)
@@ -1114,6 +1097,34 @@ def from_prefix_routes_layers(
         shape = key
         m0s.append(m0)
         steps.append(step)
+    return m0s, steps, shape
+
+
+@torch.no_grad()
+def from_prefix_routes_layers(
+    shared_initial_memories: Sequence[torch.Tensor],
+    prefixes: Sequence[dict],
+    *,
+    template_indices: torch.Tensor,
+    capacity_rows: int | None = None,
+    state_dtype: torch.dtype = torch.float32,
+    maximum_future_allocations: int | None = None,
+    growth_quantum_rows: int = 0,
+) -> tuple[list[PackedSDMCopyOnWriteState], list[torch.Tensor]]:
+    """Sparse prefill handoff of up to 8 independent pools (``from_prefix_routes``
+    per pool) in one set of launches with two host synchronisations.
+
+    ``prefixes[l]`` holds pool l's ``write_indices``, ``write_weights``,
+    ``values``, ``input_gate``, ``forget_log_gate``, ``read_indices``,
+    ``read_weights`` and optionally ``erase_gate`` (shapes ``[banks,T,W|R]``,
+    ``[banks,T,D]``, ``[banks,T]``); every pool has the same banks, T, W, R,
+    width and dtypes and uses ``template_indices``.
+    """
+    n = len(prefixes)
+    if len(shared_initial_memories) != n or not 1 <= n <= _lib.MAX_LAYERS:
+        raise ValueError(f"between 1 and {_lib.MAX_LAYERS} pools per prefill")
+    lib = _lib.load()
+    m0s, steps, shape = _prefix_steps(shared_initial_memories, prefixes, template_indices)
     banks, time, writes, reads, width, slots, idx_code, act_code = shape
     device = steps[0].widx.device
     stream = _lib.stream_of(device)
@@ -1157,6 +1168,91 @@ def from_prefix_routes_layers(
     for l, st in enumerate(states):
         st._validate_result(*flat[3 * l:3 * l + 3])
     return states, [step.output.reshape(banks, time, width) for step in steps]
+
+
+@torch.no_grad()
+@_on_dense_maps(lambda states, *_a, **_k: list(states))
+def admit_prefix_routes_layers(states: Sequence[PackedSDMCopyOnWriteState], prefixes: Sequence[dict], *,
+                               template_indices: torch.Tensor) -> list[torch.Tensor]:
+    """Prefill a cohort and admit it into ``states`` (one live pool per layer) in one
+    set of launches, without pools of its own: the same maps, free stacks,
+    rows, growth and readings as ``from_prefix_routes_layers`` (with the live
+    pools' growth quantum) followed by ``append_layers``.
+
+    Every marked slot of the cohort pops the live pool's free stack in
+    ``nonzero()`` order (the order in which appending the packed cohort pops
+    it, allocator.py:884-896), its row is filled from ``M0`` and the prefix
+    walk runs on the admitted banks in place.  Routes and templates are checked
+    before anything changes (one host synchronisation, which also reads the
+    free counts for growth).  Returns the readings ``[banks, T, width]`` per pool.
+    """
+    n = len(states)
+    if len(prefixes) != n or not 1 <= n <= _lib.MAX_LAYERS:
+        raise ValueError(f"between 1 and {_lib.MAX_LAYERS} pools per admission")
+    lib = _lib.load()
+    m0s, steps, shape = _prefix_steps([st.shared_initial_memory for st in states], prefixes, template_indices)
+    banks, time, writes, reads, width, slots, idx_code, act_code = shape
+    for st in states:
+        if st.slots != slots or st.width != width:
+            raise ValueError("admitted SDM banks do not match the destination pool")
+    if banks == 0:
+        return [step.output.reshape(0, time, width) for step in steps]
+    device = states[0].values.device
+    stream = _lib.stream_of(device)
+    templates = template_indices.to(torch.int64).contiguous()
+    marks = [torch.empty(banks, slots, device=device, dtype=torch.int32) for _ in range(n)]
+    ws = _workspace(device, max(lib.cow_pack_workspace_bytes(banks * slots, n),
+                                lib.cow_admit_prefix_workspace_bytes(banks, slots, n)))
+    out = torch.empty(2 * n, device=device, dtype=torch.int32)
+    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), idx_code, banks, time, writes,
+                                                 slots, _ptrs(marks), n, ws.data_ptr(), ws.numel(), out.data_ptr(),
+                                                 stream), "cow_prefill_mark_count_layers")
+    # One read for the mark status, live counts, free counts and the index
+    # ranges of the read routes (write routes are checked by the mark pass).
+    ranges = torch.stack([torch.stack(torch.aminmax(st.ridx)) for st in steps]).reshape(-1).to(torch.int64)
+    frees_dev = torch.stack([st.free_count.reshape(()) for st in states]).to(torch.int64)
+    host, lo, hi = _read_counts_and_range(torch.cat((out.to(torch.int64), frees_dev, ranges)), templates)
+    for l in range(n):
+        if host[2 * l]:
+            raise ValueError(_lib.status_text(host[2 * l]))
+    r = host[3 * n:]
+    if min(r[0::2]) < 0 or max(r[1::2]) >= slots:
+        raise ValueError(_lib.status_text(_lib.ST_INDEX_RANGE))
+    _check_template_range(lo, hi, m0s[0])
+    frees = []
+    for l, st in enumerate(states):
+        active, free = host[2 * l + 1], host[2 * n + l]
+        if free < active:
+            free += st.grow_capacity(st.capacity_rows + active - free)
+        frees.append(free)
+    admitted = [torch.empty(banks, slots, device=device, dtype=torch.int32) for _ in range(n)]
+    _lib.check(lib.cow_admit_prefix_layers(_pool_array(states), _ptrs(marks), templates.data_ptr(), banks, n,
+                                           _ptrs(admitted), ws.data_ptr(), ws.numel(), stream),
+               "cow_admit_prefix_layers")
+    old_banks = []
+    for l, st in enumerate(states):
+        old_banks.append(st.banks)
+        st.logical_to_physical = torch.cat((st.logical_to_physical, admitted[l]), dim=0).contiguous()
+        st.template_indices = torch.cat((st.template_indices, templates), dim=0).contiguous()
+        active = host[2 * l + 1]
+        if st.growth_quantum_rows:
+            st.proven_maximum_additional_allocations = min(st.proven_maximum_additional_allocations,
+                                                           frees[l] - active)
+        else:
+            st.capacity_is_proven = False
+            st.proven_maximum_additional_allocations = 0
+    # The walk on the admitted banks: each pool seen from its first admitted bank.
+    pools = _pool_array(states)
+    for l in range(n):
+        pools[l].map += old_banks[l] * slots * 4
+        pools[l].templates += old_banks[l] * 8
+        pools[l].banks = banks
+    structs = (_lib.CowStep * n)(*[step.struct for step in steps])
+    rws = _workspace(device, lib.cow_prefill_workspace_bytes(pools, n, time, writes, reads))
+    _lib.check(lib.cow_prefill_recurrence_layers_ws(pools, structs, n, time, writes, reads, idx_code, act_code,
+                                                    rws.data_ptr(), rws.numel(), stream),
+               "cow_prefill_recurrence_layers_ws")
+    return [step.output.reshape(banks, time, width) for step in steps]
 
 
 # --------------------------------------------------------------------------

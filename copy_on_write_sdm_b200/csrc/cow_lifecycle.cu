@@ -19,7 +19,7 @@ constexpr int kScanItems = 8;
 constexpr int kScanSeg = kScanThreads * kScanItems;
 constexpr int kScanHeader = 8;  // int32 slots before the per-block offsets
 
-enum ScanOp : int { kOpPack = 0, kOpRepack = 1, kOpAppend = 2, kOpRelease = 3 };
+enum ScanOp : int { kOpPack = 0, kOpRepack = 1, kOpAppend = 2, kOpRelease = 3, kOpAdmit = 4 };
 
 struct ScanCtx {
   int op;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(1024) scan_blocks_kernel(const __grid_constant
       c.scratch[1] = old;
       if (c.free_out != nullptr) *c.free_out = old;
       if (c.op == kOpRelease) *c.free_count = old + total;
-      if (c.op == kOpAppend) *c.free_count = old - total;
+      if (c.op == kOpAppend || c.op == kOpAdmit) *c.free_count = old - total;
     }
   }
 }
@@ -168,6 +168,16 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const __grid_c
         if (f[k]) {
           const int dst = c.free_rows[old_free - 1 - rank];
           c.src_rows[rank] = c.map[i];
+          c.dst_rows[rank] = dst;
+          c.out_map[i] = dst;
+        } else {
+          c.out_map[i] = -1;
+        }
+        break;
+      case kOpAdmit:  // append's pops, rows to come from M0 (source = flat bank*slots+slot)
+        if (f[k]) {
+          const int dst = c.free_rows[old_free - 1 - rank];
+          c.src_rows[rank] = static_cast<int32_t>(i);
           c.dst_rows[rank] = dst;
           c.out_map[i] = dst;
         } else {
@@ -302,6 +312,11 @@ __global__ void prefill_mark_kernel(const __grid_constant__ Layers<MarkCtx> L, i
     if (s < 0 || s >= slots) {
       atomicOr(c.status, COW_ST_INDEX_RANGE);
       continue;
+    }
+    // A token that writes one slot twice is refused before anything is placed.
+    const int w = static_cast<int>(i % writes);
+    for (int j = 0; j < w; ++j) {
+      if (ld_index(c.widx, i - w + j, idx64) == s) atomicOr(c.status, COW_ST_DUPLICATE_WRITE);
     }
     c.map[bank * slots + s] = 0;
   }
@@ -1066,6 +1081,59 @@ int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t inde
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   return run_scan_count(C, st);
+}
+
+int64_t cow_admit_prefix_workspace_bytes(int64_t cohort_banks, int64_t slots, int32_t layers) {
+  if (cohort_banks < 0 || slots < 1 || layers < 1 || layers > COW_MAX_LAYERS) return -1;
+  const int64_t n = cohort_banks * slots;
+  return (scan_words(n) + 2 * words16(n > 0 ? n : 1)) * 4 * layers;
+}
+
+int cow_admit_prefix_layers(const cow_pool* dsts, int32_t* const* marks, const int64_t* cohort_templates,
+                            int64_t cohort_banks, int32_t layers, int32_t* const* admitted_maps, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+  if (!dense_maps(dsts, layers)) return COW_ERR_UNSUPPORTED;
+  if (!layers_ok(dsts, layers) || !marks || !admitted_maps || cohort_banks < 0 ||
+      (cohort_banks > 0 && !cohort_templates))
+    return COW_ERR_INVALID;
+  if (!workspace_ok(workspace, workspace_bytes, cow_admit_prefix_workspace_bytes(cohort_banks, dsts[0].slots, layers)))
+    return COW_ERR_INVALID;
+  cudaStream_t st = as_stream(stream);
+  ScanLaunch C{};
+  Layers<CopyCtx> K{};
+  C.layers = K.layers = layers;
+  const int64_t n = cohort_banks * dsts[0].slots;
+  int32_t* w = static_cast<int32_t*>(workspace);
+  for (int l = 0; l < layers; ++l) {
+    const cow_pool& d = dsts[l];
+    if (d.slots != dsts[0].slots || !d.free_rows || !d.free_count || !d.slab || !d.m0 ||
+        (n > 0 && (!marks[l] || !admitted_maps[l])))
+      return COW_ERR_INVALID;
+    int32_t* flags = w;
+    int32_t* src_rows = flags + scan_words(n);
+    int32_t* dst_rows = src_rows + words16(n > 0 ? n : 1);
+    w = dst_rows + words16(n > 0 ? n : 1);
+    ScanCtx& c = C.c[l];
+    c.op = kOpAdmit;
+    c.n = n;
+    c.slots = d.slots;
+    c.map = marks[l];
+    c.out_map = admitted_maps[l];
+    c.src_rows = src_rows;
+    c.dst_rows = dst_rows;
+    c.free_rows = d.free_rows;
+    c.free_count = d.free_count;
+    c.scratch = flags;
+    K.c[l] = CopyCtx{d.slab, dst_rows, nullptr, src_rows, flags, d.m0, cohort_templates, n, d.width, d.slots,
+                     d.slab_dtype, COW_F32, 1, 0};
+    if (!copy_args_ok(K.c[l])) return COW_ERR_INVALID;
+  }
+  if (n == 0) return COW_OK;
+  int rc = run_scan_count(C, st);
+  if (rc != COW_OK) return rc;
+  rc = run_scan_apply(C, st);
+  if (rc != COW_OK) return rc;
+  return run_copy_rows(K, st);
 }
 
 int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,

@@ -22,7 +22,8 @@ from typing import TYPE_CHECKING, Sequence
 import torch
 from torch import nn
 
-from .allocator import (PackedSDMCopyOnWriteState, append_layers, dense_sdm_sparse_step, packed_sdm_cow_step,
+from .allocator import (PackedSDMCopyOnWriteState, admit_prefix_routes_layers, append_layers, dense_sdm_sparse_step,
+                        packed_sdm_cow_step,
                         release_layers, retain_layers)
 from .sdm import SparseDeltaMemory
 
@@ -215,6 +216,47 @@ class FaithfulSDMDecodeState:
         else:
             self.positions = merged
         return incoming.batch
+
+    @torch.no_grad()
+    def admit_prefix(self, prefixes: Sequence[dict], *, template_indices: torch.Tensor) -> list[torch.Tensor]:
+        """Prefill a cohort of requests from its SDM prefix routes and admit it in one
+        step, without pools of its own: the same state as prefilling the cohort
+        (``from_prefix_routes_layers``) and calling ``admit`` with it.
+
+        ``prefixes[l]`` holds SDM layer l's ``[banks, T, ...]`` routes, values
+        and gates (as for ``from_prefix_routes``); ``template_indices`` gives each
+        admitted bank's head.  Every request of the cohort sits at position T.
+        Only batches without attention layers (no K/V caches to extend) take
+        this path.  Returns each SDM layer's readings ``[banks, T, width]``.
+        """
+        if self.dense_keys or self.dense_values:
+            raise ValueError("batches with attention layers admit prefilled cohorts through admit()")
+        if len(prefixes) != len(self.sdm_states):
+            raise ValueError("one prefix per SDM layer")
+        self.compact()
+        heads = self._heads(self.sdm_states[0], self.batch) if self.batch else None
+        banks, time = prefixes[0]["write_indices"].shape[:2]
+        if heads is None:
+            if template_indices.numel() == 0:
+                heads = 1
+            else:
+                heads = int(template_indices.max().item()) + 1 if banks else 1
+        if banks % heads:
+            raise ValueError("admitted SDM banks do not divide by the batch's heads")
+        readings = admit_prefix_routes_layers(self.sdm_states, prefixes, template_indices=template_indices)
+        incoming = banks // heads
+        before = self.batch
+        total = before + incoming
+        if before == 0:
+            self.position, self.positions = time, None
+        elif self.positions is None and self.position == time:
+            pass
+        else:
+            cohort = torch.full((incoming,), time, device=self.device, dtype=torch.int64)
+            self.positions = torch.cat((self.current_positions(), cohort)).contiguous()
+            self.position = max(self.position, time)
+        self._set_active(torch.ones(total, device=self.device, dtype=torch.bool), [True] * total)
+        return readings
 
     def _max_position(self) -> int:
         """``int(positions.max())``, read again only when the positions tensor was

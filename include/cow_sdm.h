@@ -438,7 +438,8 @@ int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t laye
 
 /* Sparse prefill layout for each pool.  Phase 1 sets maps[l] [banks,slots] to
  * -1, marks the written slots of write_indices[l] [banks,T,W] and counts them:
- * out[2l] = status bits (COW_ST_INDEX_RANGE), out[2l+1] = live rows.  Phase 2
+ * out[2l] = status bits (COW_ST_INDEX_RANGE, COW_ST_DUPLICATE_WRITE for a
+ * token that writes one slot twice), out[2l+1] = live rows.  Phase 2
  * (same workspace; pools[l].map = maps[l], slab and stack sized by the host)
  * assigns rows 0..A-1 in nonzero() order, fills the free stack with
  * arange(A, capacity) and copies each live row from m0.  n = banks*slots. */
@@ -448,6 +449,25 @@ int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t inde
                                   void* workspace, int64_t workspace_bytes, int32_t* out, void* stream);
 int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,
                           void* stream);
+
+/* A prefilled cohort admitted straight into live pools: the same result as
+ * packing the cohort into pools of its own (cow_pack_apply_layers) and then
+ * appending them (cow_append_layers, allocator.py:842-915), without the
+ * cohort's slab.  `marks[l]` [cohort_banks, slots] holds the marks of
+ * cow_prefill_mark_count_layers (0 written, -1 not); every marked entry, in
+ * nonzero() order, pops dsts[l]'s free stack (free_rows[free_count-1-rank]),
+ * its row is filled from m0[cohort_templates[bank], slot] and
+ * admitted_maps[l] [cohort_banks, slots] receives the popped rows (-1
+ * elsewhere); free_count drops by the live count.  The caller proves the
+ * free rows beforehand (growing the pool as append does), then extends the
+ * pool's map and templates with admitted_maps / cohort_templates and runs the
+ * prefix walk (cow_prefill_recurrence_layers_ws) on the admitted banks.  No
+ * counterpart in the reference as one call (it is prefill_faithful_sdm_stack
+ * followed by FaithfulSDMDecodeState.admit, inference.py:161-206, 369-456). */
+int64_t cow_admit_prefix_workspace_bytes(int64_t cohort_banks, int64_t slots, int32_t layers);
+int cow_admit_prefix_layers(const cow_pool* dsts, int32_t* const* marks, const int64_t* cohort_templates,
+                            int64_t cohort_banks, int32_t layers, int32_t* const* admitted_maps, void* workspace,
+                            int64_t workspace_bytes, void* stream);
 
 /* validate_invariants for each pool: out[3l..3l+2] (device int32) = the
  * pool's status word, the partition bits (COW_ST_MULTI_OWNER,

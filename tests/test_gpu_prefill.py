@@ -136,3 +136,77 @@ def test_resolved_walk_reports_route_errors_like_per_token_walk(dev, monkeypatch
             run(m0s, [x], templates, dev, banks * 4)
         messages.append(str(err.value))
     assert messages[0] == messages[1]
+
+
+def _decode_state(states, requests, position):
+    from copy_on_write_sdm_b200.inference import FaithfulSDMDecodeState
+
+    return FaithfulSDMDecodeState(
+        layout="B" * len(states), position=position, capacity=0, activation_dtype=torch.float32,
+        active_sequences=torch.ones(requests, dtype=torch.bool, device=states[0].values.device),
+        sdm_layer_positions=tuple(range(len(states))), sdm_states=tuple(states), dense_keys=(), dense_values=())
+
+
+@pytest.mark.parametrize("quantum", [16, 4096])  # 16: the admission grows every pool
+def test_admit_prefix_matches_prefill_then_admit(dev, quantum):
+    """admit_prefix (the cohort prefilled straight into the live pools) leaves the
+    same maps, free stacks, rows, growth counters, positions and readings as
+    prefilling the cohort into pools of its own and admitting them."""
+    from copy_on_write_sdm_b200.allocator import from_prefix_routes_layers
+
+    rng = np.random.default_rng(31 + quantum)
+    heads, live, cohort, layers, slots, width, W, R = 2, 6, 3, 3, 256, 128, 4, 16
+    m0s = [(0.02 * rng.standard_normal((heads, slots, width))).astype(np.float32) for _ in range(layers)]
+    warm = [prefix(rng, live * heads, 12, slots, width, W, R) for _ in range(layers)]
+    new = [prefix(rng, cohort * heads, 9, slots, width, W, R) for _ in range(layers)]
+    live_t = np.tile(np.arange(heads), live)
+    new_t = np.tile(np.arange(heads), cohort)
+    pair = []
+    for _ in range(2):
+        states, _ = run(m0s, warm, live_t, dev, quantum)
+        state = _decode_state(states, live, 12)
+        state.release_and_compact([1, 4])
+        pair.append(state)
+    a, b = pair
+    cohort_states, want = run(m0s, new, new_t, dev, quantum)
+    a.admit(_decode_state(cohort_states, cohort, 9))
+    got = b.admit_prefix([{k: cu(x[k], dev) for k in KEYS} for x in new], template_indices=cu(new_t, dev))
+    torch.cuda.synchronize(dev)
+    for l in range(layers):
+        assert torch.equal(got[l], want[l])
+        p, q = a.sdm_states[l], b.sdm_states[l]
+        assert torch.equal(p.logical_to_physical, q.logical_to_physical)
+        assert torch.equal(p.template_indices, q.template_indices)
+        fp = int(p.free_count)
+        assert fp == int(q.free_count) and torch.equal(p.free_rows[:fp], q.free_rows[:fp])
+        assert p.capacity_rows == q.capacity_rows
+        assert (p.growth_events, p.growth_rows_added, p.proven_maximum_additional_allocations) == \
+            (q.growth_events, q.growth_rows_added, q.proven_maximum_additional_allocations)
+        live_rows = p.logical_to_physical[p.logical_to_physical >= 0].long()
+        assert torch.equal(p.values[live_rows], q.values[live_rows])
+        q.validate_invariants()
+    if quantum == 16:
+        assert b.sdm_states[0].growth_events > 0
+    assert a.batch == b.batch == live - 2 + cohort
+    assert torch.equal(a.current_positions(), b.current_positions()) and a.position == b.position
+
+
+def test_admit_prefix_refuses_bad_routes_without_changing_the_pools(dev):
+    from copy_on_write_sdm_b200.allocator import from_prefix_routes_layers  # noqa: F401
+
+    rng = np.random.default_rng(77)
+    heads, slots, width = 1, 64, 32
+    m0s = [(0.02 * rng.standard_normal((heads, slots, width))).astype(np.float32)]
+    states, _ = run(m0s, [prefix(rng, 4, 5, slots, width, 4, 16)], np.zeros(4, np.int64), dev, 64)
+    state = _decode_state(states, 4, 5)
+    before = (state.sdm_states[0].logical_to_physical.clone(), int(state.sdm_states[0].free_count))
+    for bad in ("read", "write"):
+        x = prefix(rng, 2, 3, slots, width, 4, 16)
+        if bad == "read":
+            x["read_indices"][1, 2, 5] = slots
+        else:
+            x["write_indices"][0, 1, 2] = x["write_indices"][0, 1, 0]
+        with pytest.raises(ValueError):
+            state.admit_prefix([{k: cu(x[k], dev) for k in KEYS}], template_indices=cu(np.zeros(2, np.int64), dev))
+        assert torch.equal(state.sdm_states[0].logical_to_physical, before[0])
+        assert int(state.sdm_states[0].free_count) == before[1] and state.batch == 4
