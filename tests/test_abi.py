@@ -74,6 +74,11 @@ def test_multi_pool_and_host_step_entry_points_reject_bad_arguments():
     assert lib.cow_prefill_workspace_bytes(pools, 2, 4, 4, 16) == 8 * 4 * 64 * 4
     assert lib.cow_prefill_workspace_bytes(pools, 2, 4, 0, 16) == -1
     assert lib.cow_prefill_recurrence_layers_ws(pools, None, 2, 4, 4, 16, 1, 0, ws, 16, None) == _lib.ERR_INVALID
+    # direct cohort admission: workspace per pool = scan flags + two row lists
+    assert lib.cow_admit_prefix_workspace_bytes(2, 8, 2) > 0
+    assert lib.cow_admit_prefix_workspace_bytes(-1, 8, 1) == -1
+    assert lib.cow_admit_prefix_workspace_bytes(2, 8, _lib.MAX_LAYERS + 1) == -1
+    assert lib.cow_admit_prefix_layers(pools, None, None, 2, 2, None, ws, 16, None) == _lib.ERR_INVALID
     # host-to-host steps: negative sizes, missing buffers or events
     assert lib.cow_decode_step_host(pools, None, 1, 4, 16, 1, 0, None, 0, None, None, -1, None, None, 0,
                                     None) == _lib.ERR_INVALID
