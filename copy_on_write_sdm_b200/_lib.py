@@ -166,8 +166,8 @@ _SIGNATURES = {
     "cow_append_count_layers": (c_int32, [POINTER(CowPool), POINTER(CowPool), c_int32, P, c_int64, P, P]),
     "cow_append_layers": (c_int32, [POINTER(CowPool), POINTER(CowPool), c_int32, P, P, c_int64, P]),
     "cow_pack_workspace_bytes": (c_int64, [c_int64, c_int32]),
-    "cow_prefill_mark_count_layers": (c_int32, [P, c_int32, c_int64, c_int64, c_int32, c_int64, P, c_int32, P,
-                                                c_int64, P, P]),
+    "cow_prefill_mark_count_layers": (c_int32, [P, P, c_int32, c_int64, c_int64, c_int32, c_int32, c_int64, P,
+                                                c_int32, P, c_int64, P, P]),
     "cow_pack_apply_layers": (c_int32, [POINTER(CowPool), c_int32, P, c_int64, P]),
     "cow_admit_prefix_workspace_bytes": (c_int64, [c_int64, c_int64, c_int32]),
     "cow_admit_prefix_layers": (c_int32, [POINTER(CowPool), P, P, c_int64, c_int32, P, P, c_int64, P]),

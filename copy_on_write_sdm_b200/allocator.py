@@ -1132,7 +1132,8 @@ def from_prefix_routes_layers(
     maps = [torch.empty(banks, slots, device=device, dtype=torch.int32) for _ in range(n)]
     ws = _workspace(device, lib.cow_pack_workspace_bytes(banks * slots, n))
     out = torch.empty(2 * n, device=device, dtype=torch.int32)
-    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), idx_code, banks, time, writes,
+    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), _ptrs([st.ridx for st in steps]),
+                                                 idx_code, banks, time, writes, reads,
                                                  slots, _ptrs(maps), n, ws.data_ptr(), ws.numel(), out.data_ptr(),
                                                  stream), "cow_prefill_mark_count_layers")
     host, lo, hi = _read_counts_and_range(out, templates)
@@ -1204,20 +1205,17 @@ def admit_prefix_routes_layers(states: Sequence[PackedSDMCopyOnWriteState], pref
     ws = _workspace(device, max(lib.cow_pack_workspace_bytes(banks * slots, n),
                                 lib.cow_admit_prefix_workspace_bytes(banks, slots, n)))
     out = torch.empty(2 * n, device=device, dtype=torch.int32)
-    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), idx_code, banks, time, writes,
+    _lib.check(lib.cow_prefill_mark_count_layers(_ptrs([st.widx for st in steps]), _ptrs([st.ridx for st in steps]),
+                                                 idx_code, banks, time, writes, reads,
                                                  slots, _ptrs(marks), n, ws.data_ptr(), ws.numel(), out.data_ptr(),
                                                  stream), "cow_prefill_mark_count_layers")
-    # One read for the mark status, live counts, free counts and the index
-    # ranges of the read routes (write routes are checked by the mark pass).
-    ranges = torch.stack([torch.stack(torch.aminmax(st.ridx)) for st in steps]).reshape(-1).to(torch.int64)
+    # One read for the mark status (write and read route checks), the live
+    # counts and the free counts.
     frees_dev = torch.stack([st.free_count.reshape(()) for st in states]).to(torch.int64)
-    host, lo, hi = _read_counts_and_range(torch.cat((out.to(torch.int64), frees_dev, ranges)), templates)
+    host, lo, hi = _read_counts_and_range(torch.cat((out.to(torch.int64), frees_dev)), templates)
     for l in range(n):
         if host[2 * l]:
             raise ValueError(_lib.status_text(host[2 * l]))
-    r = host[3 * n:]
-    if min(r[0::2]) < 0 or max(r[1::2]) >= slots:
-        raise ValueError(_lib.status_text(_lib.ST_INDEX_RANGE))
     _check_template_range(lo, hi, m0s[0])
     frees = []
     for l, st in enumerate(states):

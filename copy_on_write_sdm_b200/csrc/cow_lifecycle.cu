@@ -231,6 +231,7 @@ struct MarkCtx {
   const void* widx;
   int32_t* map;
   int32_t* status;
+  const void* ridx;  // read routes [banks,T,R] checked for range (may be null)
 };
 
 struct BankListCtx {
@@ -304,8 +305,14 @@ __global__ void mask_to_map_kernel(const uint8_t* active, int64_t n, int32_t* ma
 }
 
 __global__ void prefill_mark_kernel(const __grid_constant__ Layers<MarkCtx> L, int idx64, int64_t banks, int64_t time,
-                                    int writes, int64_t slots) {
+                                    int writes, int64_t slots, int reads) {
   const MarkCtx& c = L.c[blockIdx.y];
+  if (c.ridx != nullptr) {
+    COW_GRID_STRIDE(i, banks * time * reads) {
+      const int64_t r = ld_index(c.ridx, i, idx64);
+      if (r < 0 || r >= slots) atomicOr(c.status, COW_ST_INDEX_RANGE);
+    }
+  }
   COW_GRID_STRIDE(i, banks * time * writes) {
     const int64_t bank = i / (time * writes);
     const int64_t s = ld_index(c.widx, i, idx64);
@@ -638,10 +645,10 @@ int cow_prefill_mark(const void* write_indices, int32_t index_dtype, int64_t ban
   const int64_t n = banks * time * writes;
   if (n == 0) return COW_OK;
   Layers<MarkCtx> L{};
-  L.c[0] = MarkCtx{write_indices, map, status};
+  L.c[0] = MarkCtx{write_indices, map, status, nullptr};
   L.layers = 1;
   prefill_mark_kernel<<<layer_grid(n, 256, 1), 256, 0, as_stream(stream)>>>(L, index_dtype == COW_I64, banks, time,
-                                                                         writes, slots);
+                                                                         writes, slots, 0);
   return launch_status();
 }
 
@@ -1049,11 +1056,12 @@ int64_t cow_pack_workspace_bytes(int64_t n, int32_t layers) {
   return (scan_words(n) + words16(n > 0 ? n : 1)) * 4 * static_cast<int64_t>(layers);
 }
 
-int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t index_dtype, int64_t banks, int64_t time,
-                                  int32_t writes, int64_t slots, int32_t* const* maps, int32_t layers,
-                                  void* workspace, int64_t workspace_bytes, int32_t* out, void* stream) {
+int cow_prefill_mark_count_layers(const void* const* write_indices, const void* const* read_indices,
+                                  int32_t index_dtype, int64_t banks, int64_t time, int32_t writes, int32_t reads,
+                                  int64_t slots, int32_t* const* maps, int32_t layers, void* workspace,
+                                  int64_t workspace_bytes, int32_t* out, void* stream) {
   if (!write_indices || !maps || !out || layers < 1 || layers > COW_MAX_LAYERS || banks < 0 || time < 0 ||
-      writes < 1 || slots < 1)
+      writes < 1 || slots < 1 || reads < 0 || (reads > 0 && !read_indices))
     return COW_ERR_INVALID;
   const int64_t n = banks * slots;
   if (!workspace_ok(workspace, workspace_bytes, cow_pack_workspace_bytes(n, layers))) return COW_ERR_INVALID;
@@ -1066,7 +1074,8 @@ int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t inde
   for (int l = 0; l < layers; ++l) {
     if ((n > 0 && !maps[l]) || (banks * time > 0 && !write_indices[l])) return COW_ERR_INVALID;
     if (n > 0 && cudaMemsetAsync(maps[l], 0xff, sizeof(int32_t) * n, st) != cudaSuccess) return COW_ERR_CUDA;
-    M.c[l] = MarkCtx{write_indices[l], maps[l], out + 2 * l};
+    if (reads > 0 && banks * time > 0 && !read_indices[l]) return COW_ERR_INVALID;
+    M.c[l] = MarkCtx{write_indices[l], maps[l], out + 2 * l, reads > 0 ? read_indices[l] : nullptr};
     ScanCtx& c = C.c[l];
     c.op = kOpPack;
     c.n = n;
@@ -1075,9 +1084,10 @@ int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t inde
     c.scratch = static_cast<int32_t*>(workspace) + stride * l;
     c.total_out = out + 2 * l + 1;
   }
-  if (banks * time * writes > 0) {
-    prefill_mark_kernel<<<layer_grid(banks * time * writes, 256, layers), 256, 0, st>>>(M, index_dtype == COW_I64,
-                                                                                     banks, time, writes, slots);
+  const int64_t elems = banks * time * (writes > reads ? writes : reads);
+  if (elems > 0) {
+    prefill_mark_kernel<<<layer_grid(elems, 256, layers), 256, 0, st>>>(M, index_dtype == COW_I64, banks, time, writes,
+                                                                       slots, reads);
     if (launch_status() != COW_OK) return COW_ERR_CUDA;
   }
   return run_scan_count(C, st);

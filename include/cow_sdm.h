@@ -438,15 +438,18 @@ int cow_append_layers(const cow_pool* dsts, const cow_pool* others, int32_t laye
 
 /* Sparse prefill layout for each pool.  Phase 1 sets maps[l] [banks,slots] to
  * -1, marks the written slots of write_indices[l] [banks,T,W] and counts them:
- * out[2l] = status bits (COW_ST_INDEX_RANGE, COW_ST_DUPLICATE_WRITE for a
- * token that writes one slot twice), out[2l+1] = live rows.  Phase 2
+ * out[2l] = status bits (COW_ST_INDEX_RANGE for a write route, or a read
+ * route of read_indices[l] [banks,T,R] when reads > 0, outside the slots;
+ * COW_ST_DUPLICATE_WRITE for a token that writes one slot twice),
+ * out[2l+1] = live rows.  Phase 2
  * (same workspace; pools[l].map = maps[l], slab and stack sized by the host)
  * assigns rows 0..A-1 in nonzero() order, fills the free stack with
  * arange(A, capacity) and copies each live row from m0.  n = banks*slots. */
 int64_t cow_pack_workspace_bytes(int64_t n, int32_t layers);
-int cow_prefill_mark_count_layers(const void* const* write_indices, int32_t index_dtype, int64_t banks, int64_t time,
-                                  int32_t writes, int64_t slots, int32_t* const* maps, int32_t layers,
-                                  void* workspace, int64_t workspace_bytes, int32_t* out, void* stream);
+int cow_prefill_mark_count_layers(const void* const* write_indices, const void* const* read_indices,
+                                  int32_t index_dtype, int64_t banks, int64_t time, int32_t writes, int32_t reads,
+                                  int64_t slots, int32_t* const* maps, int32_t layers, void* workspace,
+                                  int64_t workspace_bytes, int32_t* out, void* stream);
 int cow_pack_apply_layers(const cow_pool* pools, int32_t layers, void* workspace, int64_t workspace_bytes,
                           void* stream);
 
